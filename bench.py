@@ -1,0 +1,346 @@
+#!/usr/bin/env python
+"""Kev scoring throughput on B200: scored requests/s, prompt tokens/s, p50 latency.
+
+Workload (default, config 2 of the benchmark definition): the Qwen3.5-0.8B-shaped
+Kev scorer in bf16 (random-init weights from a fixed seed), 32 requests with
+lengths uniform in [64, 512]; each asks a 4-option choice, a noul and a 5-level
+score, so one step scores 96 independent rows (~27.6k prompt tokens) split into
+two native batches of 48 rows. Under torchrun every rank (one per GPU) scores
+its own 32 requests (weak scaling; replicas, no collective on the data path).
+
+  value  device time of K steps with inputs resident in HBM (hk_score_device),
+         L2 flushed between steps (256 MiB write, outside the timed events);
+  e2e    the same K steps through the public host API (KevBackend.score_packed
+         -> hk_score: host->device copy of the inputs, device->host read of the
+         logits), plus host calibration and answers, wall clock;
+both are the max over ranks. `--impl reference` times the CPU reference path
+(the oracle restatement of the reference's CPU fp32 forward) on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from huncho_b200 import calibration, engine, synth  # noqa: E402
+from huncho_b200.backend import pack_rows  # noqa: E402
+
+CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi samples of one GPU while the timed region runs."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={CLOCK_QUERY}", "--format=csv,noheader",
+                                          "-i", str(self.index), "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1].split()[0]))
+                mx = float(f[2].split()[0])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def groups_of(rows, limit=64):
+    """Split rows into the fewest native batches of at most `limit` rows, equal-sized."""
+    n = len(rows)
+    k = -(-n // limit)
+    size = -(-n // k)
+    return [list(range(i, min(n, i + size))) for i in range(0, n, size)]
+
+
+def model_dir_for(name, store, seed):
+    return synth.default_dir(name, seed, store)
+
+
+def cpu_baseline(model_dir, dtype, wl, rows_idx, max_seconds=30.0):
+    """The CPU oracle on a bounded sample of the workload (whole rows)."""
+    from oracle import kev_oracle as ko
+    ko.set_threads(os.cpu_count() or 1)
+    m = ko.load_model(model_dir, dtype)
+    t0 = time.perf_counter()
+    done, toks = 0, 0
+    for i in rows_idx:
+        ko.score_row(m, wl.rows[i], wl.positions[i])
+        done += 1
+        toks += len(wl.rows[i])
+        if time.perf_counter() - t0 > max_seconds:
+            break
+    dt = time.perf_counter() - t0
+    rows_per_req = len(wl.rows) / wl.n_requests
+    return {"value": (done / rows_per_req) / dt, "unit": "requests/s", "cores": os.cpu_count(), "kind": "port",
+            "tokens_per_s": toks / dt,
+            "sample": f"{done} question rows ({toks} tokens) of the workload, CPU fp32 oracle on the same weights, "
+                      f"{dt:.1f} s"}
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    from oracle import kev_oracle as ko
+    name, store, dtype = "kev-0.8b", "bf16", "bf16"
+    d = synth.write_model(model_dir_for(name, store, args.seed), name, args.seed, store)
+    ko.set_threads(os.cpu_count() or 1)
+    m = ko.load_model(d, dtype)
+    wl = synth.make_workload(args.config, m.cfg.vocab_size, seed=args.seed)
+    rows_per_req = len(wl.rows) / wl.n_requests
+    times, toks = [], 0
+    for s in range(args.warmup + args.steps):
+        i = s % len(wl.rows)
+        t0 = time.perf_counter()
+        ko.calibrate(ko.score_row(m, wl.rows[i], wl.positions[i]), m.temperature)
+        if s >= args.warmup:
+            times.append(time.perf_counter() - t0)
+            toks += len(wl.rows[i])
+    total = sum(times)
+    value = (len(times) / rows_per_req) / total
+    line = {
+        "impl": "reference", "metric": "scored requests/s", "value": value, "unit": "requests/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "prompt_tokens_per_s": toks / total,
+        "config": {"workload": f"cfg{args.config}: Kev-0.8B, 32 requests x (choice-4, noul, score-5), "
+                                "lengths U[64,512]", "model": "kev-0.8b (bf16 weights, fp32 math)",
+                   "step": "one question row (1/3 request) per step"},
+        "cpu_baseline": {"value": value, "unit": "requests/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{len(times)} question rows, {toks} tokens; the CPU oracle restating the "
+                                   "reference CPU fp32 Kev forward (the Rust reference cannot be built here)"},
+        "e2e": {"value": value, "unit": "requests/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from huncho_b200.backend import KevBackend
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    name, store = ("kev-0.8b", "bf16")
+    dtype = {1: "fp32", 2: "bf16", 3: "int8w", 4: "bf16"}.get(args.config, "bf16")
+    if args.config == 1:
+        store = "fp32"
+    if args.config == 5:
+        name = "kev-4b"
+    d = model_dir_for(name, store, args.seed)
+    if rank == 0:
+        synth.write_model(d, name, args.seed, store)
+    barrier()
+    wl = synth.make_workload(args.config, synth.SPECS[name]["vocab_size"], seed=args.seed + rank)
+    max_len = max(len(r) for r in wl.rows)
+    backend = KevBackend(d, device=local, dtype=dtype, max_context=max(8192, max_len))
+
+    groups = groups_of(wl.rows, backend.batch_limits().max_rows)
+    packed = []
+    for g in groups:
+        tok, cu, pos, cup = pack_rows([wl.rows[i] for i in g], [wl.positions[i] for i in g])
+        dev = {"tok": torch.from_numpy(tok.view(np.int32)).cuda(), "cu": torch.from_numpy(cu).cuda(),
+               "pos": torch.from_numpy(pos).cuda(), "out": torch.empty(int(cup[-1]), device="cuda")}
+        packed.append((g, tok, cu, pos, cup, dev))
+    n_tok = wl.n_tokens
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def device_step():
+        for g, tok, cu, pos, cup, dev in packed:
+            backend.score_device(cu, cup, dev["tok"].data_ptr(), dev["cu"].data_ptr(), dev["pos"].data_ptr(),
+                                 dev["out"].data_ptr(), stream.cuda_stream)
+
+    # warm-up (also sizes the workspace)
+    for _ in range(args.warmup):
+        flush.zero_()
+        device_step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: device-resident inputs
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches0 = backend.kernel_launches
+    backend.profile(True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for k in range(args.steps):
+            flush.zero_()
+            starts[k].record(stream)
+            device_step()
+            ends[k].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    backend.profile(False)
+    prof = backend.profile_read()
+    launches = backend.kernel_launches - launches0
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    dev_total_s = max_over_ranks(sum(step_ms) / 1000.0)
+
+    # ---- e2e: the public host API, host calibration and answers included
+    h2d = sum(tok.nbytes + cu.nbytes + pos.nbytes + cup.nbytes for _, tok, cu, pos, cup, _ in packed)
+    d2h = sum(4 * int(cup[-1]) + 4 for _, _, _, _, cup, _ in packed)
+
+    def e2e_step():
+        for g, tok, cu, pos, cup, _ in packed:
+            logits = backend.score_packed(tok, cu, pos, cup)
+            for j, i in enumerate(g):
+                lo, hi = int(cup[j]), int(cup[j + 1])
+                probs = calibration.calibrate(logits[lo:hi], backend.temperature)
+                q = engine.Question(wl.qtypes[i], labels=[str(x) for x in range(hi - lo)],
+                                    descriptions=["" for _ in range(hi - lo)])
+                engine.build_answer(q, engine.candidates_for(q, wl.positions[i]), probs)
+
+    e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_times = []
+    for _ in range(args.steps):
+        ts = time.perf_counter()
+        e2e_step()
+        e2e_times.append(time.perf_counter() - ts)
+    e2e_total_s = max_over_ranks(time.perf_counter() - t0)
+
+    # single-request latency through the public API (one request's rows as one batch)
+    first = [i for i, r in enumerate(wl.request_of) if r == 0]
+    one = pack_rows([wl.rows[i] for i in first], [wl.positions[i] for i in first])
+    lat = []
+    for _ in range(max(5, args.warmup)):
+        ts = time.perf_counter()
+        backend.score_packed(*one)
+        lat.append(time.perf_counter() - ts)
+
+    reqs = wl.n_requests * world
+    toks_all = n_tok * world
+    value = reqs * args.steps / dev_total_s
+    pk = peaks()
+    gemm_ms, gemm_flops, gemm_n = prof["gemm"]
+    achieved = (gemm_flops / 1e12) / (gemm_ms / 1e3) if gemm_ms > 0 else None
+    traffic = None
+    tf = ROOT / "profiles" / "gemm_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+    total_prof_ms = sum(v[0] for v in prof.values())
+    line = {
+        "metric": "scored requests/s", "value": value, "unit": "requests/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dev_total_s / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if dtype != "fp32" else "f32",
+        "data": "synthetic",
+        "prompt_tokens_per_s": toks_all * args.steps / dev_total_s,
+        "p50_request_latency_ms": statistics.median(step_ms),
+        "p50_single_request_latency_ms": 1000.0 * statistics.median(lat),
+        "config": {"workload": f"cfg{args.config}: Kev-{name[4:]} {dtype}, {wl.n_requests} requests per GPU x "
+                               f"{len(wl.rows) // wl.n_requests} questions (choice-4, noul, score-5), lengths "
+                               "U[64,512], packed varlen", "model": name, "rows_per_step": len(wl.rows) * world,
+                   "tokens_per_step": toks_all, "native_batches_per_step": len(groups),
+                   "l2": "flushed between steps (256 MiB write, outside the timed events); weights 1 GB > L2",
+                   "parallelism": f"replicas x{world}"},
+        "e2e": {"value": reqs * args.steps / e2e_total_s, "unit": "requests/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "includes": "hk_score (H2D inputs, forward, D2H logits) + host "
+                                                      "calibration and answers"},
+        "gpu_launches": int(launches),
+        "roofline": {"kernel": "gemm_bf16_tc (tcgen05 projections)", "bound": "tensor", "achieved": achieved,
+                     "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": (achieved / pk["bf16_tflops_sustained"]) if achieved else None,
+                     "traffic": traffic, "peak_source": pk["source"] + " (sustained: kernels timed inside a step)",
+                     "launches": int(gemm_n)},
+        "time_shares": {k: round(v[0] / total_prof_ms, 4) for k, v in prof.items()} if total_prof_ms else {},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        order = [i for r in range(wl.n_requests) for i in range(len(wl.rows)) if wl.request_of[i] == r]
+        line["cpu_baseline"] = cpu_baseline(d, dtype, wl, order)
+    line["clocks"] = clk.summary()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    backend.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,261 @@
+"""KevBackend: huncho-core's `Backend` trait for the Kev scorer, over the C ABI.
+
+Mirrors the trait (crates/huncho-core/src/backend.rs:211-438) as implemented
+for Kev by `Qwen3_5Backend` (crates/huncho-backend/src/qwen3_5.rs:2515-3266):
+same method names, argument meaning, outputs and error kinds. Every forward
+runs on the GPU through libhuncho_kev.so; there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _native
+from .errors import BackendError, PackageError, UnsupportedError
+
+_ERR = {
+    _native.HK_ERR_BACKEND: BackendError,
+    _native.HK_ERR_UNSUPPORTED: UnsupportedError,
+    _native.HK_ERR_PACKAGE: PackageError,
+    _native.HK_ERR_CUDA: BackendError,
+    _native.HK_ERR_ARGUMENT: BackendError,
+}
+
+
+@dataclass
+class ForwardInput:
+    """backend.rs:52-75. Positions are relative to `tokens`, sorted ascending."""
+    tokens: Sequence[int]
+    positions: Sequence[int]
+    logit_codes: Optional[Sequence[int]] = None
+    qtype: int = 0
+    retain_cache: bool = False
+    fork_from: Optional[int] = None
+
+
+@dataclass
+class ForwardOutput:
+    """ForwardOutput::Logits: one row per readout position, one pointer logit each."""
+    positions: list
+    values: np.ndarray  # [n_positions, 1] float32
+
+
+@dataclass
+class BatchLimits:
+    """backend.rs:108-121."""
+    max_rows: int = _native.HK_MAX_ROWS
+    max_readouts: Optional[int] = None
+
+
+@dataclass
+class Capabilities:
+    id: str
+    dtype: str
+    max_context: int
+    supports_fork: bool
+    supports_lora: bool
+    families: list
+    extra: dict = field(default_factory=dict)
+
+
+class KevBackend:
+    """One Kev scorer on one GPU (a handle of the C ABI)."""
+
+    def __init__(self, model_dir, device: int = 0, dtype: str = "bf16", max_context: int = 8192,
+                 _handle=None):
+        self._lib = _native.load()
+        if dtype not in _native.HK_DTYPE:
+            raise UnsupportedError(f"Kev's B200 backend supports fp32, bf16 or int8w, not `{dtype}`")
+        self.model_dir = str(model_dir)
+        self.dtype = dtype
+        self.device = device
+        self._h = ctypes.c_void_p()
+        if _handle is not None:
+            self._h = _handle
+        else:
+            rc = self._lib.hk_create(self.model_dir.encode(), device, _native.HK_DTYPE[dtype],
+                                     int(max_context), ctypes.byref(self._h))
+            if rc != _native.HK_OK:
+                raise _ERR.get(rc, BackendError)(self._lib.hk_create_error().decode())
+        caps = _native.HkCapabilities()
+        self._check(self._lib.hk_capabilities_get(self._h, ctypes.byref(caps)))
+        self.max_context = caps.max_context
+        self.vocab_size = caps.vocab_size
+        self.hidden_size = caps.hidden_size
+        self.num_layers = caps.num_layers
+        self.pointer_dim = caps.pointer_dim
+        self.temperature = float(caps.temperature)
+        self.lora_rank = caps.lora_rank
+
+    # ---------------------------------------------------------------- plumbing
+    def _check(self, rc: int) -> None:
+        if rc != _native.HK_OK:
+            raise _ERR.get(rc, BackendError)(self._lib.hk_last_error(self._h).decode())
+
+    def close(self) -> None:
+        if self._h:
+            self._lib.hk_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def kernel_launches(self) -> int:
+        return int(self._lib.hk_kernel_launches(self._h))
+
+    # ---------------------------------------------------------------- trait
+    def id(self) -> str:
+        return "b200-kev"
+
+    def capabilities(self) -> Capabilities:
+        """qwen3_5.rs:2541-2653 (families [F2], dtype, max_context, device)."""
+        return Capabilities(
+            id=self.id(), dtype=self.dtype, max_context=self.max_context, supports_fork=False,
+            supports_lora=True, families=["F2"],
+            extra={"device": f"cuda:{self.device}", "native_execution": "b200-kev-sm100a-v1",
+                   "pointer_head_dtype": "fp32", "recurrent_state_dtype": "fp32",
+                   **({"weight_quantization": "int8-per-channel-symmetric"} if self.dtype == "int8w" else {})},
+        )
+
+    def replica(self, device: Optional[int] = None) -> "KevBackend":
+        """The same immutable weights (on `device`, default the same GPU), fresh state."""
+        h = ctypes.c_void_p()
+        dev = self.device if device is None else device
+        rc = self._lib.hk_replica(self._h, dev, ctypes.byref(h))
+        if rc != _native.HK_OK:
+            raise _ERR.get(rc, BackendError)(self._lib.hk_create_error().decode())
+        r = KevBackend.__new__(KevBackend)
+        KevBackend.__init__(r, self.model_dir, dev, self.dtype, self.max_context, _handle=h)
+        return r
+
+    def supports_batch(self) -> bool:
+        return True
+
+    def supports_padded_batch(self) -> bool:
+        return True
+
+    def supports_fork(self) -> bool:
+        return False
+
+    def batch_limits(self) -> BatchLimits:
+        return BatchLimits()
+
+    def forward(self, inp: ForwardInput) -> ForwardOutput:
+        """Backend::forward for one row (qwen3_5.rs:2655-2753)."""
+        if inp.retain_cache:
+            raise UnsupportedError("use prefill to obtain an explicit cache handle")
+        tokens = list(inp.tokens)
+        if any(int(t) < 0 or int(t) >= self.vocab_size for t in tokens):
+            raise BackendError("Qwen3.5 token ID is outside the vocabulary")
+        if inp.fork_from is not None:
+            raise BackendError("unknown Qwen3.5 cache handle")
+        positions = [int(p) for p in inp.positions]
+        if any(p < 0 or p >= len(tokens) for p in positions):
+            raise BackendError("Qwen3.5 readout position is outside the token sequence")
+        if len(tokens) > self.max_context:
+            raise BackendError(f"sequence length {len(tokens)} exceeds max_context {self.max_context}")
+        if not positions:
+            return ForwardOutput(positions=[], values=np.zeros((0, 1), np.float32))
+        if not tokens:
+            raise BackendError("cached continuation requires nonempty suffix tokens")
+        return self._run([tokens], [positions])[0]
+
+    def forward_batch(self, inputs: Sequence[ForwardInput]) -> list:
+        """Equal-length independent rows (qwen3_5.rs:2759-2761 -> 3138-3194)."""
+        return self._independent(inputs, padded=False)
+
+    def forward_padded_batch(self, inputs: Sequence[ForwardInput]) -> list:
+        """Mixed-length rows; padding is invisible (qwen3_5.rs:2806-2816 -> 3138-3194)."""
+        return self._independent(inputs, padded=True)
+
+    def prefill(self, tokens):
+        raise UnsupportedError("prefix caches are not supported by the B200 Kev backend")
+
+    def fork(self, handle):
+        raise UnsupportedError("prefix forks are not supported by the B200 Kev backend")
+
+    def _independent(self, inputs, padded: bool) -> list:
+        inputs = list(inputs)
+        if not inputs or len(inputs) > _native.HK_MAX_ROWS:
+            raise BackendError("Qwen3.5 batch must contain 1..=64 independent rows")
+        seq = max(len(i.tokens) for i in inputs)
+        bad = seq == 0 or seq > self.max_context
+        for i in inputs:
+            if (len(i.tokens) == 0 or (not padded and len(i.tokens) != seq) or i.fork_from is not None
+                    or i.retain_cache or any(int(p) < 0 or int(p) >= len(i.tokens) for p in i.positions)
+                    or any(int(t) < 0 or int(t) >= self.vocab_size for t in i.tokens)):
+                bad = True
+        if bad:
+            raise BackendError("Qwen3.5 batches require valid independent rows without cache handles; "
+                               "ordinary batches require equal lengths")
+        return self._run([list(i.tokens) for i in inputs], [[int(p) for p in i.positions] for i in inputs])
+
+    def _run(self, rows, positions) -> list:
+        logits = self.score_packed(*pack_rows(rows, positions))
+        out, k = [], 0
+        for pos in positions:
+            out.append(ForwardOutput(positions=list(pos),
+                                     values=logits[k:k + len(pos)].reshape(-1, 1).copy()))
+            k += len(pos)
+        return out
+
+    # ---------------------------------------------------------------- packed API
+    def score_packed(self, tokens, cu_seqlens, positions, cu_positions) -> np.ndarray:
+        """hk_score: raw pointer logits of every readout position, in input order."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint32)
+        cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        cup = np.ascontiguousarray(cu_positions, dtype=np.int32)
+        out = np.empty(max(int(cup[-1]), 1), np.float32)
+        self._check(self._lib.hk_score(
+            self._h, len(cu) - 1, tokens.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)),
+            cu.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), pos.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+            cup.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+        return out[:int(cup[-1])]
+
+    def score_device(self, cu_seqlens_host, cu_positions_host, d_tokens: int, d_cu_seqlens: int,
+                     d_positions: int, d_out: int, stream: int = 0) -> None:
+        """hk_score_device: inputs/outputs are device pointers; asynchronous on `stream`."""
+        cu = np.ascontiguousarray(cu_seqlens_host, dtype=np.int32)
+        cup = np.ascontiguousarray(cu_positions_host, dtype=np.int32)
+        self._check(self._lib.hk_score_device(
+            self._h, len(cu) - 1, cu.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+            cup.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ctypes.c_void_p(d_tokens),
+            ctypes.c_void_p(d_cu_seqlens), ctypes.c_void_p(d_positions), ctypes.c_void_p(d_out),
+            ctypes.c_void_p(stream)))
+
+    PROFILE_CLASSES = ("gemm", "delta_recurrence", "attention", "delta_prep", "other")
+
+    def profile(self, enable: bool) -> None:
+        """Bracket every launch with CUDA events (see hk_profile_enable)."""
+        self._check(self._lib.hk_profile_enable(self._h, 1 if enable else 0))
+
+    def profile_read(self) -> dict:
+        """{class: (milliseconds, algorithmic work, launches)} since the last read."""
+        n = len(self.PROFILE_CLASSES)
+        ms, work, cnt = (ctypes.c_double * n)(), (ctypes.c_double * n)(), (ctypes.c_int64 * n)()
+        self._check(self._lib.hk_profile_read(self._h, ms, work, cnt, n))
+        return {c: (ms[i], work[i], cnt[i]) for i, c in enumerate(self.PROFILE_CLASSES)}
+
+    def synchronize(self) -> None:
+        self._check(self._lib.hk_synchronize(self._h))
+
+
+def pack_rows(rows, positions):
+    """Pack independent rows into (tokens, cu_seqlens, positions, cu_positions)."""
+    cu = np.zeros(len(rows) + 1, np.int32)
+    cup = np.zeros(len(rows) + 1, np.int32)
+    for i, (r, p) in enumerate(zip(rows, positions)):
+        cu[i + 1] = cu[i] + len(r)
+        cup[i + 1] = cup[i] + len(p)
+    tokens = np.concatenate([np.asarray(r, np.uint32) for r in rows]) if rows else np.zeros(0, np.uint32)
+    pos = (np.concatenate([np.asarray(p, np.int32) for p in positions])
+           if any(len(p) for p in positions) else np.zeros(0, np.int32))
+    return tokens, cu, pos, cup

@@ -1,0 +1,82 @@
+// Shared helpers for the Kev sm_100a kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+namespace hk {
+
+// A CUDA failure on the host side becomes a C++ exception that the C ABI turns
+// into HK_ERR_CUDA with the message.
+struct CudaError : std::runtime_error {
+    explicit CudaError(const std::string &s) : std::runtime_error(s) {}
+};
+
+#define HK_CUDA(expr)                                                                  \
+    do {                                                                               \
+        cudaError_t _e = (expr);                                                       \
+        if (_e != cudaSuccess)                                                         \
+            throw ::hk::CudaError(std::string(#expr) + ": " + cudaGetErrorString(_e)); \
+    } while (0)
+
+// Kernels launched by the calling thread (launch accounting for the C ABI).
+extern thread_local uint64_t tl_launches;
+
+#define HK_LAUNCH_CHECK()              \
+    do {                               \
+        ++::hk::tl_launches;           \
+        HK_CUDA(cudaGetLastError());   \
+    } while (0)
+
+// Device-side error word bits. Kernels never trap: a bounded wait that gives
+// up, or an index that fails a guard, sets a bit and the kernel returns.
+enum : uint32_t {
+    kErrWaitTimeout = 1u << 0,   // an mbarrier wait exceeded its iteration limit
+    kErrBadIndex = 1u << 1,      // an index guard failed
+};
+
+__device__ __forceinline__ void set_error(uint32_t *err, uint32_t bit) {
+    if (err) atomicOr(err, bit);
+}
+
+// Activation element types: float (fp32 model) or __nv_bfloat16 (bf16/int8w models).
+template <typename T> struct Act;
+template <> struct Act<float> {
+    static __device__ __forceinline__ float load(const float *p) { return *p; }
+    static __device__ __forceinline__ float to_f(float v) { return v; }
+    static __device__ __forceinline__ float from_f(float v) { return v; }
+    // Round a float to the storage type and back (the reference's casts to the
+    // model dtype between ops).
+    static __device__ __forceinline__ float round(float v) { return v; }
+};
+template <> struct Act<__nv_bfloat16> {
+    static __device__ __forceinline__ float load(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+    static __device__ __forceinline__ float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// SiLU and sigmoid as the reference writes them: x / (1 + exp(-x)), 1 / (1 + exp(-x)).
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }
+
+}  // namespace hk

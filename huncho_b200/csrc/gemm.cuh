@@ -1,0 +1,40 @@
+// Projection GEMMs: Y = X W^T with the layer's epilogue fused.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hk {
+
+enum GemmEpilogue : int {
+    kEpiStore = 0,   // out (activation type) [M, ldo] = acc * scale
+    kEpiResidual = 1,  // out fp32 [M, ldo] += acc * scale  (residual stream, in place)
+    kEpiSwiGLU = 2,  // weight rows interleaved in blocks of kSwiGLUBlock (gate, up);
+                     // out [M, ldo] = silu(gate) * up, N/2 columns
+    kEpiStoreF32 = 3,  // out fp32 [M, ldo] = acc * scale
+};
+
+// Rows of gate and up weights alternate in blocks of this size when the MLP
+// uses the fused SwiGLU epilogue (half of the tensor-core tile's N).
+constexpr int kSwiGLUBlock = 128;
+
+struct GemmArgs {
+    int M = 0, N = 0, K = 0;  // Y[M, N] = X[M, K] * W[N, K]^T
+    const void *x = nullptr;  // activations, row-major, leading dim ldx (elements)
+    int ldx = 0;
+    const void *w = nullptr;  // weights [N, K] row-major, leading dim ldw
+    int ldw = 0;
+    const float *scale = nullptr;  // per weight row (int8 weights), or null
+    void *out = nullptr;
+    int ldo = 0;
+    int epilogue = kEpiStore;
+    uint32_t *err = nullptr;
+};
+
+// bf16 X and W on tcgen05 tensor cores (TMA-fed, TMEM accumulators).
+void gemm_bf16_tc(const GemmArgs &a, cudaStream_t s, int num_sms);
+// fp32 X and W on CUDA cores (the fp32 model path).
+void gemm_f32_simt(const GemmArgs &a, cudaStream_t s);
+
+}  // namespace hk

@@ -1,0 +1,1085 @@
+// Kev scorer runtime: model-directory loading, device weight layout, the
+// packed-batch forward and the C ABI declared in include/huncho_kev.h.
+//
+// The forward restates Model::forward_inner (crates/huncho-backend/src/
+// qwen3_5.rs:1533-1553) for a packed batch of independent rows:
+//   embed -> 24 x [RMSNorm -> mixer (Gated DeltaNet or gated GQA) -> +residual
+//                  -> RMSNorm -> SwiGLU MLP -> +residual] -> pointer readout.
+// Rows are packed without padding (cu_seqlens), which is what the reference's
+// right padding amounts to for causal rows (qwen3_5.rs:3172-3177). The final
+// RMSNorm is applied only at the readout rows (decision + option tokens),
+// the only rows Qwen3_5Backend::readout reads (qwen3_5.rs:3196-3255).
+#include <dirent.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <sstream>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/huncho_kev.h"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "json.hpp"
+#include "layers.cuh"
+#include "safetensors.hpp"
+
+namespace hk {
+
+thread_local uint64_t tl_launches = 0;
+
+namespace {
+
+struct ApiError : std::runtime_error {
+    int code;
+    ApiError(int c, const std::string &m) : std::runtime_error(m), code(c) {}
+};
+
+std::string read_file(const std::string &p) {
+    std::ifstream f(p, std::ios::binary);
+    if (!f) throw ApiError(HK_ERR_PACKAGE, "cannot read " + p);
+    std::stringstream ss;
+    ss << f.rdbuf();
+    return ss.str();
+}
+
+// ----------------------------------------------------------------- config
+// Config::from_value (qwen3_5.rs:77-164), defaults included.
+struct KevConfig {
+    int hidden = 4096, layers = 32, nh = 16, nkv = 4, hd = 0, ffn = 12288, vocab = 248320;
+    float eps = 1e-6f;
+    std::vector<int> full;  // 1 = full attention layer
+    int taps = 4, dk = 128, nk = 16, nv = 32, dv = 128;
+    double theta = 10000.0, prf = 1.0;
+
+    int rotary_dim() const {
+        int d = static_cast<int>(std::llround(hd * prf));
+        return std::max(d, 2) & ~1;
+    }
+    int key_dim() const { return nk * dk; }
+    int value_dim() const { return nv * dv; }
+    int conv_dim() const { return 2 * key_dim() + value_dim(); }
+
+    static KevConfig from_json(const json::Value &root) {
+        const json::Value *tc = root.get("text_config");
+        const json::Value &t = tc ? *tc : root;
+        auto num = [&](const char *k, double d) {
+            const json::Value *v = t.get(k);
+            return (v && v->is_num()) ? v->num : d;
+        };
+        KevConfig c;
+        c.hidden = static_cast<int>(num("hidden_size", 4096));
+        c.layers = static_cast<int>(num("num_hidden_layers", 32));
+        c.nh = static_cast<int>(num("num_attention_heads", 16));
+        c.nkv = static_cast<int>(num("num_key_value_heads", 4));
+        c.hd = static_cast<int>(num("head_dim", c.hidden / std::max(c.nh, 1)));
+        c.ffn = static_cast<int>(num("intermediate_size", 12288));
+        c.vocab = static_cast<int>(num("vocab_size", 248320));
+        c.eps = static_cast<float>(num("rms_norm_eps", 1e-6));
+        const json::Value *lt = t.get("layer_types");
+        if (lt && lt->kind == json::Value::Array) {
+            for (auto &s : lt->arr) {
+                if (s.str.find("full_attention") != std::string::npos)
+                    c.full.push_back(1);
+                else if (s.str.find("linear_attention") != std::string::npos)
+                    c.full.push_back(0);
+                else
+                    throw ApiError(HK_ERR_PACKAGE, "unknown layer type `" + s.str + "`");
+            }
+        } else {
+            int interval = std::max(1, static_cast<int>(num("full_attention_interval", 4)));
+            for (int i = 0; i < c.layers; ++i) c.full.push_back((i + 1) % interval == 0);
+        }
+        c.taps = static_cast<int>(num("linear_conv_kernel_dim", 4));
+        c.dk = static_cast<int>(num("linear_key_head_dim", 128));
+        c.nk = static_cast<int>(num("linear_num_key_heads", 16));
+        c.nv = static_cast<int>(num("linear_num_value_heads", 32));
+        c.dv = static_cast<int>(num("linear_value_head_dim", 128));
+        const json::Value *rp = t.get("rope_parameters");
+        const json::Value *th = rp ? rp->get("rope_theta") : nullptr;
+        if (!th || !th->is_num()) th = t.get("rope_theta");
+        c.theta = (th && th->is_num()) ? th->num : 10000.0;
+        const json::Value *pr = rp ? rp->get("partial_rotary_factor") : nullptr;
+        if (!pr || !pr->is_num()) pr = t.get("partial_rotary_factor");
+        c.prf = (pr && pr->is_num()) ? pr->num : 1.0;
+        if (static_cast<int>(c.full.size()) < c.layers) c.full.resize(c.layers, 0);
+        return c;
+    }
+};
+
+// qwen3_5.rs:2496-2512.
+bool canonical_weight_name(const std::string &name, std::string &out) {
+    auto starts = [](const std::string &s, const char *p) { return s.rfind(p, 0) == 0; };
+    if (starts(name, "model.language_model.") || starts(name, "lm_head.")) {
+        out = name;
+        return true;
+    }
+    std::string text = name;
+    if (starts(name, "language_model."))
+        text = name.substr(15);
+    else if (starts(name, "model."))
+        text = name.substr(6);
+    if (starts(text, "layers.") || starts(text, "embed_tokens.") || starts(text, "norm.")) {
+        out = "model.language_model." + text;
+        return true;
+    }
+    return false;
+}
+
+uint16_t f32_to_bf16_bits(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) return 0x7FC0;
+    const uint32_t lsb = (u >> 16) & 1u;
+    u += 0x7FFFu + lsb;
+    return static_cast<uint16_t>(u >> 16);
+}
+float bf16_round(float f) {
+    uint32_t u = static_cast<uint32_t>(f32_to_bf16_bits(f)) << 16;
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+}
+
+// All base tensors of a model dir plus the adapter (merged on access).
+class WeightSource {
+  public:
+    WeightSource(const std::string &dir) : dir_(dir) {
+        DIR *d = opendir(dir.c_str());
+        if (!d) throw ApiError(HK_ERR_PACKAGE, "cannot open model directory " + dir);
+        std::vector<std::string> files;
+        while (dirent *e = readdir(d)) {
+            std::string n = e->d_name;
+            if (n.size() > 12 && n.compare(n.size() - 12, 12, ".safetensors") == 0 &&
+                n != "adapter_model.safetensors" && n != "pointer_head.safetensors" &&
+                n != "joint_head.safetensors")
+                files.push_back(n);
+        }
+        closedir(d);
+        std::sort(files.begin(), files.end());
+        if (files.empty())
+            throw ApiError(HK_ERR_BACKEND, "no base-weight `*.safetensors` found in `" + dir + "`");
+        for (auto &f : files) {
+            shards_.emplace_back(new SafeTensors(dir + "/" + f));
+            for (auto &kv : shards_.back()->tensors()) {
+                std::string k;
+                if (!canonical_weight_name(kv.first, k) || k.rfind("lm_head.", 0) == 0) continue;
+                if (base_.count(k)) throw ApiError(HK_ERR_PACKAGE, "duplicate canonical base tensor `" + k + "`");
+                base_[k] = &kv.second;
+            }
+        }
+        std::ifstream probe(dir + "/adapter_model.safetensors");
+        if (probe.good()) {
+            adapter_.reset(new SafeTensors(dir + "/adapter_model.safetensors"));
+            json::Value ac = json::parse(read_file(dir + "/adapter_config.json"));
+            const json::Value *r = ac.get("r");
+            const json::Value *al = ac.get("lora_alpha");
+            rank_ = r && r->is_num() ? static_cast<int>(r->num) : 0;
+            const float alpha = al && al->is_num() ? static_cast<float>(al->num) : static_cast<float>(rank_);
+            lora_scale_ = rank_ > 0 ? alpha / static_cast<float>(rank_) : 1.0f;
+            const std::string pre = "base_model.model.", suf = ".lora_A.weight";
+            for (auto &kv : adapter_->tensors()) {
+                const std::string &n = kv.first;
+                if (n.rfind(pre, 0) != 0 || n.size() < pre.size() + suf.size() ||
+                    n.compare(n.size() - suf.size(), suf.size(), suf) != 0)
+                    continue;
+                const std::string target = n.substr(pre.size(), n.size() - pre.size() - suf.size());
+                auto bit = adapter_->tensors().find(pre + target + ".lora_B.weight");
+                if (bit == adapter_->tensors().end())
+                    throw ApiError(HK_ERR_BACKEND, "missing LoRA weight `" + pre + target + ".lora_B.weight`");
+                std::string base;
+                if (!canonical_weight_name(target + ".weight", base))
+                    throw ApiError(HK_ERR_BACKEND, "unsupported LoRA target `" + target + "`");
+                if (!base_.count(base))
+                    throw ApiError(HK_ERR_BACKEND, "missing base weight `" + base + "` required for LoRA merge");
+                lora_[base] = {&kv.second, &bit->second};
+            }
+        }
+    }
+
+    int lora_rank() const { return adapter_ ? rank_ : 0; }
+
+    // fp32 copy of a base tensor with its LoRA delta merged in fp32:
+    // W += (alpha / r) * (B @ A), the rank sum in ascending order
+    // (qwen3_5.rs:1597-1640).
+    std::vector<float> get(const std::string &k, const std::vector<int64_t> &shape) const {
+        auto it = base_.find(k);
+        if (it == base_.end()) throw ApiError(HK_ERR_PACKAGE, "missing tensor `" + k + "`");
+        const TensorView &t = *it->second;
+        int64_t want = 1;
+        for (auto d : shape) want *= d;
+        if (t.numel() != want) {
+            std::ostringstream os;
+            os << "tensor `" << k << "` has " << t.numel() << " elements, expected " << want;
+            throw ApiError(HK_ERR_PACKAGE, os.str());
+        }
+        std::vector<float> w = to_f32(t);
+        auto lit = lora_.find(k);
+        if (lit != lora_.end()) {
+            std::vector<float> a = to_f32(*lit->second.first), b = to_f32(*lit->second.second);
+            const int64_t r = lit->second.first->shape.at(0), in = lit->second.first->shape.at(1);
+            const int64_t out = lit->second.second->shape.at(0);
+            if (shape.size() != 2 || shape[0] != out || shape[1] != in || lit->second.second->shape.at(1) != r)
+                throw ApiError(HK_ERR_BACKEND, "LoRA shape mismatch for `" + k + "`");
+            for (int64_t o = 0; o < out; ++o)
+                for (int64_t i = 0; i < in; ++i) {
+                    float d = 0.0f;
+                    for (int64_t j = 0; j < r; ++j) d = d + b[o * r + j] * a[j * in + i];
+                    w[o * in + i] = w[o * in + i] + d * lora_scale_;
+                }
+        }
+        return w;
+    }
+
+  private:
+    std::string dir_;
+    std::vector<std::unique_ptr<SafeTensors>> shards_;
+    std::unordered_map<std::string, const TensorView *> base_;
+    std::unique_ptr<SafeTensors> adapter_;
+    std::unordered_map<std::string, std::pair<const TensorView *, const TensorView *>> lora_;
+    int rank_ = 0;
+    float lora_scale_ = 1.0f;
+};
+
+// ----------------------------------------------------------------- device weights
+struct Mat {
+    void *w = nullptr;
+    float *scale = nullptr;  // int8-weight models: per row
+    int rows = 0, cols = 0, ld = 0;
+};
+
+struct Layer {
+    bool full = false;
+    float *in_norm = nullptr, *post_norm = nullptr;
+    Mat mix_in, mix_out, gu, down;
+    float *conv_w = nullptr, *base_g = nullptr, *dt_bias = nullptr, *gnorm_w = nullptr;
+    float *qn_w = nullptr, *kn_w = nullptr;
+};
+
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+}  // namespace
+
+struct Model {
+    std::string dir;
+    int device = 0;
+    int dtype = HK_DTYPE_BF16;
+    int max_context = 0;
+    int num_sms = 148;
+    KevConfig cfg;
+    bool fused_swiglu = false;
+    int lora_rank = 0;
+    float temperature = 1.0f;
+    int dp = 256;
+    cudaStream_t stream = nullptr;
+    std::vector<void *> allocs;
+    void *embed = nullptr;
+    float *final_norm = nullptr;
+    float *inv_freq = nullptr;
+    float *wq = nullptr, *bq = nullptr, *wk = nullptr, *bk = nullptr;
+    std::vector<Layer> layers;
+
+    // workspace
+    int cap_tokens = 0, cap_rows = 0, cap_readouts = 0;
+    std::vector<void *> ws;
+    float *x = nullptr;
+    void *xn = nullptr, *proj = nullptr, *mix = nullptr, *ffn = nullptr;
+    float *dq = nullptr, *dkk = nullptr, *dvv = nullptr, *dg = nullptr, *db = nullptr, *dout = nullptr;
+    void *aq = nullptr, *ak = nullptr, *av = nullptr;
+    float *hn = nullptr, *rproj = nullptr, *logits = nullptr;
+    uint32_t *err = nullptr;
+    // device batch description (see build_meta_kernel)
+    int32_t *meta = nullptr;
+    size_t meta_cap = 0;
+    // pinned staging for hk_score
+    void *pinned = nullptr;
+    size_t pinned_cap = 0;
+    int ld_xn = 0, ldp = 0, ldmix = 0, ldf = 0;
+    uint64_t launches = 0;
+    std::string last_error;
+
+    // Optional per-class device timing of the forward's launches (CUDA events
+    // on the handle's stream): 0 GEMM, 1 delta recurrence, 2 attention,
+    // 3 delta input stage, 4 everything else.
+    static constexpr int kProfClasses = 5;
+    bool prof = false;
+    struct ProfRec {
+        cudaEvent_t a, b;
+        int cls;
+        double work;
+    };
+    std::vector<ProfRec> prof_recs;
+    std::vector<cudaEvent_t> prof_pool;
+    cudaEvent_t prof_event() {
+        if (!prof_pool.empty()) {
+            cudaEvent_t e = prof_pool.back();
+            prof_pool.pop_back();
+            return e;
+        }
+        cudaEvent_t e;
+        HK_CUDA(cudaEventCreate(&e));
+        return e;
+    }
+    cudaEvent_t prof_begin() {
+        if (!prof) return nullptr;
+        cudaEvent_t e = prof_event();
+        HK_CUDA(cudaEventRecord(e, stream));
+        return e;
+    }
+    void prof_end(cudaEvent_t a, int cls, double work) {
+        if (!prof || !a) return;
+        cudaEvent_t b = prof_event();
+        HK_CUDA(cudaEventRecord(b, stream));
+        prof_recs.push_back({a, b, cls, work});
+    }
+
+    int act() const { return dtype == HK_DTYPE_FP32 ? kActF32 : kActBF16; }
+    size_t esz() const { return dtype == HK_DTYPE_FP32 ? 4 : 2; }
+
+    ~Model() {
+        if (device >= 0) cudaSetDevice(device);
+        for (auto &r : prof_recs) {
+            cudaEventDestroy(r.a);
+            cudaEventDestroy(r.b);
+        }
+        for (auto e : prof_pool) cudaEventDestroy(e);
+        for (void *p : ws) cudaFree(p);
+        for (void *p : allocs) cudaFree(p);
+        if (pinned) cudaFreeHost(pinned);
+        if (stream) cudaStreamDestroy(stream);
+    }
+
+    template <typename T>
+    T *dev_alloc(size_t count, std::vector<void *> &owner) {
+        void *p = nullptr;
+        HK_CUDA(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T)));
+        owner.push_back(p);
+        return static_cast<T *>(p);
+    }
+    float *upload_f32(const std::vector<float> &v) {
+        float *p = dev_alloc<float>(v.size(), allocs);
+        HK_CUDA(cudaMemcpy(p, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+        return p;
+    }
+
+    // Pack row blocks [(tensor, rows)] into one [R, K] matrix in the model's
+    // weight format. `order` optionally permutes output rows (SwiGLU interleave).
+    Mat pack(const WeightSource &src, const std::vector<std::pair<std::string, int>> &parts, int K,
+             const std::vector<int> *order = nullptr) {
+        int R = 0;
+        for (auto &p : parts) R += p.second;
+        std::vector<float> full(static_cast<size_t>(R) * K);
+        int r0 = 0;
+        for (auto &p : parts) {
+            std::vector<float> w = src.get(p.first, {p.second, K});
+            std::memcpy(full.data() + static_cast<size_t>(r0) * K, w.data(), w.size() * sizeof(float));
+            r0 += p.second;
+        }
+        Mat m;
+        m.rows = R;
+        m.cols = K;
+        m.ld = round_up(K, 8);
+        auto src_row = [&](int r) { return order ? (*order)[r] : r; };
+        if (dtype == HK_DTYPE_FP32) {
+            std::vector<float> h(static_cast<size_t>(R) * m.ld, 0.0f);
+            for (int r = 0; r < R; ++r)
+                std::memcpy(&h[static_cast<size_t>(r) * m.ld], &full[static_cast<size_t>(src_row(r)) * K], K * 4);
+            float *d = dev_alloc<float>(h.size(), allocs);
+            HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+            m.w = d;
+        } else {
+            std::vector<uint16_t> h(static_cast<size_t>(R) * m.ld, 0);
+            std::vector<float> sc;
+            if (dtype == HK_DTYPE_INT8W) sc.resize(R);
+            for (int r = 0; r < R; ++r) {
+                const float *row = &full[static_cast<size_t>(src_row(r)) * K];
+                uint16_t *dst = &h[static_cast<size_t>(r) * m.ld];
+                if (dtype == HK_DTYPE_INT8W) {
+                    // Symmetric per-output-channel int8: scale = max|w| / 127,
+                    // q = rint(w / scale) clamped to [-127, 127]; zero rows get scale 1.
+                    float amax = 0.0f;
+                    for (int i = 0; i < K; ++i) amax = std::max(amax, std::fabs(row[i]));
+                    float s = amax / 127.0f;
+                    if (s == 0.0f) s = 1.0f;
+                    sc[r] = s;
+                    for (int i = 0; i < K; ++i) {
+                        float q = std::nearbyint(row[i] / s);
+                        q = std::min(127.0f, std::max(-127.0f, q));
+                        dst[i] = f32_to_bf16_bits(q);  // exact for |q| <= 127
+                    }
+                } else {
+                    for (int i = 0; i < K; ++i) dst[i] = f32_to_bf16_bits(row[i]);
+                }
+            }
+            uint16_t *d = dev_alloc<uint16_t>(h.size(), allocs);
+            HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+            m.w = d;
+            if (dtype == HK_DTYPE_INT8W) m.scale = upload_f32(sc);
+        }
+        return m;
+    }
+
+    // A small fp32 tensor, rounded to bf16 first in the bf16 / int8w models
+    // (the reference loader casts every tensor to the model dtype).
+    std::vector<float> small(const WeightSource &src, const std::string &k, std::vector<int64_t> shape) {
+        std::vector<float> v = src.get(k, shape);
+        if (dtype != HK_DTYPE_FP32)
+            for (auto &x : v) x = bf16_round(x);
+        return v;
+    }
+    float *norm_eff(const WeightSource &src, const std::string &k, int n) {
+        std::vector<float> v = small(src, k, {n});
+        for (auto &x : v) x = x * 1.0f + 1.0f;  // effective_norm_weight, qwen3_5.rs:180-182
+        return upload_f32(v);
+    }
+
+    void load(const std::string &model_dir) {
+        dir = model_dir;
+        cfg = KevConfig::from_json(json::parse(read_file(model_dir + "/config.json")));
+        const KevConfig &c = cfg;
+        if (c.nv % c.nk != 0) throw ApiError(HK_ERR_UNSUPPORTED, "value heads must be a multiple of key heads");
+        if (c.nh % c.nkv != 0) throw ApiError(HK_ERR_UNSUPPORTED, "query heads must be a multiple of kv heads");
+        WeightSource src(model_dir);
+        lora_rank = src.lora_rank();
+        // Pointer head (kev.rs:118-165): fp32, shapes [dp, hidden] and [dp].
+        json::Value meta = json::parse(read_file(model_dir + "/kev_head.json"));
+        const json::Value *tv = meta.get("temperature");
+        temperature = tv && tv->is_num() ? static_cast<float>(tv->num) : 1.0f;
+        if (!std::isfinite(temperature) || temperature <= 0.0f)
+            throw ApiError(HK_ERR_PACKAGE, "invalid Kev head: temperature must be finite and positive");
+        const json::Value *hdv = meta.get("head_dim");
+        dp = hdv && hdv->is_num() ? static_cast<int>(hdv->num) : 256;
+        {
+            SafeTensors head(model_dir + "/pointer_head.safetensors");
+            auto get = [&](const std::string &n, std::vector<int64_t> shape) {
+                auto it = head.tensors().find(n);
+                if (it == head.tensors().end()) throw ApiError(HK_ERR_PACKAGE, "invalid Kev head: missing `" + n + "`");
+                if (it->second.shape != shape) {
+                    std::ostringstream os;
+                    os << "invalid Kev head: `" << n << "` shape mismatch, expected [";
+                    for (size_t i = 0; i < shape.size(); ++i) os << (i ? ", " : "") << shape[i];
+                    os << "]";
+                    throw ApiError(HK_ERR_PACKAGE, os.str());
+                }
+                std::vector<float> v = to_f32(it->second);
+                for (float f : v)
+                    if (!std::isfinite(f)) throw ApiError(HK_ERR_PACKAGE, "invalid Kev head: `" + n + "` contains non-finite weights");
+                return upload_f32(v);
+            };
+            wq = get("q.weight", {dp, c.hidden});
+            bq = get("q.bias", {dp});
+            wk = get("k.weight", {dp, c.hidden});
+            bk = get("k.bias", {dp});
+        }
+        // Embedding table in the model dtype.
+        {
+            std::vector<float> e = src.get("model.language_model.embed_tokens.weight",
+                                           {static_cast<int64_t>(c.vocab), c.hidden});
+            if (dtype == HK_DTYPE_FP32) {
+                float *d = dev_alloc<float>(e.size(), allocs);
+                HK_CUDA(cudaMemcpy(d, e.data(), e.size() * 4, cudaMemcpyHostToDevice));
+                embed = d;
+            } else {
+                std::vector<uint16_t> h(e.size());
+                for (size_t i = 0; i < e.size(); ++i) h[i] = f32_to_bf16_bits(e[i]);
+                uint16_t *d = dev_alloc<uint16_t>(h.size(), allocs);
+                HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+                embed = d;
+            }
+        }
+        final_norm = norm_eff(src, "model.language_model.norm.weight", c.hidden);
+        // RoPE inverse frequencies in fp32 (qwen3_5.rs:225-232).
+        {
+            const int rd = c.rotary_dim(), half = rd / 2;
+            std::vector<float> inv(std::max(half, 1));
+            for (int i = 0; i < half; ++i)
+                inv[i] = std::pow(static_cast<float>(c.theta), -(2.0f * static_cast<float>(i)) / static_cast<float>(rd));
+            inv_freq = upload_f32(inv);
+        }
+        fused_swiglu = dtype != HK_DTYPE_FP32 && (c.ffn % kSwiGLUBlock) == 0;
+        std::vector<int> gu_order;
+        if (fused_swiglu) {
+            for (int b = 0; b < c.ffn / kSwiGLUBlock; ++b) {
+                for (int i = 0; i < kSwiGLUBlock; ++i) gu_order.push_back(b * kSwiGLUBlock + i);
+                for (int i = 0; i < kSwiGLUBlock; ++i) gu_order.push_back(c.ffn + b * kSwiGLUBlock + i);
+            }
+        }
+        for (int i = 0; i < c.layers; ++i) {
+            const std::string p = "model.language_model.layers." + std::to_string(i);
+            Layer L;
+            L.full = c.full[i] != 0;
+            L.in_norm = norm_eff(src, p + ".input_layernorm.weight", c.hidden);
+            L.post_norm = norm_eff(src, p + ".post_attention_layernorm.weight", c.hidden);
+            if (!L.full) {
+                const std::string a = p + ".linear_attn";
+                L.mix_in = pack(src, {{a + ".in_proj_qkv.weight", c.conv_dim()}, {a + ".in_proj_z.weight", c.value_dim()},
+                                      {a + ".in_proj_b.weight", c.nv}, {a + ".in_proj_a.weight", c.nv}},
+                                c.hidden);
+                L.mix_out = pack(src, {{a + ".out_proj.weight", c.hidden}}, c.value_dim());
+                L.conv_w = upload_f32(small(src, a + ".conv1d.weight", {c.conv_dim(), 1, c.taps}));
+                std::vector<float> alog = small(src, a + ".A_log", {c.nv});
+                for (auto &v : alog) v = -std::exp(v);  // base_g = -exp(A_log), qwen3_5.rs:800
+                L.base_g = upload_f32(alog);
+                L.dt_bias = upload_f32(small(src, a + ".dt_bias", {c.nv}));
+                L.gnorm_w = upload_f32(small(src, a + ".norm.weight", {c.dv}));
+            } else {
+                const std::string a = p + ".self_attn";
+                L.mix_in = pack(src, {{a + ".q_proj.weight", c.nh * c.hd * 2}, {a + ".k_proj.weight", c.nkv * c.hd},
+                                      {a + ".v_proj.weight", c.nkv * c.hd}},
+                                c.hidden);
+                L.mix_out = pack(src, {{a + ".o_proj.weight", c.hidden}}, c.nh * c.hd);
+                L.qn_w = norm_eff(src, a + ".q_norm.weight", c.hd);
+                L.kn_w = norm_eff(src, a + ".k_norm.weight", c.hd);
+            }
+            const std::string m = p + ".mlp";
+            L.gu = pack(src, {{m + ".gate_proj.weight", c.ffn}, {m + ".up_proj.weight", c.ffn}}, c.hidden,
+                        fused_swiglu ? &gu_order : nullptr);
+            L.down = pack(src, {{m + ".down_proj.weight", c.hidden}}, c.ffn);
+            layers.push_back(L);
+        }
+        ld_xn = round_up(c.hidden, 8);
+        const int pd = c.conv_dim() + c.value_dim() + 2 * c.nv;
+        const int pa = c.nh * c.hd * 2 + 2 * c.nkv * c.hd;
+        ldp = round_up(std::max(std::max(pd, pa), fused_swiglu ? 0 : 2 * c.ffn), 8);
+        ldmix = round_up(std::max(c.value_dim(), c.nh * c.hd), 8);
+        ldf = round_up(c.ffn, 8);
+        err = dev_alloc<uint32_t>(1, allocs);
+        HK_CUDA(cudaMemset(err, 0, 4));
+    }
+
+    void ensure_workspace(int tokens, int rows, int readouts) {
+        if (tokens <= cap_tokens && rows <= cap_rows && readouts <= cap_readouts) return;
+        for (void *p : ws) cudaFree(p);
+        ws.clear();
+        cap_tokens = std::max(tokens, cap_tokens);
+        cap_tokens = round_up(std::max(cap_tokens, 256), 256);
+        cap_rows = std::max(std::max(rows, cap_rows), HK_MAX_ROWS);
+        cap_readouts = round_up(std::max(std::max(readouts, cap_readouts), 1024), 256);
+        const KevConfig &c = cfg;
+        const size_t N = cap_tokens, R = cap_readouts + cap_rows, e = esz();
+        x = dev_alloc<float>(N * c.hidden, ws);
+        xn = dev_alloc<uint8_t>(N * ld_xn * e, ws);
+        proj = dev_alloc<uint8_t>(N * ldp * e, ws);
+        mix = dev_alloc<uint8_t>(N * ldmix * e, ws);
+        ffn = dev_alloc<uint8_t>(N * ldf * e, ws);
+        HK_CUDA(cudaMemset(xn, 0, N * ld_xn * e));
+        HK_CUDA(cudaMemset(mix, 0, N * ldmix * e));
+        HK_CUDA(cudaMemset(ffn, 0, N * ldf * e));
+        dq = dev_alloc<float>(N * c.key_dim(), ws);
+        dkk = dev_alloc<float>(N * c.key_dim(), ws);
+        dvv = dev_alloc<float>(N * c.value_dim(), ws);
+        dg = dev_alloc<float>(N * c.nv, ws);
+        db = dev_alloc<float>(N * c.nv, ws);
+        dout = dev_alloc<float>(N * c.value_dim(), ws);
+        aq = dev_alloc<uint8_t>(N * c.nh * c.hd * e, ws);
+        ak = dev_alloc<uint8_t>(N * c.nkv * c.hd * e, ws);
+        av = dev_alloc<uint8_t>(N * c.nkv * c.hd * e, ws);
+        hn = dev_alloc<float>(R * c.hidden, ws);
+        rproj = dev_alloc<float>(R * dp, ws);
+        logits = dev_alloc<float>(R, ws);
+        meta_cap = 4 * N + 4 * static_cast<size_t>(cap_rows) + 4 * R + 64;
+        meta = dev_alloc<int32_t>(meta_cap, ws);
+    }
+
+    void gemm(const Mat &W, const void *xin, int ldx, int M, void *out, int ldo, int epi) {
+        GemmArgs a;
+        a.M = M;
+        a.N = W.rows;
+        a.K = W.cols;
+        a.x = xin;
+        a.ldx = ldx;
+        a.w = W.w;
+        a.ldw = W.ld;
+        a.scale = W.scale;
+        a.out = out;
+        a.ldo = ldo;
+        a.epilogue = epi;
+        a.err = err;
+        cudaEvent_t ev = prof_begin();
+        if (dtype == HK_DTYPE_FP32)
+            gemm_f32_simt(a, stream);
+        else
+            gemm_bf16_tc(a, stream, num_sms);
+        prof_end(ev, 0, 2.0 * M * W.rows * W.cols);
+    }
+
+    // The forward over a packed batch whose description is already on the
+    // device in `meta` (layout: see MetaLayout).
+    void forward(int n_rows, int n_tok, int max_len, int n_opt, const uint32_t *ids,
+                 const int32_t *cu_seqlens, const int32_t *pos, const int32_t *tok_row,
+                 const int32_t *ridx, const int32_t *opt_dec, float *out_logits) {
+        const KevConfig &c = cfg;
+        const int A = act();
+        const size_t e = esz();
+        cudaEvent_t ev = prof_begin();
+        launch_embed(A, ids, n_tok, embed, c.hidden, x, stream);
+        prof_end(ev, 4, 0);
+        for (const Layer &L : layers) {
+            ev = prof_begin();
+            launch_rmsnorm(A, x, c.hidden, L.in_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream);
+            prof_end(ev, 4, 0);
+            gemm(L.mix_in, xn, ld_xn, n_tok, proj, ldp, kEpiStore);
+            if (!L.full) {
+                DeltaPrepArgs d;
+                d.proj = proj;
+                d.ldp = ldp;
+                d.pos = pos;
+                d.n = n_tok;
+                d.conv_w = L.conv_w;
+                d.taps = c.taps;
+                d.base_g = L.base_g;
+                d.dt_bias = L.dt_bias;
+                d.nk = c.nk;
+                d.nv = c.nv;
+                d.dk = c.dk;
+                d.dv = c.dv;
+                d.q = dq;
+                d.k = dkk;
+                d.v = dvv;
+                d.g = dg;
+                d.beta = db;
+                ev = prof_begin();
+                launch_delta_prep(A, d, stream);
+                prof_end(ev, 3, 0);
+                DeltaRecArgs r;
+                r.q = dq;
+                r.k = dkk;
+                r.v = dvv;
+                r.g = dg;
+                r.beta = db;
+                r.cu_seqlens = cu_seqlens;
+                r.n_rows = n_rows;
+                r.nk = c.nk;
+                r.nv = c.nv;
+                r.dk = c.dk;
+                r.dv = c.dv;
+                r.out = dout;
+                r.exact = dtype == HK_DTYPE_FP32;
+                ev = prof_begin();
+                launch_delta_recurrent(r, stream);
+                prof_end(ev, 1, 4.0 * n_tok * c.nv * c.dk * c.dv);
+                ev = prof_begin();
+                launch_gated_norm(A, dout, static_cast<uint8_t *>(proj) + static_cast<size_t>(c.conv_dim()) * e, ldp,
+                                  L.gnorm_w, c.eps, n_tok, c.nv, c.dv, mix, ldmix, stream);
+                prof_end(ev, 4, 0);
+            } else {
+                AttnPrepArgs p;
+                p.proj = proj;
+                p.ldp = ldp;
+                p.pos = pos;
+                p.n = n_tok;
+                p.nh = c.nh;
+                p.nkv = c.nkv;
+                p.hd = c.hd;
+                p.rd = c.rotary_dim();
+                p.qn_w = L.qn_w;
+                p.kn_w = L.kn_w;
+                p.inv_freq = inv_freq;
+                p.eps = c.eps;
+                p.q = aq;
+                p.k = ak;
+                p.v = av;
+                ev = prof_begin();
+                launch_attn_prep(A, p, stream);
+                prof_end(ev, 4, 0);
+                AttnArgs at;
+                at.q = aq;
+                at.k = ak;
+                at.v = av;
+                at.proj = proj;
+                at.ldp = ldp;
+                at.cu_seqlens = cu_seqlens;
+                at.tok_row = tok_row;
+                at.n = n_tok;
+                at.n_rows = n_rows;
+                at.max_len = max_len;
+                at.nh = c.nh;
+                at.nkv = c.nkv;
+                at.hd = c.hd;
+                at.out = mix;
+                at.ldo = ldmix;
+                ev = prof_begin();
+                launch_attention(A, at, stream);
+                prof_end(ev, 2, 0);
+            }
+            gemm(L.mix_out, mix, ldmix, n_tok, x, c.hidden, kEpiResidual);
+            ev = prof_begin();
+            launch_rmsnorm(A, x, c.hidden, L.post_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream);
+            prof_end(ev, 4, 0);
+            if (fused_swiglu) {
+                gemm(L.gu, xn, ld_xn, n_tok, ffn, ldf, kEpiSwiGLU);
+            } else {
+                gemm(L.gu, xn, ld_xn, n_tok, proj, ldp, kEpiStore);
+                ev = prof_begin();
+                launch_swiglu(A, proj, ldp, n_tok, c.ffn, ffn, ldf, stream);
+                prof_end(ev, 4, 0);
+            }
+            gemm(L.down, ffn, ldf, n_tok, x, c.hidden, kEpiResidual);
+        }
+        ReadoutArgs ro;
+        ro.x = x;
+        ro.hidden = c.hidden;
+        ro.final_w = final_norm;
+        ro.eps = c.eps;
+        ro.idx = ridx;
+        ro.opt_dec = opt_dec;
+        ro.n_dec = n_rows;
+        ro.n_opt = n_opt;
+        ro.wq = wq;
+        ro.bq = bq;
+        ro.wk = wk;
+        ro.bk = bk;
+        ro.dp = dp;
+        ro.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dp)));
+        ro.hn = hn;
+        ro.proj = rproj;
+        ro.logits = out_logits;
+        ev = prof_begin();
+        launch_readout(ro, stream);
+        prof_end(ev, 4, 0);
+    }
+};
+
+// ----------------------------------------------------------------- batch meta
+// Device layout of one batch in Model::meta (int32 words):
+//   ids[N] | cu_seqlens[R+1] | positions[P] | cu_positions[R+1]     (inputs)
+//   pos[N] | tok_row[N] | ridx[R + P] | opt_dec[P]                  (derived)
+// ridx lists the decision token of every row, then every option token.
+struct MetaLayout {
+    size_t ids, cu, positions, cu_pos, pos, tok_row, ridx, opt_dec, total;
+    MetaLayout(int rows, int n, int p) {
+        ids = 0;
+        cu = ids + n;
+        positions = cu + rows + 1;
+        cu_pos = positions + p;
+        pos = cu_pos + rows + 1;
+        tok_row = pos + n;
+        ridx = tok_row + n;
+        opt_dec = ridx + rows + p;
+        total = opt_dec + p;
+    }
+};
+
+namespace {
+
+__device__ int find_row(const int32_t *cu, int rows, int v) {
+    int lo = 0, hi = rows - 1;  // largest r with cu[r] <= v
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) / 2;
+        if (cu[mid] <= v)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+
+__global__ void build_meta_kernel(int32_t *meta, int rows, int n, int p, MetaLayout L) {
+    const int32_t *cu = meta + L.cu;
+    const int32_t *cup = meta + L.cu_pos;
+    const int32_t *positions = meta + L.positions;
+    const int total = n + rows + p;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        if (i < n) {
+            const int r = find_row(cu, rows, i);
+            meta[L.tok_row + i] = r;
+            meta[L.pos + i] = i - cu[r];
+        } else if (i < n + rows) {
+            const int r = i - n;
+            meta[L.ridx + r] = cu[r + 1] - 1;
+        } else {
+            const int j = i - n - rows;
+            const int r = find_row(cup, rows, j);
+            meta[L.opt_dec + j] = r;
+            meta[L.ridx + rows + j] = cu[r] + positions[j];
+        }
+    }
+}
+
+}  // namespace
+
+}  // namespace hk
+
+// =================================================================== C ABI
+struct hk_model {
+    std::unique_ptr<hk::Model> m;
+};
+
+namespace {
+
+thread_local std::string tl_create_error;
+
+int fail(hk_model *h, int code, const std::string &msg) {
+    if (h && h->m) h->m->last_error = msg;
+    return code;
+}
+
+template <typename F>
+int guarded(hk_model *h, F &&f) {
+    try {
+        return f();
+    } catch (const hk::ApiError &e) {
+        return fail(h, e.code, e.what());
+    } catch (const hk::CudaError &e) {
+        return fail(h, HK_ERR_CUDA, e.what());
+    } catch (const std::exception &e) {
+        return fail(h, HK_ERR_PACKAGE, e.what());
+    }
+}
+
+int create_impl(const std::string &dir, int device, int dtype, int max_context, hk_model **out) {
+    *out = nullptr;
+    if (dtype != HK_DTYPE_FP32 && dtype != HK_DTYPE_BF16 && dtype != HK_DTYPE_INT8W) {
+        tl_create_error = "unsupported dtype";
+        return HK_ERR_UNSUPPORTED;
+    }
+    std::unique_ptr<hk_model> h(new hk_model);
+    h->m.reset(new hk::Model);
+    hk::Model &m = *h->m;
+    try {
+        int ndev = 0;
+        HK_CUDA(cudaGetDeviceCount(&ndev));
+        if (device < 0 || device >= ndev) throw hk::ApiError(HK_ERR_BACKEND, "no CUDA device " + std::to_string(device));
+        m.device = device;
+        HK_CUDA(cudaSetDevice(device));
+        int major = 0;
+        HK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+        if (major != 10)
+            throw hk::ApiError(HK_ERR_UNSUPPORTED, "this build targets sm_100a (B200); device is sm_" +
+                                                       std::to_string(major) + "x");
+        HK_CUDA(cudaDeviceGetAttribute(&m.num_sms, cudaDevAttrMultiProcessorCount, device));
+        HK_CUDA(cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking));
+        m.dtype = dtype;
+        m.max_context = max_context;
+        m.load(dir);
+        HK_CUDA(cudaDeviceSynchronize());
+    } catch (const hk::ApiError &e) {
+        tl_create_error = e.what();
+        return e.code;
+    } catch (const hk::CudaError &e) {
+        tl_create_error = e.what();
+        return HK_ERR_CUDA;
+    } catch (const std::exception &e) {
+        tl_create_error = std::string("invalid Kev package: ") + e.what();
+        return HK_ERR_PACKAGE;
+    }
+    *out = h.release();
+    return HK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hk_create(const char *model_dir, int device, int dtype, int max_context, hk_model **out) {
+    if (!model_dir || !out) return HK_ERR_ARGUMENT;
+    if (max_context <= 0) {
+        tl_create_error = "max_context must be positive";
+        return HK_ERR_ARGUMENT;
+    }
+    return create_impl(model_dir, device, dtype, max_context, out);
+}
+
+int hk_replica(const hk_model *src, int device, hk_model **out) {
+    if (!src || !out || !src->m) return HK_ERR_ARGUMENT;
+    return create_impl(src->m->dir, device, src->m->dtype, src->m->max_context, out);
+}
+
+int hk_capabilities_get(const hk_model *h, hk_capabilities *out) {
+    if (!h || !out || !h->m) return HK_ERR_ARGUMENT;
+    const hk::Model &m = *h->m;
+    out->dtype = m.dtype;
+    out->device = m.device;
+    out->max_context = m.max_context;
+    out->max_rows = HK_MAX_ROWS;
+    out->hidden_size = m.cfg.hidden;
+    out->num_layers = m.cfg.layers;
+    out->vocab_size = m.cfg.vocab;
+    out->pointer_dim = m.dp;
+    out->temperature = m.temperature;
+    out->lora_rank = m.lora_rank;
+    return HK_OK;
+}
+
+static int score_device_impl(hk::Model &m, int n_rows, const int32_t *cu_h, const int32_t *cup_h,
+                             cudaStream_t stream) {
+    (void)stream;
+    const int n = cu_h[n_rows], p = cup_h[n_rows];
+    int max_len = 0;
+    for (int r = 0; r < n_rows; ++r) max_len = std::max(max_len, cu_h[r + 1] - cu_h[r]);
+    hk::MetaLayout L(n_rows, n, p);
+    const uint64_t before = hk::tl_launches;
+    hk::build_meta_kernel<<<std::min(hk::ceil_div(L.total, 256), 1024), 256, 0, m.stream>>>(m.meta, n_rows, n, p, L);
+    HK_LAUNCH_CHECK();
+    m.forward(n_rows, n, max_len, p, reinterpret_cast<const uint32_t *>(m.meta + L.ids), m.meta + L.cu,
+              m.meta + L.pos, m.meta + L.tok_row, m.meta + L.ridx, m.meta + L.opt_dec, m.logits);
+    m.launches += hk::tl_launches - before;
+    return HK_OK;
+}
+
+int hk_score(hk_model *h, int n_rows, const uint32_t *tokens, const int32_t *cu_seqlens,
+             const int32_t *positions, const int32_t *cu_positions, float *out_logits) {
+    if (!h || !h->m || !cu_seqlens || !cu_positions) return HK_ERR_ARGUMENT;
+    hk::Model &m = *h->m;
+    return guarded(h, [&]() -> int {
+        // Validation mirrors forward_independent_batch (qwen3_5.rs:3143-3171)
+        // and Backend::forward (qwen3_5.rs:2669-2705).
+        if (n_rows < 1 || n_rows > HK_MAX_ROWS)
+            throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 batch must contain 1..=64 independent rows");
+        if (cu_seqlens[0] != 0 || cu_positions[0] != 0)
+            throw hk::ApiError(HK_ERR_ARGUMENT, "cu_seqlens[0] and cu_positions[0] must be 0");
+        for (int r = 0; r < n_rows; ++r) {
+            const int len = cu_seqlens[r + 1] - cu_seqlens[r];
+            const int np = cu_positions[r + 1] - cu_positions[r];
+            if (len <= 0)
+                throw hk::ApiError(HK_ERR_BACKEND,
+                                   "Qwen3.5 batches require valid independent rows without cache handles");
+            if (np < 0) throw hk::ApiError(HK_ERR_ARGUMENT, "cu_positions must be non-decreasing");
+            if (len > m.max_context)
+                throw hk::ApiError(HK_ERR_BACKEND, "sequence length " + std::to_string(len) +
+                                                       " exceeds max_context " + std::to_string(m.max_context));
+            for (int i = cu_seqlens[r]; i < cu_seqlens[r + 1]; ++i)
+                if (tokens[i] >= static_cast<uint32_t>(m.cfg.vocab))
+                    throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 token ID is outside the vocabulary");
+            for (int j = cu_positions[r]; j < cu_positions[r + 1]; ++j)
+                if (positions[j] < 0 || positions[j] >= len)
+                    throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 readout position is outside the token sequence");
+        }
+        const int n = cu_seqlens[n_rows], p = cu_positions[n_rows];
+        HK_CUDA(cudaSetDevice(m.device));
+        m.ensure_workspace(n, n_rows, p);
+        hk::MetaLayout L(n_rows, n, p);
+        const size_t in_words = L.pos;  // ids | cu | positions | cu_pos
+        const size_t bytes = in_words * 4 + static_cast<size_t>(p) * 4 + 64;
+        if (bytes > m.pinned_cap) {
+            if (m.pinned) cudaFreeHost(m.pinned);
+            m.pinned = nullptr;
+            m.pinned_cap = 0;
+            HK_CUDA(cudaHostAlloc(&m.pinned, bytes * 2, cudaHostAllocDefault));
+            m.pinned_cap = bytes * 2;
+        }
+        int32_t *st = static_cast<int32_t *>(m.pinned);
+        std::memcpy(st + L.ids, tokens, static_cast<size_t>(n) * 4);
+        std::memcpy(st + L.cu, cu_seqlens, static_cast<size_t>(n_rows + 1) * 4);
+        if (p) std::memcpy(st + L.positions, positions, static_cast<size_t>(p) * 4);
+        std::memcpy(st + L.cu_pos, cu_positions, static_cast<size_t>(n_rows + 1) * 4);
+        HK_CUDA(cudaMemcpyAsync(m.meta, st, in_words * 4, cudaMemcpyHostToDevice, m.stream));
+        score_device_impl(m, n_rows, cu_seqlens, cu_positions, m.stream);
+        float *res = reinterpret_cast<float *>(st + in_words);
+        uint32_t *errw = reinterpret_cast<uint32_t *>(res + p);
+        if (p) HK_CUDA(cudaMemcpyAsync(res, m.logits, static_cast<size_t>(p) * 4, cudaMemcpyDeviceToHost, m.stream));
+        HK_CUDA(cudaMemcpyAsync(errw, m.err, 4, cudaMemcpyDeviceToHost, m.stream));
+        HK_CUDA(cudaStreamSynchronize(m.stream));
+        if (*errw) {
+            HK_CUDA(cudaMemsetAsync(m.err, 0, 4, m.stream));
+            HK_CUDA(cudaStreamSynchronize(m.stream));
+            throw hk::ApiError(HK_ERR_CUDA, "device error flag " + std::to_string(*errw) + " set during the forward");
+        }
+        if (p) std::memcpy(out_logits, res, static_cast<size_t>(p) * 4);
+        return HK_OK;
+    });
+}
+
+int hk_score_device(hk_model *h, int n_rows, const int32_t *cu_seqlens_host, const int32_t *cu_positions_host,
+                    const uint32_t *d_tokens, const int32_t *d_cu_seqlens, const int32_t *d_positions,
+                    float *d_out_logits, void *stream) {
+    if (!h || !h->m || !cu_seqlens_host || !cu_positions_host || !d_tokens || !d_cu_seqlens) return HK_ERR_ARGUMENT;
+    hk::Model &m = *h->m;
+    return guarded(h, [&]() -> int {
+        if (n_rows < 1 || n_rows > HK_MAX_ROWS)
+            throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 batch must contain 1..=64 independent rows");
+        const int n = cu_seqlens_host[n_rows], p = cu_positions_host[n_rows];
+        HK_CUDA(cudaSetDevice(m.device));
+        m.ensure_workspace(n, n_rows, p);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.stream;
+        cudaStream_t own = m.stream;
+        m.stream = s;
+        hk::MetaLayout L(n_rows, n, p);
+        HK_CUDA(cudaMemcpyAsync(m.meta + L.ids, d_tokens, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToDevice, s));
+        HK_CUDA(cudaMemcpyAsync(m.meta + L.cu, d_cu_seqlens, static_cast<size_t>(n_rows + 1) * 4,
+                                cudaMemcpyDeviceToDevice, s));
+        if (p)
+            HK_CUDA(cudaMemcpyAsync(m.meta + L.positions, d_positions, static_cast<size_t>(p) * 4,
+                                    cudaMemcpyDeviceToDevice, s));
+        HK_CUDA(cudaMemcpyAsync(m.meta + L.cu_pos, cu_positions_host, static_cast<size_t>(n_rows + 1) * 4,
+                                cudaMemcpyHostToDevice, s));
+        int rc;
+        try {
+            rc = score_device_impl(m, n_rows, cu_seqlens_host, cu_positions_host, s);
+            if (p)
+                HK_CUDA(cudaMemcpyAsync(d_out_logits, m.logits, static_cast<size_t>(p) * 4, cudaMemcpyDeviceToDevice, s));
+        } catch (...) {
+            m.stream = own;
+            throw;
+        }
+        m.stream = own;
+        return rc;
+    });
+}
+
+int hk_synchronize(hk_model *h) {
+    if (!h || !h->m) return HK_ERR_ARGUMENT;
+    hk::Model &m = *h->m;
+    return guarded(h, [&]() -> int {
+        HK_CUDA(cudaSetDevice(m.device));
+        HK_CUDA(cudaDeviceSynchronize());
+        uint32_t e = 0;
+        HK_CUDA(cudaMemcpy(&e, m.err, 4, cudaMemcpyDeviceToHost));
+        if (e) {
+            HK_CUDA(cudaMemset(m.err, 0, 4));
+            throw hk::ApiError(HK_ERR_CUDA, "device error flag " + std::to_string(e) + " set during the forward");
+        }
+        return HK_OK;
+    });
+}
+
+uint64_t hk_kernel_launches(const hk_model *h) { return (h && h->m) ? h->m->launches : 0; }
+
+int hk_profile_enable(hk_model *h, int enable) {
+    if (!h || !h->m) return HK_ERR_ARGUMENT;
+    h->m->prof = enable != 0;
+    return HK_OK;
+}
+
+int hk_profile_read(hk_model *h, double *ms, double *work, int64_t *count, int n_classes) {
+    if (!h || !h->m || !ms || !work || !count) return HK_ERR_ARGUMENT;
+    hk::Model &m = *h->m;
+    return guarded(h, [&]() -> int {
+        HK_CUDA(cudaSetDevice(m.device));
+        HK_CUDA(cudaDeviceSynchronize());  // events may sit on a caller's stream
+        for (int i = 0; i < n_classes; ++i) {
+            ms[i] = 0.0;
+            work[i] = 0.0;
+            count[i] = 0;
+        }
+        for (auto &r : m.prof_recs) {
+            float t = 0.f;
+            HK_CUDA(cudaEventElapsedTime(&t, r.a, r.b));
+            if (r.cls < n_classes) {
+                ms[r.cls] += t;
+                work[r.cls] += r.work;
+                count[r.cls] += 1;
+            }
+            m.prof_pool.push_back(r.a);
+            m.prof_pool.push_back(r.b);
+        }
+        m.prof_recs.clear();
+        return HK_OK;
+    });
+}
+
+const char *hk_last_error(const hk_model *h) {
+    if (!h || !h->m) return "null handle";
+    return h->m->last_error.c_str();
+}
+
+const char *hk_create_error(void) { return tl_create_error.c_str(); }
+
+void hk_destroy(hk_model *h) { delete h; }
+
+}  // extern "C"

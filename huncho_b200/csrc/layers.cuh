@@ -1,0 +1,110 @@
+// Host launchers for the bandwidth-bound Kev layer kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hk {
+
+// Activation type selector for the launchers: the fp32 model runs float
+// activations, the bf16 and int8-weight models bf16.
+enum ActType : int { kActF32 = 0, kActBF16 = 1 };
+
+// x[t, :] = table[ids[t], :] widened to fp32 (qwen3_5.rs:1319-1323, 1537).
+void launch_embed(int act, const uint32_t *ids, int n, const void *table, int hidden, float *x,
+                  cudaStream_t s);
+
+// out[r, :] = rms_norm(x[r, :]) * w_eff (qwen3_5.rs:180-190); w_eff = 1 + w, fp32.
+void launch_rmsnorm(int act, const float *x, int ldx, const float *w_eff, float eps, int rows,
+                    int hidden, void *out, int ldo, cudaStream_t s);
+
+// Gated DeltaNet input stage for every token (qwen3_5.rs:817-925): causal
+// depthwise conv (K taps, restricted to the token's own row) + SiLU on the
+// q|k|v channels of proj, L2 norm of q and k per key head (q also scaled by
+// 1/sqrt(dk)), beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias).
+struct DeltaPrepArgs {
+    const void *proj;  // [n, ldp]: qkv (conv_dim) | z (vd) | b (nv) | a (nv)
+    int ldp;
+    const int32_t *pos;  // position of each token inside its row
+    int n;
+    const float *conv_w;  // [conv_dim, taps]
+    int taps;
+    const float *base_g;   // -exp(A_log) [nv]
+    const float *dt_bias;  // [nv]
+    int nk, nv, dk, dv;
+    float *q, *k;  // [n, nk, dk] fp32
+    float *v;      // [n, nv, dv] fp32
+    float *g, *beta;  // [n, nv] fp32
+};
+void launch_delta_prep(int act, const DeltaPrepArgs &a, cudaStream_t s);
+
+// Per-token gated delta rule with an fp32 state per (row, value head)
+// (qwen3_5.rs:950-987). `exact` keeps the reference's ascending-key fp32
+// operation order with no fused multiply-adds (delta_cpu.rs:99-136).
+struct DeltaRecArgs {
+    const float *q, *k, *v, *g, *beta;
+    const int32_t *cu_seqlens;
+    int n_rows, nk, nv, dk, dv;
+    float *out;  // [n, nv, dv]
+    int exact;
+};
+void launch_delta_recurrent(const DeltaRecArgs &a, cudaStream_t s);
+
+// out[t, h*dv + j] = rms(o)[j] * w[j] * silu(z[t, h, j]) after rounding o to
+// the activation type (qwen3_5.rs:193-201, 934-938).
+void launch_gated_norm(int act, const float *o, const void *z, int ldz, const float *w, float eps,
+                       int n, int nv, int dv, void *out, int ldo, cudaStream_t s);
+
+// Full-attention input stage (qwen3_5.rs:596-615): split q | gate per head,
+// q_norm / k_norm (zero-centred weights, fp32), partial RoPE on the first
+// rotary_dim dims at each token's in-row position.
+struct AttnPrepArgs {
+    const void *proj;  // [n, ldp]: per q head [q(hd) | gate(hd)], then k (nkv*hd), v (nkv*hd)
+    int ldp;
+    const int32_t *pos;
+    int n, nh, nkv, hd, rd;
+    const float *qn_w, *kn_w;  // effective norm weights [hd]
+    const float *inv_freq;     // [rd/2]
+    float eps;
+    void *q, *k, *v;  // [n, nh, hd], [n, nkv, hd], [n, nkv, hd]
+};
+void launch_attn_prep(int act, const AttnPrepArgs &a, cudaStream_t s);
+
+// Causal softmax(q k^T / sqrt(hd)) v per row with GQA (qwen3_5.rs:669-714),
+// multiplied by sigmoid(gate) and written token-major [n, nh*hd].
+struct AttnArgs {
+    const void *q, *k, *v;  // [n, nh, hd], [n, nkv, hd], [n, nkv, hd]
+    const void *proj;       // gate source: proj[t, h*2*hd + hd + i]
+    int ldp;
+    const int32_t *cu_seqlens;
+    const int32_t *tok_row;  // row of each token
+    int n, n_rows, max_len, nh, nkv, hd;
+    void *out;
+    int ldo;
+};
+void launch_attention(int act, const AttnArgs &a, cudaStream_t s);
+
+// out[t, j] = silu(gu[t, j]) * gu[t, F + j] (qwen3_5.rs:1020-1031).
+void launch_swiglu(int act, const void *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s);
+
+// Pointer readout (qwen3_5.rs:3196-3255, kev.rs:169-173). idx lists the token
+// rows to read: first the n_dec decision rows, then the n_opt option rows.
+struct ReadoutArgs {
+    const float *x;  // residual stream [n, hidden] (before the final norm)
+    int hidden;
+    const float *final_w;  // effective final norm weight
+    float eps;
+    const int32_t *idx;   // [n_dec + n_opt] token indices
+    const int32_t *opt_dec;  // [n_opt] decision row of each option
+    int n_dec, n_opt;
+    const float *wq, *bq, *wk, *bk;  // [dp, hidden], [dp]
+    int dp;
+    float scale;  // 1 / sqrt(dp), rounded from double as the reference does
+    float *hn;    // scratch [n_dec + n_opt, hidden]
+    float *proj;  // scratch [n_dec + n_opt, dp]
+    float *logits;  // [n_opt]
+};
+void launch_readout(const ReadoutArgs &a, cudaStream_t s);
+
+}  // namespace hk

@@ -1,0 +1,112 @@
+// Kernel-level C entry points (include/huncho_kev_ops.h) for per-kernel
+// parity tests and timing.
+#include <string>
+
+#include "../../include/huncho_kev.h"
+#include "../../include/huncho_kev_ops.h"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "layers.cuh"
+
+namespace {
+thread_local std::string tl_op_error;
+
+template <typename F>
+int op_guard(F &&f) {
+    try {
+        f();
+        return HK_OK;
+    } catch (const hk::CudaError &e) {
+        tl_op_error = e.what();
+        return HK_ERR_CUDA;
+    } catch (const std::exception &e) {
+        tl_op_error = e.what();
+        return HK_ERR_ARGUMENT;
+    }
+}
+
+int current_sms() {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+}  // namespace
+
+extern "C" {
+
+int hk_op_gemm(int dtype, int epilogue, int M, int N, int K, const void *x, int ldx, const void *w, int ldw,
+               const float *scale, void *out, int ldo, void *stream) {
+    return op_guard([&] {
+        hk::GemmArgs a;
+        a.M = M;
+        a.N = N;
+        a.K = K;
+        a.x = x;
+        a.ldx = ldx;
+        a.w = w;
+        a.ldw = ldw;
+        a.scale = scale;
+        a.out = out;
+        a.ldo = ldo;
+        a.epilogue = epilogue;
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (dtype == 0)
+            hk::gemm_f32_simt(a, s);
+        else if (dtype == 1)
+            hk::gemm_bf16_tc(a, s, current_sms());
+        else
+            throw std::runtime_error("hk_op_gemm: dtype must be 0 (fp32) or 1 (bf16)");
+    });
+}
+
+int hk_op_delta_recurrent(const float *q, const float *k, const float *v, const float *g, const float *beta,
+                          const int32_t *cu_seqlens, int n_rows, int nk, int nv, int dk, int dv, int exact,
+                          float *out, void *stream) {
+    return op_guard([&] {
+        hk::DeltaRecArgs a;
+        a.q = q;
+        a.k = k;
+        a.v = v;
+        a.g = g;
+        a.beta = beta;
+        a.cu_seqlens = cu_seqlens;
+        a.n_rows = n_rows;
+        a.nk = nk;
+        a.nv = nv;
+        a.dk = dk;
+        a.dv = dv;
+        a.out = out;
+        a.exact = exact;
+        hk::launch_delta_recurrent(a, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int hk_op_attention(int act, const void *q, const void *k, const void *v, const void *proj, int ldp,
+                    const int32_t *cu_seqlens, const int32_t *tok_row, int n, int n_rows, int max_len, int nh,
+                    int nkv, int hd, void *out, int ldo, void *stream) {
+    return op_guard([&] {
+        hk::AttnArgs a;
+        a.q = q;
+        a.k = k;
+        a.v = v;
+        a.proj = proj;
+        a.ldp = ldp;
+        a.cu_seqlens = cu_seqlens;
+        a.tok_row = tok_row;
+        a.n = n;
+        a.n_rows = n_rows;
+        a.max_len = max_len;
+        a.nh = nh;
+        a.nkv = nkv;
+        a.hd = hd;
+        a.out = out;
+        a.ldo = ldo;
+        hk::launch_attention(act, a, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int hk_op_num_sms(void) { return current_sms(); }
+
+const char *hk_op_last_error(void) { return tl_op_error.c_str(); }
+
+}  // extern "C"

@@ -1,0 +1,141 @@
+/*
+ * huncho_kev.h -- C ABI of the B200-native Kev scoring forward.
+ *
+ * One handle is one Kev scorer on one GPU: the Qwen3.5-hybrid backbone
+ * (Gated DeltaNet + gated GQA), its merged LoRA and the fp32 pointer head, with
+ * a CUDA stream and a device workspace of its own. The entry points replace the
+ * reference's `Backend` trait implementation for Kev
+ * (crates/huncho-core/src/backend.rs:211-438, implemented by
+ * crates/huncho-backend/src/qwen3_5.rs:2515-3266). Calibration, answers and
+ * batching stay with the caller (huncho-core), exactly as they do above the
+ * reference trait.
+ *
+ * Plain pointers and sizes only. All calls on one handle must come from one
+ * thread at a time (the reference backend is `&mut self`, used behind a Mutex:
+ * crates/huncho-core/src/engine.rs:173-180); concurrency comes from replicas,
+ * one handle per GPU (crates/huncho-api/src/replicas.rs:7-61).
+ */
+#ifndef HUNCHO_KEV_H
+#define HUNCHO_KEV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. They map onto huncho_core::error::Error variants
+ * (crates/huncho-core/src/error.rs:10-45). */
+#define HK_OK 0
+#define HK_ERR_BACKEND (-1)     /* Error::Backend: invalid request or failed inference  */
+#define HK_ERR_UNSUPPORTED (-2) /* Error::Unsupported                                  */
+#define HK_ERR_PACKAGE (-3)     /* Error::Package: unreadable or inconsistent model dir */
+#define HK_ERR_CUDA (-4)        /* Error::Backend raised by a CUDA failure             */
+#define HK_ERR_ARGUMENT (-5)    /* null pointer or bad enum at the C boundary          */
+
+/* Model dtypes. HK_FP32 and HK_BF16 are the weight and activation types;
+ * HK_INT8W is int8 per-output-channel symmetric projection weights
+ * (scale = max|w| / 127, fp32 scales) with bf16 activations. */
+#define HK_DTYPE_FP32 0
+#define HK_DTYPE_BF16 1
+#define HK_DTYPE_INT8W 2
+
+/* The reference's hard limit on independent rows per native batch
+ * (qwen3_5.rs:3143-3148; BatchLimits default, backend.rs:108-121). */
+#define HK_MAX_ROWS 64
+
+typedef struct hk_model hk_model;
+
+typedef struct hk_capabilities {
+    int32_t dtype;             /* HK_DTYPE_*                                         */
+    int32_t device;            /* CUDA device ordinal                                */
+    int32_t max_context;       /* longest accepted row (qwen3_5.rs:2700-2705)         */
+    int32_t max_rows;          /* HK_MAX_ROWS                                        */
+    int32_t hidden_size;
+    int32_t num_layers;
+    int32_t vocab_size;        /* input vocabulary: token ids must be below it       */
+    int32_t pointer_dim;       /* pointer-head width d_p (kev.rs:97, default 256)     */
+    float temperature;         /* the package's calibration temperature (kev.rs:86)  */
+    int32_t lora_rank;         /* 0 when no adapter was merged                       */
+} hk_capabilities;
+
+/*
+ * Load a Kev model directory onto `device`:
+ *   config.json, base *.safetensors (any of the HF text/conditional/PEFT name
+ *   prefixes), optional adapter_model.safetensors + adapter_config.json (merged
+ *   in fp32 as W += (alpha/r) B A), pointer_head.safetensors + kev_head.json.
+ * Replaces Qwen3_5Backend::load_kev_on_device (qwen3_5.rs:2086-2111 ->
+ * load_with_head 2185-2348).
+ */
+int hk_create(const char *model_dir, int device, int dtype, int max_context, hk_model **out);
+
+/* The same immutable weights on another GPU, with fresh mutable state.
+ * Replaces Backend::replica (backend.rs:217-222; qwen3_5.rs:2515-2535). */
+int hk_replica(const hk_model *src, int device, hk_model **out);
+
+/* Replaces Backend::capabilities (qwen3_5.rs:2541-2653). */
+int hk_capabilities_get(const hk_model *m, hk_capabilities *out);
+
+/*
+ * Score `n_rows` independent rows (a packed, unpadded batch).
+ *   tokens       [cu_seqlens[n_rows]]   row r is tokens[cu_seqlens[r] .. cu_seqlens[r+1])
+ *   cu_seqlens   [n_rows + 1]           cu_seqlens[0] == 0, non-decreasing
+ *   positions    [cu_positions[n_rows]] readout positions, relative to their row
+ *   cu_positions [n_rows + 1]
+ *   out_logits   [cu_positions[n_rows]] raw pointer logits, in input order
+ * The decision row of every row is its last token. Synchronous; all buffers
+ * are caller-owned host memory. Validation follows the reference: 1..=64
+ * rows, no empty row, every token below the vocabulary, every position inside
+ * its row, every row within max_context (qwen3_5.rs:2669-2705, 3143-3171).
+ * Replaces Backend::forward / forward_batch / forward_padded_batch
+ * (qwen3_5.rs:2655-2753, 2759-2761, 2806-2816 -> 3138-3194 + readout 3196-3255);
+ * right padding is not needed because rows are packed.
+ */
+int hk_score(hk_model *m, int n_rows, const uint32_t *tokens, const int32_t *cu_seqlens,
+             const int32_t *positions, const int32_t *cu_positions, float *out_logits);
+
+/*
+ * The same forward with device-resident inputs and output, enqueued on
+ * `stream` (a cudaStream_t; NULL = the handle's own stream) without a host
+ * synchronisation. Host copies of the two offset arrays are still needed to
+ * size the launches; they must equal the device copies. Device inputs are not
+ * validated (hk_score validates); use it for inputs already checked.
+ * No reference counterpart: it is hk_score minus the host<->device copies.
+ */
+int hk_score_device(hk_model *m, int n_rows, const int32_t *cu_seqlens_host,
+                    const int32_t *cu_positions_host, const uint32_t *d_tokens,
+                    const int32_t *d_cu_seqlens, const int32_t *d_positions,
+                    float *d_out_logits, void *stream);
+
+/* Block until the handle's queued work is done; report a device-side error flag. */
+int hk_synchronize(hk_model *m);
+
+/* Number of kernels this handle launched since creation (for launch accounting). */
+uint64_t hk_kernel_launches(const hk_model *m);
+
+/*
+ * Device-time profile of the forward's launches, by class: 0 projection GEMMs,
+ * 1 delta-rule recurrence, 2 attention, 3 delta input stage, 4 the rest.
+ * While enabled, each launch is bracketed by CUDA events on the handle's
+ * stream. hk_profile_read synchronises the stream, writes per-class summed
+ * milliseconds, algorithmic work (FLOPs) and launch counts for the first
+ * n_classes classes, and clears the record. No reference counterpart (the
+ * reference has no GPU profiler integration).
+ */
+int hk_profile_enable(hk_model *m, int enable);
+int hk_profile_read(hk_model *m, double *ms, double *work, int64_t *count, int n_classes);
+
+/* The last error message on this handle (never NULL). */
+const char *hk_last_error(const hk_model *m);
+
+/* The error message of the last failed hk_create / hk_replica on this thread. */
+const char *hk_create_error(void);
+
+void hk_destroy(hk_model *m);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HUNCHO_KEV_H */

@@ -1,0 +1,51 @@
+/*
+ * huncho_kev_ops.h -- kernel-level entry points of libhuncho_kev.so.
+ *
+ * Single kernels of the Kev forward over caller-owned DEVICE pointers,
+ * enqueued on `stream` (a cudaStream_t; NULL = legacy default stream). They
+ * exist so each kernel can be checked and timed in isolation; the model-level
+ * API is include/huncho_kev.h. Return HK_OK or a negative HK_ERR_* code;
+ * hk_op_last_error() holds the message of the calling thread's last failure.
+ */
+#ifndef HUNCHO_KEV_OPS_H
+#define HUNCHO_KEV_OPS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Y[M, N] (epilogue) X[M, K] W[N, K]^T. `dtype` 0: fp32 X/W (CUDA cores),
+ * 1: bf16 X/W (tcgen05 tensor cores). `epilogue` 0: store (bf16 for dtype 1),
+ * 1: fp32 residual add into out, 2: SwiGLU over 128-row gate/up blocks (bf16),
+ * 3: store fp32. `scale` (nullable) multiplies output column n by scale[n].
+ * Replaces one Linear::forward of the backbone (qwen3_5.rs:306-515). */
+int hk_op_gemm(int dtype, int epilogue, int M, int N, int K, const void *x, int ldx, const void *w,
+               int ldw, const float *scale, void *out, int ldo, void *stream);
+
+/* Per-token gated delta rule (qwen3_5.rs:950-987) over packed rows:
+ * q, k [n, nk, dk]; v [n, nv, dv]; g, beta [n, nv]; out [n, nv, dv]; fp32.
+ * `exact` = 1 keeps the reference's operation order (delta_cpu.rs:99-136). */
+int hk_op_delta_recurrent(const float *q, const float *k, const float *v, const float *g,
+                          const float *beta, const int32_t *cu_seqlens, int n_rows, int nk, int nv,
+                          int dk, int dv, int exact, float *out, void *stream);
+
+/* Causal GQA attention with the sigmoid output gate (qwen3_5.rs:669-714).
+ * act 0: fp32, 1: bf16. q [n, nh, hd]; k, v [n, nkv, hd]; gate read from
+ * proj[t, h*2*hd + hd + i] (row stride ldp); out [n, ldo]. tok_row[n] gives
+ * each token's row. */
+int hk_op_attention(int act, const void *q, const void *k, const void *v, const void *proj, int ldp,
+                    const int32_t *cu_seqlens, const int32_t *tok_row, int n, int n_rows, int max_len,
+                    int nh, int nkv, int hd, void *out, int ldo, void *stream);
+
+/* Number of SMs the GEMM grid is sized for on the current device. */
+int hk_op_num_sms(void);
+
+const char *hk_op_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HUNCHO_KEV_OPS_H */

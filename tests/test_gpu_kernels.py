@@ -1,0 +1,213 @@
+"""Per-kernel parity on the GPU, through the kernel-level C entry points.
+
+The tensor-core GEMM is checked against an fp32 PyTorch matmul of the same
+bf16 operands; the fp32 GEMM against an fp32 matmul with TF32 disabled; the
+delta-rule recurrence against the CPU oracle (bit-exact in its exact mode when
+the decay is exactly representable); attention against an fp32 PyTorch
+reference of qwen3_5.rs:669-714.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle import kev_oracle as ko
+
+
+@pytest.fixture(scope="module")
+def lib(native_lib):
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    torch.backends.cuda.matmul.allow_tf32 = False
+    return native_lib
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def gemm(lib, dtype, epi, x, w, out, scale=None):
+    M, K = x.shape
+    N = w.shape[0]
+    lib.hk_op_gemm.argtypes = [ctypes.c_int] * 5 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    rc = lib.hk_op_gemm(dtype, epi, M, N, K, _p(x), x.stride(0), _p(w), w.stride(0), _p(scale), _p(out),
+                        out.stride(0), None)
+    assert rc == 0, lib.hk_op_last_error()
+    torch.cuda.synchronize()
+
+
+SHAPES = [(1, 256, 64), (7, 32, 16), (130, 300, 1024), (257, 512, 72), (300, 8224, 1024), (1000, 1024, 2048),
+          (2048, 7168, 1024), (555, 1024, 3584)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_tc_gemm_store_bf16(lib, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    out = torch.zeros(M, N, device="cuda", dtype=torch.bfloat16)
+    gemm(lib, 1, 0, x, w, out)
+    ref = x.float() @ w.float().T
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_tc_gemm_residual_f32(lib, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M + N * 3)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    res = torch.randn(M, N, device="cuda", generator=g)
+    out = res.clone()
+    gemm(lib, 1, 1, x, w, out)
+    ref = res + x.float() @ w.float().T
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
+
+
+def test_tc_gemm_scale_and_f32_store(lib):
+    g = torch.Generator(device="cuda").manual_seed(5)
+    M, N, K = 300, 520, 256
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    wq = torch.randint(-127, 128, (N, K), device="cuda", generator=g).float().bfloat16()
+    scale = torch.rand(N, device="cuda", generator=g) * 1e-3
+    out = torch.zeros(M, N, device="cuda")
+    gemm(lib, 1, 3, x, wq, out, scale)
+    ref = (x.float() @ wq.float().T) * scale
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
+
+
+def test_tc_gemm_swiglu(lib):
+    g = torch.Generator(device="cuda").manual_seed(9)
+    M, F, K = 333, 512, 1024
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    gate = (torch.randn(F, K, device="cuda", generator=g) * 0.05).bfloat16()
+    up = (torch.randn(F, K, device="cuda", generator=g) * 0.05).bfloat16()
+    w = torch.cat([torch.cat([gate[b:b + 128], up[b:b + 128]]) for b in range(0, F, 128)])
+    out = torch.zeros(M, F, device="cuda", dtype=torch.bfloat16)
+    gemm(lib, 1, 2, x, w, out)
+    gf, uf = x.float() @ gate.float().T, x.float() @ up.float().T
+    ref = gf / (1 + torch.exp(-gf)) * uf
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+def test_tc_gemm_repeatable(lib):
+    """Same inputs, same bits (no nondeterministic reduction)."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn(777, 1024, device="cuda", generator=g).bfloat16()
+    w = torch.randn(2048, 1024, device="cuda", generator=g).bfloat16()
+    a = torch.zeros(777, 2048, device="cuda")
+    b = torch.zeros(777, 2048, device="cuda")
+    gemm(lib, 1, 3, x, w, a)
+    gemm(lib, 1, 3, x, w, b)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 5, 3), (70, 130, 16), (256, 1000, 1024)])
+def test_simt_gemm_f32(lib, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.05
+    out = torch.zeros(M, N, device="cuda")
+    gemm(lib, 0, 0, x, w, out)
+    torch.testing.assert_close(out, x @ w.T, rtol=1e-5, atol=1e-5)
+    res = torch.randn(M, N, device="cuda", generator=g)
+    out2 = res.clone()
+    gemm(lib, 0, 1, x, w, out2)
+    torch.testing.assert_close(out2, res + x @ w.T, rtol=1e-5, atol=1e-5)
+
+
+def _delta_inputs(rng, lens, nk, nv, dk, dv, zero_g=False):
+    n = sum(lens)
+    q = ko.l2norm(rng.standard_normal((n, nk, dk), dtype=np.float32)) * np.float32(dk ** -0.5)
+    k = ko.l2norm(rng.standard_normal((n, nk, dk), dtype=np.float32))
+    v = rng.standard_normal((n, nv, dv), dtype=np.float32)
+    g = np.zeros((n, nv), np.float32) if zero_g else -rng.random((n, nv), dtype=np.float32) * np.float32(0.5)
+    b = rng.random((n, nv), dtype=np.float32)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    return q.astype(np.float32), k.astype(np.float32), v, g, b, cu
+
+
+def _delta_oracle(q, k, v, g, b, cu, nk, nv):
+    rep = nv // nk
+    out = np.zeros_like(v)
+    for r in range(len(cu) - 1):
+        s, e = cu[r], cu[r + 1]
+        qq = np.repeat(q[s:e], rep, axis=1).transpose(1, 0, 2).copy()
+        kk = np.repeat(k[s:e], rep, axis=1).transpose(1, 0, 2).copy()
+        o, _ = ko.delta_recurrent(qq, kk, v[s:e].transpose(1, 0, 2).copy(), g[s:e].T.copy(), b[s:e].T.copy())
+        out[s:e] = o.transpose(1, 0, 2)
+    return out
+
+
+def _run_delta(lib, q, k, v, g, b, cu, nk, nv, exact):
+    t = [torch.from_numpy(a).cuda() for a in (q, k, v, g, b, cu)]
+    out = torch.zeros_like(t[2])
+    lib.hk_op_delta_recurrent.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int] * 6 + [ctypes.c_void_p] * 2
+    rc = lib.hk_op_delta_recurrent(*[_p(x) for x in t], len(cu) - 1, nk, nv, q.shape[2], v.shape[2], exact,
+                                   _p(out), None)
+    assert rc == 0, lib.hk_op_last_error()
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("exact", [1, 0])
+def test_delta_recurrence_vs_oracle(lib, exact):
+    rng = np.random.default_rng(1)
+    nk, nv, dk, dv = 16, 16, 128, 128
+    args = _delta_inputs(rng, [37, 1, 130], nk, nv, dk, dv)
+    got = _run_delta(lib, *args, nk, nv, exact)
+    ref = _delta_oracle(*args, nk, nv)
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_delta_recurrence_exact_order_bitwise(lib):
+    """With decay exp(0) = 1 the exact mode reproduces the reference loop bit for bit."""
+    rng = np.random.default_rng(2)
+    nk, nv, dk, dv = 2, 4, 32, 32
+    args = _delta_inputs(rng, [20, 9], nk, nv, dk, dv, zero_g=True)
+    got = _run_delta(lib, *args, nk, nv, 1)
+    ref = _delta_oracle(*args, nk, nv)
+    assert np.array_equal(got, ref)
+
+
+def _attn_ref(q, k, v, gate, lens, nh, nkv):
+    outs = []
+    s = 0
+    for L in lens:
+        qq = q[s:s + L].transpose(0, 1)
+        kk = k[s:s + L].transpose(0, 1).repeat_interleave(nh // nkv, 0)
+        vv = v[s:s + L].transpose(0, 1).repeat_interleave(nh // nkv, 0)
+        sc = qq @ kk.transpose(1, 2) / qq.shape[-1] ** 0.5
+        sc = sc + torch.triu(torch.full((L, L), float("-inf"), device=q.device), 1)
+        o = (torch.softmax(sc, -1) @ vv).transpose(0, 1)
+        outs.append(o * torch.sigmoid(gate[s:s + L]))
+        s += L
+    return torch.cat(outs).reshape(sum(lens), -1)
+
+
+@pytest.mark.parametrize("act,hd", [(0, 4), (0, 64), (1, 256)])
+def test_attention_vs_torch(lib, act, hd):
+    g = torch.Generator(device="cuda").manual_seed(hd)
+    nh, nkv = 8, 2
+    lens = [5, 70, 1, 33]
+    n = sum(lens)
+    dt = torch.float32 if act == 0 else torch.bfloat16
+    q = torch.randn(n, nh, hd, device="cuda", generator=g).to(dt)
+    k = torch.randn(n, nkv, hd, device="cuda", generator=g).to(dt)
+    v = torch.randn(n, nkv, hd, device="cuda", generator=g).to(dt)
+    proj = torch.randn(n, nh, 2 * hd, device="cuda", generator=g).to(dt)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device="cuda")
+    tok_row = torch.tensor(np.repeat(np.arange(len(lens)), lens), dtype=torch.int32, device="cuda")
+    out = torch.zeros(n, nh * hd, device="cuda", dtype=dt)
+    lib.hk_op_attention.argtypes = ([ctypes.c_int] + [ctypes.c_void_p] * 4 + [ctypes.c_int] + [ctypes.c_void_p] * 2
+                                    + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p])
+    rc = lib.hk_op_attention(act, _p(q), _p(k), _p(v), _p(proj), nh * 2 * hd, _p(cu), _p(tok_row), n, len(lens),
+                             max(lens), nh, nkv, hd, _p(out), nh * hd, None)
+    assert rc == 0, lib.hk_op_last_error()
+    torch.cuda.synchronize()
+    ref = _attn_ref(q.float(), k.float(), v.float(), proj.float()[:, :, hd:], lens, nh, nkv)
+    tol = 1e-5 if act == 0 else 2e-2
+    torch.testing.assert_close(out.float(), ref, rtol=tol, atol=tol)

@@ -1,0 +1,177 @@
+"""End-to-end parity of the B200 Kev forward through the C ABI.
+
+Gates:
+  * reference golden (tiny_kev, upstream PyTorch): fp32 raw logits < 2e-4 and
+    probabilities < 2e-5; bf16 probabilities < 2e-3 -- the gates of
+    crates/huncho-backend/tests/kev_reference.rs:64-76 (its half-precision
+    gate is 2e-3);
+  * the CPU oracle on seeded synthetic models: fp32 probabilities < 1e-4,
+    bf16 / int8-weight probabilities < 2e-3 against the fp32 oracle on the
+    same (dequantized) weights, and the same argmax on every row;
+  * batch invariants of crates/huncho-backend/tests/padded_batch.rs:25-83 and
+    native_batch.rs (batched == independent within 1e-4, same argmax).
+"""
+import json
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+from oracle import kev_oracle as ko
+from huncho_b200 import calibration, synth
+from huncho_b200.backend import pack_rows
+
+from conftest import GOLDEN
+
+
+def _gpu():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return json.loads((GOLDEN / "golden.json").read_text())
+
+
+def _backend(path, dtype, max_context=512):
+    _gpu()
+    from huncho_b200.backend import KevBackend
+    return KevBackend(path, device=0, dtype=dtype, max_context=max_context)
+
+
+@pytest.fixture(scope="module")
+def tiny_fp32(native_lib):
+    return _backend(GOLDEN, "fp32")
+
+
+@pytest.fixture(scope="module")
+def tiny_bf16(native_lib):
+    return _backend(GOLDEN, "bf16")
+
+
+def test_tiny_fp32_matches_upstream(tiny_fp32, golden):
+    from huncho_b200.backend import ForwardInput
+    b = tiny_fp32
+    assert b.capabilities().families == ["F2"]
+    assert abs(b.temperature - 2.40605) < 1e-5
+    for case in golden["cases"]:
+        for row in case["rows"]:
+            out = b.forward(ForwardInput(row["tokens"], row["positions"]))
+            assert out.values.shape == (len(row["positions"]), 1)
+            raw = out.values[:, 0]
+            assert np.abs(raw - np.array(row["raw_logits"], np.float32)).max() < 2e-4
+            p = calibration.calibrate(raw, b.temperature)
+            assert np.abs(p - np.array(row["probabilities"], np.float32)).max() < 2e-5
+    out = b.forward(ForwardInput([1, 2], [0]))
+    assert np.isfinite(out.values).all()
+    assert abs(out.values[0, 0] - golden["short_logits"][0]) < 2e-4
+
+
+def test_tiny_bf16_matches_upstream_at_half_precision_gate(tiny_bf16, golden):
+    from huncho_b200.backend import ForwardInput
+    for case in golden["cases"]:
+        for row in case["rows"]:
+            raw = tiny_bf16.forward(ForwardInput(row["tokens"], row["positions"])).values[:, 0]
+            p = calibration.calibrate(raw, tiny_bf16.temperature)
+            assert np.abs(p - np.array(row["probabilities"], np.float32)).max() < 2e-3
+
+
+def _padded_inputs():
+    from huncho_b200.backend import ForwardInput
+    return [ForwardInput([(i * 19 + row * 7 + 1) % 380 for i in range(n)], [n - 1, 1, n - 1])
+            for row, n in enumerate([5, 13, 47])]
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_padded_batch_invariants(native_lib, dtype):
+    """padded_batch.rs:25-83 on the B200 backend."""
+    from huncho_b200.backend import ForwardInput
+    from huncho_b200.errors import BackendError
+    b = _backend(GOLDEN, dtype)
+    inputs = _padded_inputs()
+    reference = [b.forward(i) for i in inputs]
+    padded = b.forward_padded_batch(inputs)
+    for a, r in zip(padded, reference):
+        assert a.positions == r.positions
+        pa = calibration.calibrate(a.values[:, 0], 2.40605)
+        pr = calibration.calibrate(r.values[:, 0], 2.40605)
+        assert calibration.argmax(pa.tolist()) == calibration.argmax(pr.tolist())
+        assert np.all(np.abs(pa - pr) <= 1e-4)
+    wrong = ForwardInput(list(inputs[0].tokens) + [0] * 42, inputs[0].positions)
+    w = b.forward(wrong)
+    assert np.any(np.abs(w.values - padded[0].values) > 1e-4), "must detect a padded decision row"
+    replica = b.replica()
+    replay = replica.forward_padded_batch(inputs)
+    assert all(np.array_equal(x.values, y.values) for x, y in zip(padded, replay))
+    with pytest.raises(BackendError):
+        b.forward_batch(inputs)  # unequal lengths
+    bad = list(inputs)
+    bad[0] = ForwardInput(inputs[0].tokens, [5])
+    with pytest.raises(BackendError):
+        b.forward_padded_batch(bad)
+    with pytest.raises(BackendError):
+        b.forward_padded_batch([ForwardInput([], [])])
+    with pytest.raises(BackendError):
+        b.forward_padded_batch([inputs[0]] * 65)
+    assert np.array_equal(reference[0].values, b.forward(inputs[0]).values)
+
+
+def test_forward_validation_errors(tiny_fp32):
+    from huncho_b200.backend import ForwardInput
+    from huncho_b200.errors import BackendError, UnsupportedError
+    b = tiny_fp32
+    with pytest.raises(BackendError):
+        b.forward(ForwardInput([1, 2, 384], [0]))  # token >= vocab
+    with pytest.raises(BackendError):
+        b.forward(ForwardInput([1, 2, 3], [3]))  # position outside
+    with pytest.raises(BackendError):
+        b.forward(ForwardInput(list(range(1, 300)) * 2, [0]))  # > max_context 512
+    with pytest.raises(UnsupportedError):
+        b.forward(ForwardInput([1, 2], [0], retain_cache=True))
+    assert b.forward(ForwardInput([1, 2, 3], [])).values.shape == (0, 1)
+    # The backend stays usable after errors.
+    assert np.isfinite(b.forward(ForwardInput([1, 2, 3], [0, 2])).values).all()
+
+
+def test_equal_length_batch_equals_independent(tiny_fp32):
+    from huncho_b200.backend import ForwardInput
+    rng = np.random.default_rng(0)
+    inputs = [ForwardInput(rng.integers(0, 384, 21).tolist(), [3, 9, 20]) for _ in range(64)]
+    batched = tiny_fp32.forward_batch(inputs)
+    for inp, out in zip(inputs[:8], batched[:8]):
+        single = tiny_fp32.forward(inp)
+        assert np.abs(single.values - out.values).max() <= 1e-6
+
+
+def _synth(synth_root, name, store):
+    return synth.write_model(synth_root / f"{name}-{store}", name=name, seed=0, store=store)
+
+
+@pytest.mark.parametrize("name,dtype,store,tol", [
+    ("kev-mini", "fp32", "fp32", 1e-4),
+    ("kev-mini", "bf16", "bf16", 2e-3),
+    ("kev-mini", "int8w", "bf16", 2e-3),
+    ("kev-0.8b-l4", "bf16", "bf16", 2e-3),
+    ("kev-0.8b-l4", "int8w", "bf16", 2e-3),
+])
+def test_synthetic_model_vs_oracle(native_lib, synth_root, name, dtype, store, tol):
+    d = _synth(synth_root, name, store)
+    b = _backend(d, dtype, max_context=4096)
+    m = ko.load_model(d, dtype)
+    vocab = m.cfg.vocab_size
+    wl = synth.make_workload(2, vocab, seed=1, n_requests=4)
+    rows, pos = wl.rows, wl.positions
+    got = b.score_packed(*pack_rows(rows, pos))
+    k = 0
+    worst = 0.0
+    for r, p in zip(rows, pos):
+        raw_ref = ko.score_row(m, r, p)
+        pr = ko.calibrate(raw_ref, m.temperature)
+        pg = calibration.calibrate(got[k:k + len(p)], m.temperature)
+        k += len(p)
+        worst = max(worst, float(np.abs(pr - pg).max()))
+        assert calibration.argmax(pg.tolist()) == calibration.argmax(pr.tolist()), (pr, pg)
+    assert worst < tol, worst
