@@ -17,7 +17,7 @@ HK_ERR_PACKAGE = -3
 HK_ERR_CUDA = -4
 HK_ERR_ARGUMENT = -5
 
-HK_DTYPE = {"fp32": 0, "bf16": 1, "int8w": 2}
+HK_DTYPE = {"fp32": 0, "bf16": 1, "int8w": 2, "fp16": 3}
 HK_MAX_ROWS = 64
 
 EXPORTED = (

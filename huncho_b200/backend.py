@@ -68,7 +68,7 @@ class KevBackend:
                  _handle=None):
         self._lib = _native.load()
         if dtype not in _native.HK_DTYPE:
-            raise UnsupportedError(f"Kev's B200 backend supports fp32, bf16 or int8w, not `{dtype}`")
+            raise UnsupportedError(f"Kev's B200 backend supports fp32, bf16, fp16 or int8w, not `{dtype}`")
         self.model_dir = str(model_dir)
         self.dtype = dtype
         self.device = device

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -44,7 +45,9 @@ __device__ __forceinline__ void set_error(uint32_t *err, uint32_t bit) {
     if (err) atomicOr(err, bit);
 }
 
-// Activation element types: float (fp32 model) or __nv_bfloat16 (bf16/int8w models).
+// Activation element types: float (fp32 model) or __half (the half-precision
+// models: tensor-core operands are fp16, the type the reference's CUDA path
+// runs half-precision checkpoints in).
 template <typename T> struct Act;
 template <> struct Act<float> {
     static __device__ __forceinline__ float load(const float *p) { return *p; }
@@ -54,11 +57,11 @@ template <> struct Act<float> {
     // model dtype between ops).
     static __device__ __forceinline__ float round(float v) { return v; }
 };
-template <> struct Act<__nv_bfloat16> {
-    static __device__ __forceinline__ float load(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
-    static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
-    static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
-    static __device__ __forceinline__ float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+template <> struct Act<__half> {
+    static __device__ __forceinline__ float load(const __half *p) { return __half2float(*p); }
+    static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+    static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+    static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }
 };
 
 __device__ __forceinline__ float warp_sum(float v) {

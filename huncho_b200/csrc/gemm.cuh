@@ -1,14 +1,14 @@
 // Projection GEMMs: Y = X W^T with the layer's epilogue fused.
 #pragma once
 
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace hk {
 
 enum GemmEpilogue : int {
-    kEpiStore = 0,   // out (activation type) [M, ldo] = acc * scale
+    kEpiStore = 0,   // out (fp16 on tensor cores, fp32 on CUDA cores) [M, ldo] = acc * scale
     kEpiResidual = 1,  // out fp32 [M, ldo] += acc * scale  (residual stream, in place)
     kEpiSwiGLU = 2,  // weight rows interleaved in blocks of kSwiGLUBlock (gate, up);
                      // out [M, ldo] = silu(gate) * up, N/2 columns
@@ -32,8 +32,8 @@ struct GemmArgs {
     uint32_t *err = nullptr;
 };
 
-// bf16 X and W on tcgen05 tensor cores (TMA-fed, TMEM accumulators).
-void gemm_bf16_tc(const GemmArgs &a, cudaStream_t s, int num_sms);
+// fp16 X and W on tcgen05 tensor cores (TMA-fed, TMEM accumulators), fp32 accumulation.
+void gemm_f16_tc(const GemmArgs &a, cudaStream_t s, int num_sms);
 // fp32 X and W on CUDA cores (the fp32 model path).
 void gemm_f32_simt(const GemmArgs &a, cudaStream_t s);
 

@@ -1,4 +1,4 @@
-// bf16 projection GEMM on the 5th-generation tensor cores (tcgen05), sm_100a.
+// fp16 projection GEMM on the 5th-generation tensor cores (tcgen05), sm_100a.
 //
 // Y[M, N] = X[M, K] * W[N, K]^T: X is the token-major activation matrix, W a
 // projection weight in its checkpoint layout ([out, in], K contiguous), so
@@ -44,14 +44,13 @@ struct TcParams {
     uint32_t *err;
 };
 
-__device__ __forceinline__ void store_bf16_32(__nv_bfloat16 *dst, const float (&v)[32], int valid,
-                                              bool vec) {
+__device__ __forceinline__ void store_half_32(__half *dst, const float (&v)[32], int valid, bool vec) {
     if (vec && valid >= 32) {
         uint4 pk[4];
         uint32_t *w = reinterpret_cast<uint32_t *>(pk);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
             w[i] = *reinterpret_cast<uint32_t *>(&h);
         }
         uint4 *d = reinterpret_cast<uint4 *>(dst);
@@ -60,13 +59,13 @@ __device__ __forceinline__ void store_bf16_32(__nv_bfloat16 *dst, const float (&
     } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-            if (i < valid) dst[i] = __float2bfloat16_rn(v[i]);
+            if (i < valid) dst[i] = __float2half_rn(v[i]);
     }
 }
 
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
+    gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                         const __grid_constant__ CUtensorMap tm_w, TcParams p) {
     using namespace sm100;
     extern __shared__ uint8_t smem_raw[];
@@ -146,7 +145,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ------------------------------------------------ MMA issuer
-            constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+            constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -170,7 +169,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint32_t b0 = smem_addr(sB + stage * B_STAGE_BYTES);
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
-                        mma_bf16(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32),
+                        mma_f16(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32),
                                  idesc, (kb | k) != 0);
                     }
                     mma_commit(&empty[stage]);
@@ -226,9 +225,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int i = 0; i < 32; ++i) g[i] = silu_f(g[i]) * u[i];
                     const int ocol = n_blk * (BN / 2) + c;
                     if (row_ok) {
-                        __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.out) +
-                                             static_cast<size_t>(row) * p.ldo + ocol;
-                        store_bf16_32(dst, g, p.N / 2 - ocol, p.vec_ok);
+                        __half *dst = reinterpret_cast<__half *>(p.out) + static_cast<size_t>(row) * p.ldo + ocol;
+                        store_half_32(dst, g, p.N / 2 - ocol, p.vec_ok);
                     }
                 }
             } else {
@@ -245,9 +243,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     if (!row_ok || valid <= 0) continue;
                     if (EPI == kEpiStore) {
-                        __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.out) +
-                                             static_cast<size_t>(row) * p.ldo + col;
-                        store_bf16_32(dst, v, valid, p.vec_ok);
+                        __half *dst = reinterpret_cast<__half *>(p.out) + static_cast<size_t>(row) * p.ldo + col;
+                        store_half_32(dst, v, valid, p.vec_ok);
                     } else {
                         float *dst = reinterpret_cast<float *>(p.out) + static_cast<size_t>(row) * p.ldo + col;
                         if (p.vec_ok && valid >= 32) {
@@ -310,7 +307,7 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// A 2-D bf16 tensor map over rows x inner (row stride ld elements) with a
+// A 2-D fp16 tensor map over rows x inner (row stride ld elements) with a
 // box of box_rows x 64 elements (128 bytes, one swizzle row) and zero fill.
 CUtensorMap make_map(const void *base, int rows, int inner, int ld, int box_rows) {
     if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16)
@@ -320,7 +317,7 @@ CUtensorMap make_map(const void *base, int rows, int inner, int ld, int box_rows
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
     cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
+    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
                              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -334,7 +331,7 @@ void launch(const GemmArgs &a, cudaStream_t s, int num_sms) {
     int dev = 0;
     HK_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(gemm_bf16_tc_kernel<EPI>,
+        HK_CUDA(cudaFuncSetAttribute(gemm_f16_tc_kernel<EPI>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
@@ -355,13 +352,13 @@ void launch(const GemmArgs &a, cudaStream_t s, int num_sms) {
     p.err = a.err;
     const int tiles = p.m_tiles * p.n_tiles;
     const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_bf16_tc_kernel<EPI><<<grid, THREADS, SMEM_BYTES, s>>>(tx, tw, p);
+    gemm_f16_tc_kernel<EPI><<<grid, THREADS, SMEM_BYTES, s>>>(tx, tw, p);
     HK_LAUNCH_CHECK();
 }
 
 }  // namespace
 
-void gemm_bf16_tc(const GemmArgs &a, cudaStream_t s, int num_sms) {
+void gemm_f16_tc(const GemmArgs &a, cudaStream_t s, int num_sms) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return;
     if (a.epilogue == kEpiSwiGLU && (a.N % BN) != 0)
         throw CudaError("fused SwiGLU GEMM needs N to be a multiple of 256");

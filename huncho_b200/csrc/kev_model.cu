@@ -146,6 +146,41 @@ float bf16_round(float f) {
     return r;
 }
 
+// IEEE binary16 with round-to-nearest-even (overflow to inf, subnormals kept).
+uint16_t f32_to_f16_bits(float f) {
+    uint32_t x;
+    std::memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t ax = x & 0x7FFFFFFFu;
+    if (ax >= 0x7F800000u) return static_cast<uint16_t>(sign | (ax > 0x7F800000u ? 0x7E00u : 0x7C00u));
+    if (ax >= 0x477FF000u) return static_cast<uint16_t>(sign | 0x7C00u);  // rounds to >= 65520
+    if (ax < 0x38800000u) {  // below 2^-14: subnormal (multiples of 2^-24) or zero
+        float v;
+        std::memcpy(&v, &ax, 4);
+        return static_cast<uint16_t>(sign | static_cast<uint32_t>(std::nearbyint(v * 16777216.0f)));
+    }
+    uint32_t h = (((ax >> 23) - 112u) << 10) | ((ax & 0x7FFFFFu) >> 13);
+    const uint32_t rem = ax & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;
+    return static_cast<uint16_t>(sign | h);
+}
+float f16_bits_to_f32(uint16_t h) {
+    const uint32_t sign = static_cast<uint32_t>(h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 0x1Fu, m = h & 0x3FFu, u;
+    if (e == 0) {
+        float v = static_cast<float>(m) * (1.0f / 16777216.0f);
+        std::memcpy(&u, &v, 4);
+        u |= sign;
+    } else if (e == 31) {
+        u = sign | 0x7F800000u | (m << 13);
+    } else {
+        u = sign | ((e + 112u) << 23) | (m << 13);
+    }
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+}
+
 // All base tensors of a model dir plus the adapter (merged on access).
 class WeightSource {
   public:
@@ -288,7 +323,8 @@ struct Model {
     int cap_tokens = 0, cap_rows = 0, cap_readouts = 0;
     std::vector<void *> ws;
     float *x = nullptr;
-    void *xn = nullptr, *proj = nullptr, *mix = nullptr, *ffn = nullptr;
+    void *xn = nullptr, *mix = nullptr, *ffn = nullptr;
+    float *proj = nullptr;  // projection outputs, always fp32
     float *dq = nullptr, *dkk = nullptr, *dvv = nullptr, *dg = nullptr, *db = nullptr, *dout = nullptr;
     void *aq = nullptr, *ak = nullptr, *av = nullptr;
     float *hn = nullptr, *rproj = nullptr, *logits = nullptr;
@@ -338,8 +374,15 @@ struct Model {
         prof_recs.push_back({a, b, cls, work});
     }
 
-    int act() const { return dtype == HK_DTYPE_FP32 ? kActF32 : kActBF16; }
+    int act() const { return dtype == HK_DTYPE_FP32 ? kActF32 : kActF16; }
     size_t esz() const { return dtype == HK_DTYPE_FP32 ? 4 : 2; }
+    // The checkpoint value in the model dtype (the reference casts every
+    // tensor to it at load): bf16 for the bf16 and int8-weight models.
+    float model_round(float v) const {
+        if (dtype == HK_DTYPE_BF16 || dtype == HK_DTYPE_INT8W) return bf16_round(v);
+        if (dtype == HK_DTYPE_FP16) return f16_bits_to_f32(f32_to_f16_bits(v));
+        return v;
+    }
 
     ~Model() {
         if (device >= 0) cudaSetDevice(device);
@@ -410,10 +453,11 @@ struct Model {
                     for (int i = 0; i < K; ++i) {
                         float q = std::nearbyint(row[i] / s);
                         q = std::min(127.0f, std::max(-127.0f, q));
-                        dst[i] = f32_to_bf16_bits(q);  // exact for |q| <= 127
+                        dst[i] = f32_to_f16_bits(q);  // exact for |q| <= 127
                     }
                 } else {
-                    for (int i = 0; i < K; ++i) dst[i] = f32_to_bf16_bits(row[i]);
+                    // bf16 checkpoint values convert to fp16 exactly unless |w| < 2^-17.
+                    for (int i = 0; i < K; ++i) dst[i] = f32_to_f16_bits(model_round(row[i]));
                 }
             }
             uint16_t *d = dev_alloc<uint16_t>(h.size(), allocs);
@@ -424,12 +468,11 @@ struct Model {
         return m;
     }
 
-    // A small fp32 tensor, rounded to bf16 first in the bf16 / int8w models
-    // (the reference loader casts every tensor to the model dtype).
+    // A small fp32 tensor, rounded to the model dtype first (the reference
+    // loader casts every tensor to it) and kept in fp32 on the device.
     std::vector<float> small(const WeightSource &src, const std::string &k, std::vector<int64_t> shape) {
         std::vector<float> v = src.get(k, shape);
-        if (dtype != HK_DTYPE_FP32)
-            for (auto &x : v) x = bf16_round(x);
+        for (auto &x : v) x = model_round(x);
         return v;
     }
     float *norm_eff(const WeightSource &src, const std::string &k, int n) {
@@ -486,7 +529,7 @@ struct Model {
                 embed = d;
             } else {
                 std::vector<uint16_t> h(e.size());
-                for (size_t i = 0; i < e.size(); ++i) h[i] = f32_to_bf16_bits(e[i]);
+                for (size_t i = 0; i < e.size(); ++i) h[i] = f32_to_f16_bits(model_round(e[i]));
                 uint16_t *d = dev_alloc<uint16_t>(h.size(), allocs);
                 HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
                 embed = d;
@@ -564,7 +607,7 @@ struct Model {
         const size_t N = cap_tokens, R = cap_readouts + cap_rows, e = esz();
         x = dev_alloc<float>(N * c.hidden, ws);
         xn = dev_alloc<uint8_t>(N * ld_xn * e, ws);
-        proj = dev_alloc<uint8_t>(N * ldp * e, ws);
+        proj = dev_alloc<float>(N * ldp, ws);
         mix = dev_alloc<uint8_t>(N * ldmix * e, ws);
         ffn = dev_alloc<uint8_t>(N * ldf * e, ws);
         HK_CUDA(cudaMemset(xn, 0, N * ld_xn * e));
@@ -604,7 +647,7 @@ struct Model {
         if (dtype == HK_DTYPE_FP32)
             gemm_f32_simt(a, stream);
         else
-            gemm_bf16_tc(a, stream, num_sms);
+            gemm_f16_tc(a, stream, num_sms);
         prof_end(ev, 0, 2.0 * M * W.rows * W.cols);
     }
 
@@ -623,7 +666,7 @@ struct Model {
             ev = prof_begin();
             launch_rmsnorm(A, x, c.hidden, L.in_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream);
             prof_end(ev, 4, 0);
-            gemm(L.mix_in, xn, ld_xn, n_tok, proj, ldp, kEpiStore);
+            gemm(L.mix_in, xn, ld_xn, n_tok, proj, ldp, kEpiStoreF32);
             if (!L.full) {
                 DeltaPrepArgs d;
                 d.proj = proj;
@@ -644,7 +687,7 @@ struct Model {
                 d.g = dg;
                 d.beta = db;
                 ev = prof_begin();
-                launch_delta_prep(A, d, stream);
+                launch_delta_prep(d, stream);
                 prof_end(ev, 3, 0);
                 DeltaRecArgs r;
                 r.q = dq;
@@ -664,8 +707,8 @@ struct Model {
                 launch_delta_recurrent(r, stream);
                 prof_end(ev, 1, 4.0 * n_tok * c.nv * c.dk * c.dv);
                 ev = prof_begin();
-                launch_gated_norm(A, dout, static_cast<uint8_t *>(proj) + static_cast<size_t>(c.conv_dim()) * e, ldp,
-                                  L.gnorm_w, c.eps, n_tok, c.nv, c.dv, mix, ldmix, stream);
+                launch_gated_norm(A, dout, proj + c.conv_dim(), ldp, L.gnorm_w, c.eps, n_tok, c.nv, c.dv, mix, ldmix,
+                                  stream);
                 prof_end(ev, 4, 0);
             } else {
                 AttnPrepArgs p;
@@ -714,7 +757,7 @@ struct Model {
             if (fused_swiglu) {
                 gemm(L.gu, xn, ld_xn, n_tok, ffn, ldf, kEpiSwiGLU);
             } else {
-                gemm(L.gu, xn, ld_xn, n_tok, proj, ldp, kEpiStore);
+                gemm(L.gu, xn, ld_xn, n_tok, proj, ldp, kEpiStoreF32);
                 ev = prof_begin();
                 launch_swiglu(A, proj, ldp, n_tok, c.ffn, ffn, ldf, stream);
                 prof_end(ev, 4, 0);
@@ -834,7 +877,7 @@ int guarded(hk_model *h, F &&f) {
 
 int create_impl(const std::string &dir, int device, int dtype, int max_context, hk_model **out) {
     *out = nullptr;
-    if (dtype != HK_DTYPE_FP32 && dtype != HK_DTYPE_BF16 && dtype != HK_DTYPE_INT8W) {
+    if (dtype != HK_DTYPE_FP32 && dtype != HK_DTYPE_BF16 && dtype != HK_DTYPE_INT8W && dtype != HK_DTYPE_FP16) {
         tl_create_error = "unsupported dtype";
         return HK_ERR_UNSUPPORTED;
     }

@@ -1,8 +1,10 @@
 // Bandwidth-bound layer kernels of the Kev forward: embedding gather, RMSNorm,
 // the Gated DeltaNet input stage and recurrence, gated RMSNorm, the attention
-// input stage, SwiGLU and the pointer readout. All compute in fp32 and store
-// the activation type (float or bf16); one warp or one CTA per token row, so
-// loads of a row are contiguous and coalesced.
+// input stage, SwiGLU and the pointer readout. All compute in fp32; projection
+// outputs are read as fp32, and only tensors that feed a tensor-core GEMM or
+// attention are stored in the activation type (float, or fp16 for the
+// half-precision models). One warp or one CTA per token row, so the loads of a
+// row are contiguous and coalesced.
 #include <math.h>
 
 #include "common.cuh"
@@ -49,25 +51,25 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, int ldx, const float
 // ------------------------------------------------------------------ delta prep
 // One CTA per token. Stage 1: conv + SiLU of every q|k|v channel (fp32, taps in
 // ascending order from a zero accumulator, no fused multiply-add, matching
-// conv_cpu.rs:38-49), rounded to the activation type (qwen3_5.rs:843).
-// Stage 2: per key head L2 norm of q and k; v widened. Stage 3: beta and g.
-template <typename T>
+// conv_cpu.rs:38-49). Stage 2: per key head L2 norm of q and k. Stage 3: beta
+// and g. Everything stays fp32 (the half-precision reference path rounds the
+// conv output to the model dtype, qwen3_5.rs:843; this path keeps fp32).
 __global__ void delta_prep_kernel(DeltaPrepArgs a) {
     extern __shared__ float conv_s[];  // [conv_dim]
     const int t = blockIdx.x;
     const int key_dim = a.nk * a.dk, value_dim = a.nv * a.dv;
     const int conv_dim = 2 * key_dim + value_dim;
     const int pos = a.pos[t];
-    const T *proj = static_cast<const T *>(a.proj);
+    const float *proj = a.proj;
     for (int c = threadIdx.x; c < conv_dim; c += blockDim.x) {
         float acc = 0.f;
         for (int tap = 0; tap < a.taps; ++tap) {
             const int shift = a.taps - 1 - tap;
             if (shift > pos) continue;
-            const float xv = Act<T>::to_f(proj[static_cast<size_t>(t - shift) * a.ldp + c]);
+            const float xv = proj[static_cast<size_t>(t - shift) * a.ldp + c];
             acc = __fadd_rn(acc, __fmul_rn(a.conv_w[c * a.taps + tap], xv));
         }
-        conv_s[c] = Act<T>::round(silu_f(acc));
+        conv_s[c] = silu_f(acc);
     }
     __syncthreads();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31, nwarps = blockDim.x / 32;
@@ -86,9 +88,9 @@ __global__ void delta_prep_kernel(DeltaPrepArgs a) {
     for (int i = threadIdx.x; i < value_dim; i += blockDim.x)
         a.v[static_cast<size_t>(t) * value_dim + i] = conv_s[2 * key_dim + i];
     for (int h = threadIdx.x; h < a.nv; h += blockDim.x) {
-        const float b = Act<T>::to_f(proj[static_cast<size_t>(t) * a.ldp + conv_dim + value_dim + h]);
-        const float av = Act<T>::to_f(proj[static_cast<size_t>(t) * a.ldp + conv_dim + value_dim + a.nv + h]);
-        a.beta[static_cast<size_t>(t) * a.nv + h] = Act<T>::round(sigmoid_f(b));
+        const float b = proj[static_cast<size_t>(t) * a.ldp + conv_dim + value_dim + h];
+        const float av = proj[static_cast<size_t>(t) * a.ldp + conv_dim + value_dim + a.nv + h];
+        a.beta[static_cast<size_t>(t) * a.nv + h] = sigmoid_f(b);
         const float sp = logf(expf(av + a.dt_bias[h]) + 1.0f);
         a.g[static_cast<size_t>(t) * a.nv + h] = a.base_g[h] * sp;
     }
@@ -161,7 +163,7 @@ __global__ void __launch_bounds__(128) delta_recurrent_kernel(DeltaRecArgs a) {
 
 // ------------------------------------------------------------------ gated norm
 template <typename T>
-__global__ void gated_norm_kernel(const float *__restrict__ o, const T *__restrict__ z, int ldz,
+__global__ void gated_norm_kernel(const float *__restrict__ o, const float *__restrict__ z, int ldz,
                                   const float *__restrict__ w, float eps, int n, int nv, int dv,
                                   T *__restrict__ out, int ldo) {
     const int item = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
@@ -170,18 +172,12 @@ __global__ void gated_norm_kernel(const float *__restrict__ o, const T *__restri
     const int t = item / nv, h = item % nv;
     const float *src = o + static_cast<size_t>(item) * dv;
     float ss = 0.f;
-    for (int i = lane; i < dv; i += 32) {
-        const float v = Act<T>::round(src[i]);
-        ss += v * v;
-    }
+    for (int i = lane; i < dv; i += 32) ss += src[i] * src[i];
     ss = warp_sum(ss);
     const float denom = sqrtf(ss / static_cast<float>(dv) + eps);
-    const T *zr = z + static_cast<size_t>(t) * ldz + h * dv;
+    const float *zr = z + static_cast<size_t>(t) * ldz + h * dv;
     T *dst = out + static_cast<size_t>(t) * ldo + h * dv;
-    for (int i = lane; i < dv; i += 32) {
-        const float v = Act<T>::round(src[i]);
-        dst[i] = Act<T>::from_f(((v / denom) * w[i]) * silu_f(Act<T>::to_f(zr[i])));
-    }
+    for (int i = lane; i < dv; i += 32) dst[i] = Act<T>::from_f(((src[i] / denom) * w[i]) * silu_f(zr[i]));
 }
 
 // ------------------------------------------------------------------ attention prep
@@ -197,28 +193,24 @@ __global__ void attn_prep_kernel(AttnPrepArgs a) {
     const int item = blockIdx.x * warps + wid;
     if (item >= a.n * slots) return;
     const int t = item / slots, slot = item % slots;
-    const T *proj = static_cast<const T *>(a.proj) + static_cast<size_t>(t) * a.ldp;
+    const float *proj = a.proj + static_cast<size_t>(t) * a.ldp;
     float *buf = rowbuf + wid * a.hd;
-    if (slot >= a.nh + a.nkv) {  // value head: copy
+    if (slot >= a.nh + a.nkv) {  // value head: convert
         const int h = slot - a.nh - a.nkv;
-        const T *src = proj + a.nh * 2 * a.hd + a.nkv * a.hd + h * a.hd;
+        const float *src = proj + a.nh * 2 * a.hd + a.nkv * a.hd + h * a.hd;
         T *dst = static_cast<T *>(a.v) + (static_cast<size_t>(t) * a.nkv + h) * a.hd;
-        for (int i = lane; i < a.hd; i += 32) dst[i] = src[i];
+        for (int i = lane; i < a.hd; i += 32) dst[i] = Act<T>::from_f(src[i]);
         return;
     }
     const bool is_q = slot < a.nh;
     const int h = is_q ? slot : slot - a.nh;
-    const T *src = is_q ? proj + h * 2 * a.hd : proj + a.nh * 2 * a.hd + h * a.hd;
+    const float *src = is_q ? proj + h * 2 * a.hd : proj + a.nh * 2 * a.hd + h * a.hd;
     const float *w = is_q ? a.qn_w : a.kn_w;
     float ss = 0.f;
-    for (int i = lane; i < a.hd; i += 32) {
-        const float v = Act<T>::to_f(src[i]);
-        ss += v * v;
-    }
+    for (int i = lane; i < a.hd; i += 32) ss += src[i] * src[i];
     ss = warp_sum(ss);
     const float denom = sqrtf(ss / static_cast<float>(a.hd) + a.eps);
-    for (int i = lane; i < a.hd; i += 32)
-        buf[i] = Act<T>::round((Act<T>::to_f(src[i]) / denom) * w[i]);
+    for (int i = lane; i < a.hd; i += 32) buf[i] = (src[i] / denom) * w[i];
     __syncwarp();
     const float p = static_cast<float>(a.pos[t]);
     const int half = a.rd / 2;
@@ -283,30 +275,24 @@ __global__ void attn_simt_kernel(AttnArgs a) {
         }
         m = mn;
     }
-    const T *gate = static_cast<const T *>(a.proj) + static_cast<size_t>(t) * a.ldp + h * 2 * a.hd + a.hd;
+    const float *gate = a.proj + static_cast<size_t>(t) * a.ldp + h * 2 * a.hd + a.hd;
     T *dst = static_cast<T *>(a.out) + static_cast<size_t>(t) * a.ldo + h * a.hd;
 #pragma unroll
     for (int e = 0; e < MAXE; ++e) {
         const int i = lane + 32 * e;
-        if (i < a.hd) {
-            const float o = Act<T>::round(acc[e] / l);
-            const float gt = Act<T>::round(sigmoid_f(Act<T>::to_f(gate[i])));
-            dst[i] = Act<T>::from_f(o * gt);
-        }
+        if (i < a.hd) dst[i] = Act<T>::from_f((acc[e] / l) * sigmoid_f(gate[i]));
     }
 }
 
 // ------------------------------------------------------------------ swiglu
 template <typename T>
-__global__ void swiglu_kernel(const T *__restrict__ gu, int ldg, int n, int f, T *__restrict__ out,
+__global__ void swiglu_kernel(const float *__restrict__ gu, int ldg, int n, int f, T *__restrict__ out,
                               int ldo) {
     const size_t total = static_cast<size_t>(n) * f;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const size_t t = i / f, j = i % f;
-        const float g = Act<T>::to_f(gu[t * ldg + j]);
-        const float u = Act<T>::to_f(gu[t * ldg + f + j]);
-        out[t * ldo + j] = Act<T>::from_f(Act<T>::round(silu_f(g)) * u);
+        out[t * ldo + j] = Act<T>::from_f(silu_f(gu[t * ldg + j]) * gu[t * ldg + f + j]);
     }
 }
 
@@ -365,8 +351,7 @@ void launch_embed(int act, const uint32_t *ids, int n, const void *table, int hi
     if (act == kActF32)
         embed_kernel<float><<<n, 256, 0, s>>>(ids, n, static_cast<const float *>(table), hidden, x);
     else
-        embed_kernel<__nv_bfloat16><<<n, 256, 0, s>>>(ids, n, static_cast<const __nv_bfloat16 *>(table),
-                                                       hidden, x);
+        embed_kernel<__half><<<n, 256, 0, s>>>(ids, n, static_cast<const __half *>(table), hidden, x);
     HK_LAUNCH_CHECK();
 }
 
@@ -377,23 +362,17 @@ void launch_rmsnorm(int act, const float *x, int ldx, const float *w_eff, float 
     if (act == kActF32)
         rmsnorm_kernel<float><<<grid, 256, 0, s>>>(x, ldx, w_eff, eps, rows, hidden, static_cast<float *>(out), ldo);
     else
-        rmsnorm_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(x, ldx, w_eff, eps, rows, hidden,
-                                                           static_cast<__nv_bfloat16 *>(out), ldo);
+        rmsnorm_kernel<__half><<<grid, 256, 0, s>>>(x, ldx, w_eff, eps, rows, hidden, static_cast<__half *>(out),
+                                                    ldo);
     HK_LAUNCH_CHECK();
 }
 
-void launch_delta_prep(int act, const DeltaPrepArgs &a, cudaStream_t s) {
+void launch_delta_prep(const DeltaPrepArgs &a, cudaStream_t s) {
     if (a.n <= 0) return;
     const size_t smem = sizeof(float) * (2 * a.nk * a.dk + a.nv * a.dv);
-    if (act == kActF32) {
-        HK_CUDA(cudaFuncSetAttribute(delta_prep_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(smem)));
-        delta_prep_kernel<float><<<a.n, 256, smem, s>>>(a);
-    } else {
-        HK_CUDA(cudaFuncSetAttribute(delta_prep_kernel<__nv_bfloat16>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-        delta_prep_kernel<__nv_bfloat16><<<a.n, 256, smem, s>>>(a);
-    }
+    HK_CUDA(cudaFuncSetAttribute(delta_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem)));
+    delta_prep_kernel<<<a.n, 256, smem, s>>>(a);
     HK_LAUNCH_CHECK();
 }
 
@@ -422,17 +401,14 @@ void launch_delta_recurrent(const DeltaRecArgs &a, cudaStream_t s) {
     HK_LAUNCH_CHECK();
 }
 
-void launch_gated_norm(int act, const float *o, const void *z, int ldz, const float *w, float eps,
+void launch_gated_norm(int act, const float *o, const float *z, int ldz, const float *w, float eps,
                        int n, int nv, int dv, void *out, int ldo, cudaStream_t s) {
     if (n <= 0) return;
     const int grid = ceil_div(static_cast<long>(n) * nv, 8);
     if (act == kActF32)
-        gated_norm_kernel<float><<<grid, 256, 0, s>>>(o, static_cast<const float *>(z), ldz, w, eps, n, nv, dv,
-                                                      static_cast<float *>(out), ldo);
+        gated_norm_kernel<float><<<grid, 256, 0, s>>>(o, z, ldz, w, eps, n, nv, dv, static_cast<float *>(out), ldo);
     else
-        gated_norm_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(o, static_cast<const __nv_bfloat16 *>(z), ldz, w,
-                                                              eps, n, nv, dv,
-                                                              static_cast<__nv_bfloat16 *>(out), ldo);
+        gated_norm_kernel<__half><<<grid, 256, 0, s>>>(o, z, ldz, w, eps, n, nv, dv, static_cast<__half *>(out), ldo);
     HK_LAUNCH_CHECK();
 }
 
@@ -444,7 +420,7 @@ void launch_attn_prep(int act, const AttnPrepArgs &a, cudaStream_t s) {
     if (act == kActF32)
         attn_prep_kernel<float><<<grid, 256, smem, s>>>(a);
     else
-        attn_prep_kernel<__nv_bfloat16><<<grid, 256, smem, s>>>(a);
+        attn_prep_kernel<__half><<<grid, 256, smem, s>>>(a);
     HK_LAUNCH_CHECK();
 }
 
@@ -455,20 +431,18 @@ void launch_attention(int act, const AttnArgs &a, cudaStream_t s) {
     if (act == kActF32)
         attn_simt_kernel<float><<<grid, 256, 0, s>>>(a);
     else
-        attn_simt_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
+        attn_simt_kernel<__half><<<grid, 256, 0, s>>>(a);
     HK_LAUNCH_CHECK();
 }
 
-void launch_swiglu(int act, const void *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s) {
+void launch_swiglu(int act, const float *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s) {
     if (n <= 0) return;
     const long total = static_cast<long>(n) * f;
     const int grid = static_cast<int>(total / 256 + 1 < 148 * 16 ? total / 256 + 1 : 148 * 16);
     if (act == kActF32)
-        swiglu_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float *>(gu), ldg, n, f,
-                                                   static_cast<float *>(out), ldo);
+        swiglu_kernel<float><<<grid, 256, 0, s>>>(gu, ldg, n, f, static_cast<float *>(out), ldo);
     else
-        swiglu_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(gu), ldg, n, f,
-                                                           static_cast<__nv_bfloat16 *>(out), ldo);
+        swiglu_kernel<__half><<<grid, 256, 0, s>>>(gu, ldg, n, f, static_cast<__half *>(out), ldo);
     HK_LAUNCH_CHECK();
 }
 

@@ -1,17 +1,19 @@
 // Host launchers for the bandwidth-bound Kev layer kernels.
 #pragma once
 
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace hk {
 
 // Activation type selector for the launchers: the fp32 model runs float
-// activations, the bf16 and int8-weight models bf16.
-enum ActType : int { kActF32 = 0, kActBF16 = 1 };
+// activations; the half-precision models (bf16 / fp16 / int8-weight
+// checkpoints) run fp16 tensor-core operands.
+enum ActType : int { kActF32 = 0, kActF16 = 1 };
 
 // x[t, :] = table[ids[t], :] widened to fp32 (qwen3_5.rs:1319-1323, 1537).
+// The table is float (act 0) or fp16 (act 1).
 void launch_embed(int act, const uint32_t *ids, int n, const void *table, int hidden, float *x,
                   cudaStream_t s);
 
@@ -24,7 +26,7 @@ void launch_rmsnorm(int act, const float *x, int ldx, const float *w_eff, float 
 // q|k|v channels of proj, L2 norm of q and k per key head (q also scaled by
 // 1/sqrt(dk)), beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias).
 struct DeltaPrepArgs {
-    const void *proj;  // [n, ldp]: qkv (conv_dim) | z (vd) | b (nv) | a (nv)
+    const float *proj;  // [n, ldp] fp32: qkv (conv_dim) | z (vd) | b (nv) | a (nv)
     int ldp;
     const int32_t *pos;  // position of each token inside its row
     int n;
@@ -37,7 +39,7 @@ struct DeltaPrepArgs {
     float *v;      // [n, nv, dv] fp32
     float *g, *beta;  // [n, nv] fp32
 };
-void launch_delta_prep(int act, const DeltaPrepArgs &a, cudaStream_t s);
+void launch_delta_prep(const DeltaPrepArgs &a, cudaStream_t s);
 
 // Per-token gated delta rule with an fp32 state per (row, value head)
 // (qwen3_5.rs:950-987). `exact` keeps the reference's ascending-key fp32
@@ -51,16 +53,16 @@ struct DeltaRecArgs {
 };
 void launch_delta_recurrent(const DeltaRecArgs &a, cudaStream_t s);
 
-// out[t, h*dv + j] = rms(o)[j] * w[j] * silu(z[t, h, j]) after rounding o to
-// the activation type (qwen3_5.rs:193-201, 934-938).
-void launch_gated_norm(int act, const float *o, const void *z, int ldz, const float *w, float eps,
+// out[t, h*dv + j] = rms(o)[j] * w[j] * silu(z[t, h, j]) (qwen3_5.rs:193-201,
+// 934-938); o and z fp32, out in the activation type (the out_proj input).
+void launch_gated_norm(int act, const float *o, const float *z, int ldz, const float *w, float eps,
                        int n, int nv, int dv, void *out, int ldo, cudaStream_t s);
 
 // Full-attention input stage (qwen3_5.rs:596-615): split q | gate per head,
 // q_norm / k_norm (zero-centred weights, fp32), partial RoPE on the first
 // rotary_dim dims at each token's in-row position.
 struct AttnPrepArgs {
-    const void *proj;  // [n, ldp]: per q head [q(hd) | gate(hd)], then k (nkv*hd), v (nkv*hd)
+    const float *proj;  // [n, ldp] fp32: per q head [q(hd) | gate(hd)], then k (nkv*hd), v (nkv*hd)
     int ldp;
     const int32_t *pos;
     int n, nh, nkv, hd, rd;
@@ -75,7 +77,7 @@ void launch_attn_prep(int act, const AttnPrepArgs &a, cudaStream_t s);
 // multiplied by sigmoid(gate) and written token-major [n, nh*hd].
 struct AttnArgs {
     const void *q, *k, *v;  // [n, nh, hd], [n, nkv, hd], [n, nkv, hd]
-    const void *proj;       // gate source: proj[t, h*2*hd + hd + i]
+    const float *proj;      // gate source (fp32): proj[t, h*2*hd + hd + i]
     int ldp;
     const int32_t *cu_seqlens;
     const int32_t *tok_row;  // row of each token
@@ -85,8 +87,8 @@ struct AttnArgs {
 };
 void launch_attention(int act, const AttnArgs &a, cudaStream_t s);
 
-// out[t, j] = silu(gu[t, j]) * gu[t, F + j] (qwen3_5.rs:1020-1031).
-void launch_swiglu(int act, const void *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s);
+// out[t, j] = silu(gu[t, j]) * gu[t, F + j] (qwen3_5.rs:1020-1031); gu fp32.
+void launch_swiglu(int act, const float *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s);
 
 // Pointer readout (qwen3_5.rs:3196-3255, kev.rs:169-173). idx lists the token
 // rows to read: first the n_dec decision rows, then the n_opt option rows.

@@ -53,9 +53,9 @@ int hk_op_gemm(int dtype, int epilogue, int M, int N, int K, const void *x, int 
         if (dtype == 0)
             hk::gemm_f32_simt(a, s);
         else if (dtype == 1)
-            hk::gemm_bf16_tc(a, s, current_sms());
+            hk::gemm_f16_tc(a, s, current_sms());
         else
-            throw std::runtime_error("hk_op_gemm: dtype must be 0 (fp32) or 1 (bf16)");
+            throw std::runtime_error("hk_op_gemm: dtype must be 0 (fp32) or 1 (fp16)");
     });
 }
 
@@ -81,7 +81,7 @@ int hk_op_delta_recurrent(const float *q, const float *k, const float *v, const 
     });
 }
 
-int hk_op_attention(int act, const void *q, const void *k, const void *v, const void *proj, int ldp,
+int hk_op_attention(int act, const void *q, const void *k, const void *v, const float *proj, int ldp,
                     const int32_t *cu_seqlens, const int32_t *tok_row, int n, int n_rows, int max_len, int nh,
                     int nkv, int hd, void *out, int ldo, void *stream) {
     return op_guard([&] {

@@ -115,16 +115,15 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor for kind::f16 with bf16 A/B, fp32 accumulation,
-// both operands K-major: D format bits 4-5, A/B format bits 7-9 / 10-12,
-// N>>3 in bits 17-22, M>>4 in bits 24-28.
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
-           (static_cast<uint32_t>(M >> 4) << 24);
+// Instruction descriptor for kind::f16 with fp16 A/B (format 0 in bits 7-9 and
+// 10-12; both operands always the same type), fp32 accumulation (D format 1
+// in bits 4-5), both operands K-major, N>>3 in bits 17-22, M>>4 in bits 24-28.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+    return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n.reg .pred p;\n"

@@ -34,12 +34,22 @@ extern "C" {
 #define HK_ERR_CUDA (-4)        /* Error::Backend raised by a CUDA failure             */
 #define HK_ERR_ARGUMENT (-5)    /* null pointer or bad enum at the C boundary          */
 
-/* Model dtypes. HK_FP32 and HK_BF16 are the weight and activation types;
- * HK_INT8W is int8 per-output-channel symmetric projection weights
- * (scale = max|w| / 127, fp32 scales) with bf16 activations. */
+/* Model dtypes: the type every checkpoint tensor is cast to at load, as the
+ * reference's `dtype` argument (qwen3_5.rs:2202-2210).
+ *   HK_DTYPE_FP32   fp32 weights and activations (CUDA-core GEMMs).
+ *   HK_DTYPE_BF16   bf16 weights; tensor-core operands run as fp16, into which
+ *                   bf16 values convert exactly (|w| >= 2^-17), the way the
+ *                   reference runs bf16 checkpoints as fp16 on CUDA.
+ *   HK_DTYPE_INT8W  int8 per-output-channel symmetric projection weights
+ *                   (scale = max|w| / 127, fp32 scales, applied in the GEMM
+ *                   epilogue); other tensors as HK_DTYPE_BF16.
+ *   HK_DTYPE_FP16   fp16 weights and tensor-core operands.
+ * In the half-precision models the residual stream, projection outputs and
+ * all elementwise math stay fp32; only tensor-core operands are fp16. */
 #define HK_DTYPE_FP32 0
 #define HK_DTYPE_BF16 1
 #define HK_DTYPE_INT8W 2
+#define HK_DTYPE_FP16 3
 
 /* The reference's hard limit on independent rows per native batch
  * (qwen3_5.rs:3143-3148; BatchLimits default, backend.rs:108-121). */

@@ -17,9 +17,9 @@ extern "C" {
 #endif
 
 /* Y[M, N] (epilogue) X[M, K] W[N, K]^T. `dtype` 0: fp32 X/W (CUDA cores),
- * 1: bf16 X/W (tcgen05 tensor cores). `epilogue` 0: store (bf16 for dtype 1),
- * 1: fp32 residual add into out, 2: SwiGLU over 128-row gate/up blocks (bf16),
- * 3: store fp32. `scale` (nullable) multiplies output column n by scale[n].
+ * 1: fp16 X/W (tcgen05 tensor cores, fp32 accumulation). `epilogue` 0: store
+ * (fp16 for dtype 1), 1: fp32 residual add into out, 2: SwiGLU over 128-row
+ * gate/up blocks (fp16), 3: store fp32. `scale` (nullable) multiplies output column n by scale[n].
  * Replaces one Linear::forward of the backbone (qwen3_5.rs:306-515). */
 int hk_op_gemm(int dtype, int epilogue, int M, int N, int K, const void *x, int ldx, const void *w,
                int ldw, const float *scale, void *out, int ldo, void *stream);
@@ -32,10 +32,11 @@ int hk_op_delta_recurrent(const float *q, const float *k, const float *v, const 
                           int dk, int dv, int exact, float *out, void *stream);
 
 /* Causal GQA attention with the sigmoid output gate (qwen3_5.rs:669-714).
- * act 0: fp32, 1: bf16. q [n, nh, hd]; k, v [n, nkv, hd]; gate read from
- * proj[t, h*2*hd + hd + i] (row stride ldp); out [n, ldo]. tok_row[n] gives
+ * act 0: fp32, 1: fp16. q [n, nh, hd]; k, v [n, nkv, hd] (act type); gate read
+ * from the fp32 proj[t, h*2*hd + hd + i] (row stride ldp); out [n, ldo] (act
+ * type). tok_row[n] gives
  * each token's row. */
-int hk_op_attention(int act, const void *q, const void *k, const void *v, const void *proj, int ldp,
+int hk_op_attention(int act, const void *q, const void *k, const void *v, const float *proj, int ldp,
                     const int32_t *cu_seqlens, const int32_t *tok_row, int n, int n_rows, int max_len,
                     int nh, int nkv, int hd, void *out, int ldo, void *stream);
 

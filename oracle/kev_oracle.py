@@ -275,8 +275,9 @@ def load_model(model_dir, dtype: str = "fp32") -> KevModel:
 
     Follows load_with_head (qwen3_5.rs:2185-2348): canonical names
     (2496-2512), LoRA merge ``W += (alpha/r) * B @ A`` in fp32 (1597-1640), then
-    the cast to the model dtype. ``bf16`` rounds every backbone tensor to bf16
-    (the reference loader casts all tensors to the model dtype); ``int8w`` is
+    the cast to the model dtype. ``bf16`` / ``fp16`` round every backbone
+    tensor to that type (the reference loader casts all tensors to the model
+    dtype); ``int8w`` is
     ``bf16`` with the projection weights instead quantized per output channel
     and dequantized (``q * scale``) for the fp32 math. The pointer head stays
     fp32 (kev.rs:124-165).
@@ -321,6 +322,9 @@ def load_model(model_dir, dtype: str = "fp32") -> KevModel:
                 w[k] = (q.astype(F32) * s[:, None]).astype(F32)
             else:
                 w[k] = bf16_round(w[k])
+    elif dtype == "fp16":
+        for k in list(w):
+            w[k] = w[k].astype(np.float16).astype(F32)
     elif dtype != "fp32":
         raise ValueError(f"unsupported dtype {dtype}")
     meta = json.loads((d / "kev_head.json").read_text())

@@ -1,7 +1,7 @@
 """Per-kernel parity on the GPU, through the kernel-level C entry points.
 
 The tensor-core GEMM is checked against an fp32 PyTorch matmul of the same
-bf16 operands; the fp32 GEMM against an fp32 matmul with TF32 disabled; the
+fp16 operands; the fp32 GEMM against an fp32 matmul with TF32 disabled; the
 delta-rule recurrence against the CPU oracle (bit-exact in its exact mode when
 the decay is exactly representable); attention against an fp32 PyTorch
 reference of qwen3_5.rs:669-714.
@@ -47,9 +47,9 @@ SHAPES = [(1, 256, 64), (7, 32, 16), (130, 300, 1024), (257, 512, 72), (300, 822
 @pytest.mark.parametrize("M,N,K", SHAPES)
 def test_tc_gemm_store_bf16(lib, M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
-    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
-    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
-    out = torch.zeros(M, N, device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
+    out = torch.zeros(M, N, device="cuda", dtype=torch.float16)
     gemm(lib, 1, 0, x, w, out)
     ref = x.float() @ w.float().T
     torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2)
@@ -58,8 +58,8 @@ def test_tc_gemm_store_bf16(lib, M, N, K):
 @pytest.mark.parametrize("M,N,K", SHAPES)
 def test_tc_gemm_residual_f32(lib, M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M + N * 3)
-    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
-    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
     res = torch.randn(M, N, device="cuda", generator=g)
     out = res.clone()
     gemm(lib, 1, 1, x, w, out)
@@ -70,8 +70,8 @@ def test_tc_gemm_residual_f32(lib, M, N, K):
 def test_tc_gemm_scale_and_f32_store(lib):
     g = torch.Generator(device="cuda").manual_seed(5)
     M, N, K = 300, 520, 256
-    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
-    wq = torch.randint(-127, 128, (N, K), device="cuda", generator=g).float().bfloat16()
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    wq = torch.randint(-127, 128, (N, K), device="cuda", generator=g).float().half()
     scale = torch.rand(N, device="cuda", generator=g) * 1e-3
     out = torch.zeros(M, N, device="cuda")
     gemm(lib, 1, 3, x, wq, out, scale)
@@ -82,11 +82,11 @@ def test_tc_gemm_scale_and_f32_store(lib):
 def test_tc_gemm_swiglu(lib):
     g = torch.Generator(device="cuda").manual_seed(9)
     M, F, K = 333, 512, 1024
-    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
-    gate = (torch.randn(F, K, device="cuda", generator=g) * 0.05).bfloat16()
-    up = (torch.randn(F, K, device="cuda", generator=g) * 0.05).bfloat16()
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    gate = (torch.randn(F, K, device="cuda", generator=g) * 0.05).half()
+    up = (torch.randn(F, K, device="cuda", generator=g) * 0.05).half()
     w = torch.cat([torch.cat([gate[b:b + 128], up[b:b + 128]]) for b in range(0, F, 128)])
-    out = torch.zeros(M, F, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros(M, F, device="cuda", dtype=torch.float16)
     gemm(lib, 1, 2, x, w, out)
     gf, uf = x.float() @ gate.float().T, x.float() @ up.float().T
     ref = gf / (1 + torch.exp(-gf)) * uf
@@ -96,8 +96,8 @@ def test_tc_gemm_swiglu(lib):
 def test_tc_gemm_repeatable(lib):
     """Same inputs, same bits (no nondeterministic reduction)."""
     g = torch.Generator(device="cuda").manual_seed(11)
-    x = torch.randn(777, 1024, device="cuda", generator=g).bfloat16()
-    w = torch.randn(2048, 1024, device="cuda", generator=g).bfloat16()
+    x = torch.randn(777, 1024, device="cuda", generator=g).half()
+    w = torch.randn(2048, 1024, device="cuda", generator=g).half()
     a = torch.zeros(777, 2048, device="cuda")
     b = torch.zeros(777, 2048, device="cuda")
     gemm(lib, 1, 3, x, w, a)
@@ -188,17 +188,17 @@ def _attn_ref(q, k, v, gate, lens, nh, nkv):
     return torch.cat(outs).reshape(sum(lens), -1)
 
 
-@pytest.mark.parametrize("act,hd", [(0, 4), (0, 64), (1, 256)])
+@pytest.mark.parametrize("act,hd", [(0, 4), (0, 64), (1, 64), (1, 256)])
 def test_attention_vs_torch(lib, act, hd):
     g = torch.Generator(device="cuda").manual_seed(hd)
     nh, nkv = 8, 2
     lens = [5, 70, 1, 33]
     n = sum(lens)
-    dt = torch.float32 if act == 0 else torch.bfloat16
+    dt = torch.float32 if act == 0 else torch.float16
     q = torch.randn(n, nh, hd, device="cuda", generator=g).to(dt)
     k = torch.randn(n, nkv, hd, device="cuda", generator=g).to(dt)
     v = torch.randn(n, nkv, hd, device="cuda", generator=g).to(dt)
-    proj = torch.randn(n, nh, 2 * hd, device="cuda", generator=g).to(dt)
+    proj = torch.randn(n, nh, 2 * hd, device="cuda", generator=g)
     cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device="cuda")
     tok_row = torch.tensor(np.repeat(np.arange(len(lens)), lens), dtype=torch.int32, device="cuda")
     out = torch.zeros(n, nh * hd, device="cuda", dtype=dt)
@@ -209,5 +209,5 @@ def test_attention_vs_torch(lib, act, hd):
     assert rc == 0, lib.hk_op_last_error()
     torch.cuda.synchronize()
     ref = _attn_ref(q.float(), k.float(), v.float(), proj.float()[:, :, hd:], lens, nh, nkv)
-    tol = 1e-5 if act == 0 else 2e-2
+    tol = 1e-5 if act == 0 else 5e-3
     torch.testing.assert_close(out.float(), ref, rtol=tol, atol=tol)

@@ -47,11 +47,6 @@ def tiny_fp32(native_lib):
     return _backend(GOLDEN, "fp32")
 
 
-@pytest.fixture(scope="module")
-def tiny_bf16(native_lib):
-    return _backend(GOLDEN, "bf16")
-
-
 def test_tiny_fp32_matches_upstream(tiny_fp32, golden):
     from huncho_b200.backend import ForwardInput
     b = tiny_fp32
@@ -70,12 +65,15 @@ def test_tiny_fp32_matches_upstream(tiny_fp32, golden):
     assert abs(out.values[0, 0] - golden["short_logits"][0]) < 2e-4
 
 
-def test_tiny_bf16_matches_upstream_at_half_precision_gate(tiny_bf16, golden):
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_tiny_half_matches_upstream_at_half_precision_gate(native_lib, golden, dtype):
+    """The reference's own half-precision gate (kev_reference.rs:74-76): 2e-3."""
     from huncho_b200.backend import ForwardInput
+    b = _backend(GOLDEN, dtype)
     for case in golden["cases"]:
         for row in case["rows"]:
-            raw = tiny_bf16.forward(ForwardInput(row["tokens"], row["positions"])).values[:, 0]
-            p = calibration.calibrate(raw, tiny_bf16.temperature)
+            raw = b.forward(ForwardInput(row["tokens"], row["positions"])).values[:, 0]
+            p = calibration.calibrate(raw, b.temperature)
             assert np.abs(p - np.array(row["probabilities"], np.float32)).max() < 2e-3
 
 
@@ -156,6 +154,7 @@ def _synth(synth_root, name, store):
     ("kev-mini", "int8w", "bf16", 2e-3),
     ("kev-0.8b-l4", "bf16", "bf16", 2e-3),
     ("kev-0.8b-l4", "int8w", "bf16", 2e-3),
+    ("kev-0.8b-l4", "fp16", "bf16", 2e-3),
 ])
 def test_synthetic_model_vs_oracle(native_lib, synth_root, name, dtype, store, tol):
     d = _synth(synth_root, name, store)
@@ -175,3 +174,46 @@ def test_synthetic_model_vs_oracle(native_lib, synth_root, name, dtype, store, t
         worst = max(worst, float(np.abs(pr - pg).max()))
         assert calibration.argmax(pg.tolist()) == calibration.argmax(pr.tolist()), (pr, pg)
     assert worst < tol, worst
+
+
+def test_full_kev_08b_bf16_vs_oracle(native_lib, synth_root):
+    """The benchmark model itself (24 layers, vocab 248320) on two requests of
+    the benchmark workload: probabilities within 2e-3 of the fp32 oracle on the
+    same bf16 weights, same argmax on every row."""
+    d = synth.write_model(synth.default_dir("kev-0.8b", 0, "bf16"), "kev-0.8b", 0, "bf16")
+    b = _backend(d, "bf16", max_context=8192)
+    m = ko.load_model(d, "bf16")
+    wl = synth.make_workload(2, m.cfg.vocab_size, seed=0, n_requests=2)
+    got = b.score_packed(*pack_rows(wl.rows, wl.positions))
+    k, worst = 0, 0.0
+    for r, p in zip(wl.rows, wl.positions):
+        pr = ko.calibrate(ko.score_row(m, r, p), m.temperature)
+        pg = calibration.calibrate(got[k:k + len(p)], m.temperature)
+        k += len(p)
+        worst = max(worst, float(np.abs(pr - pg).max()))
+        assert calibration.argmax(pg.tolist()) == calibration.argmax(pr.tolist()), (pr, pg)
+    assert worst < 2e-3, worst
+
+
+def test_full_size_batch_invariance(native_lib):
+    """At the full benchmark size (96 rows in two native batches of 48), each
+    row's logits equal those of the same row scored alone (within 1e-4 in
+    probability) -- a size-independent property of packed independent rows."""
+    d = synth.write_model(synth.default_dir("kev-0.8b", 0, "bf16"), "kev-0.8b", 0, "bf16")
+    b = _backend(d, "bf16", max_context=8192)
+    wl = synth.make_workload(2, 248320, seed=0)
+    assert len(wl.rows) == 96
+    outs = []
+    for s in (0, 48):
+        outs.append(b.score_packed(*pack_rows(wl.rows[s:s + 48], wl.positions[s:s + 48])))
+    got = np.concatenate(outs)
+    assert np.isfinite(got).all()
+    k = 0
+    for i, (r, p) in enumerate(zip(wl.rows, wl.positions)):
+        if i % 16 == 0:
+            single = b.score_packed(*pack_rows([r], [p]))
+            pa = calibration.calibrate(single, b.temperature)
+            pb = calibration.calibrate(got[k:k + len(p)], b.temperature)
+            assert np.abs(pa - pb).max() <= 1e-4
+            assert calibration.argmax(pa.tolist()) == calibration.argmax(pb.tolist())
+        k += len(p)
