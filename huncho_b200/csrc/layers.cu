@@ -96,6 +96,83 @@ __global__ void delta_prep_kernel(DeltaPrepArgs a) {
     }
 }
 
+// Vectorised variant for 128-wide heads and 4 taps: one warp per (block of
+// TB consecutive tokens, head slot); slot < nk: a q head, < 2nk: a k head,
+// < 2nk + nv: a v head, == 2nk + nv: beta and g for the block. Each lane owns
+// 4 channels and keeps the last 3 inputs of each in registers, so every
+// projection element is read once (float4) and every output written once.
+// The conv sum keeps the taps' ascending order with separately rounded
+// products (conv_cpu.rs:38-49).
+template <int TB>
+__global__ void delta_prep_vec_kernel(DeltaPrepArgs a) {
+    const int warps = blockDim.x / 32;
+    const int wid = blockIdx.x * warps + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    const int slots = 2 * a.nk + a.nv + 1;
+    const int nblk = (a.n + TB - 1) / TB;
+    if (wid >= nblk * slots) return;
+    const int blk = wid / slots, slot = wid % slots;
+    const int t0 = blk * TB, t1 = min(a.n, t0 + TB);
+    const int key_dim = a.nk * 128, value_dim = a.nv * 128;
+    const int conv_dim = 2 * key_dim + value_dim;
+    if (slot == 2 * a.nk + a.nv) {  // gating: lanes over value heads
+        for (int t = t0; t < t1; ++t)
+            for (int h = lane; h < a.nv; h += 32) {
+                const float *pr = a.proj + static_cast<size_t>(t) * a.ldp + conv_dim + value_dim;
+                a.beta[static_cast<size_t>(t) * a.nv + h] = sigmoid_f(pr[h]);
+                const float sp = logf(expf(pr[a.nv + h] + a.dt_bias[h]) + 1.0f);
+                a.g[static_cast<size_t>(t) * a.nv + h] = a.base_g[h] * sp;
+            }
+        return;
+    }
+    const bool is_q = slot < a.nk, is_k = !is_q && slot < 2 * a.nk;
+    const int c0 = (is_q ? slot * 128 : is_k ? key_dim + (slot - a.nk) * 128
+                                            : 2 * key_dim + (slot - 2 * a.nk) * 128) + lane * 4;
+    float w[4][4];  // [channel][tap]
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) w[c][k] = a.conv_w[(c0 + c) * 4 + k];
+    // History x[t-3], x[t-2], x[t-1] for the 4 channels (zero outside the row).
+    float4 h3 = make_float4(0.f, 0.f, 0.f, 0.f), h2 = h3, h1 = h3;
+    {
+        const int p0 = a.pos[t0];
+        if (p0 >= 3) h3 = *reinterpret_cast<const float4 *>(a.proj + static_cast<size_t>(t0 - 3) * a.ldp + c0);
+        if (p0 >= 2) h2 = *reinterpret_cast<const float4 *>(a.proj + static_cast<size_t>(t0 - 2) * a.ldp + c0);
+        if (p0 >= 1) h1 = *reinterpret_cast<const float4 *>(a.proj + static_cast<size_t>(t0 - 1) * a.ldp + c0);
+    }
+    const float qscale = 1.0f / sqrtf(128.0f);
+    for (int t = t0; t < t1; ++t) {
+        if (a.pos[t] == 0) h3 = h2 = h1 = make_float4(0.f, 0.f, 0.f, 0.f);  // a new row starts
+        const float4 x = *reinterpret_cast<const float4 *>(a.proj + static_cast<size_t>(t) * a.ldp + c0);
+        const float xs[4][4] = {{h3.x, h2.x, h1.x, x.x}, {h3.y, h2.y, h1.y, x.y},
+                                {h3.z, h2.z, h1.z, x.z}, {h3.w, h2.w, h1.w, x.w}};
+        float y[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            float acc = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc = __fadd_rn(acc, __fmul_rn(w[c][k], xs[c][k]));
+            y[c] = silu_f(acc);
+        }
+        float4 out;
+        if (is_q || is_k) {
+            float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
+            const float inv = 1.0f / sqrtf(ss + 1e-6f);
+            const float sc = is_q ? qscale : 1.0f;
+            out = make_float4((y[0] * inv) * sc, (y[1] * inv) * sc, (y[2] * inv) * sc, (y[3] * inv) * sc);
+            float *dst = (is_q ? a.q : a.k) + static_cast<size_t>(t) * key_dim + (c0 - (is_q ? 0 : key_dim));
+            *reinterpret_cast<float4 *>(dst) = out;
+        } else {
+            out = make_float4(y[0], y[1], y[2], y[3]);
+            *reinterpret_cast<float4 *>(a.v + static_cast<size_t>(t) * value_dim + (c0 - 2 * key_dim)) = out;
+        }
+        h3 = h2;
+        h2 = h1;
+        h1 = x;
+    }
+}
+
 // ------------------------------------------------------------------ delta recurrence
 // One CTA per (row, value head); thread j owns state column S[:, j] in
 // registers, so the memory readout sum_i S[i,j] k_i and the output readout
@@ -158,6 +235,76 @@ __global__ void __launch_bounds__(128) delta_recurrent_kernel(DeltaRecArgs a) {
             a.out[(static_cast<size_t>(t) * a.nv + h) * a.dv + j] = o;
         }
         buf ^= 1;
+    }
+}
+
+// Split variant for DK = 128 (the reassociated, non-exact mode): SPLIT threads
+// share one state column, thread `part` owning rows part, part + SPLIT, ...
+// (so the threads of a column read different shared-memory banks); partial
+// sums combine with shuffles (the threads of a column are adjacent lanes).
+// Token inputs are prefetched PF tokens ahead into registers, so global load
+// latency stays off the serial per-token chain.
+template <int DK, int SPLIT, int PF>
+__global__ void __launch_bounds__(128 * SPLIT) delta_recurrent_split_kernel(DeltaRecArgs a) {
+    constexpr int R = DK / SPLIT;
+    __shared__ float kq[2][2][DK];
+    const int row = blockIdx.x, h = blockIdx.y;
+    const int col = threadIdx.x / SPLIT, part = threadIdx.x % SPLIT;
+    const int kh = h / (a.nv / a.nk);
+    const int start = a.cu_seqlens[row], end = a.cu_seqlens[row + 1];
+    if (start >= end) return;
+    const bool active = col < a.dv;
+    const int li = threadIdx.x;  // loader role: li < DK loads k[li], li < 2*DK loads q[li - DK]
+    float S[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) S[i] = 0.f;
+    float pkq[PF], pv[PF], pg[PF], pb[PF];
+    auto fetch = [&](int u, int t) {
+        if (li < DK)
+            pkq[u] = a.k[(static_cast<size_t>(t) * a.nk + kh) * DK + li];
+        else if (li < 2 * DK)
+            pkq[u] = a.q[(static_cast<size_t>(t) * a.nk + kh) * DK + (li - DK)];
+        pv[u] = active ? a.v[(static_cast<size_t>(t) * a.nv + h) * a.dv + col] : 0.f;
+        pg[u] = a.g[static_cast<size_t>(t) * a.nv + h];
+        pb[u] = a.beta[static_cast<size_t>(t) * a.nv + h];
+    };
+#pragma unroll
+    for (int u = 0; u < PF; ++u)
+        if (start + u < end) fetch(u, start + u);
+    int buf = 0;
+    for (int t0 = start; t0 < end; t0 += PF) {
+#pragma unroll
+        for (int u = 0; u < PF; ++u) {
+            const int t = t0 + u;
+            if (t >= end) break;
+            if (li < 2 * DK) kq[buf][li / DK][li % DK] = pkq[u];
+            const float vj = pv[u], d = expf(pg[u]), b = pb[u];
+            __syncthreads();
+            if (t + PF < end) fetch(u, t + PF);
+            const float *ks = kq[buf][0] + part;
+            const float *qs = kq[buf][1] + part;
+            float m4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                S[i] *= d;
+                m4[i & 3] = fmaf(S[i], ks[i * SPLIT], m4[i & 3]);
+            }
+            float m = (m4[0] + m4[1]) + (m4[2] + m4[3]);
+#pragma unroll
+            for (int o = 1; o < SPLIT; o <<= 1) m += __shfl_xor_sync(0xffffffffu, m, o);
+            const float delta = (vj - m) * b;
+            float o4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                S[i] = fmaf(ks[i * SPLIT], delta, S[i]);
+                o4[i & 3] = fmaf(S[i], qs[i * SPLIT], o4[i & 3]);
+            }
+            float o = (o4[0] + o4[1]) + (o4[2] + o4[3]);
+#pragma unroll
+            for (int off = 1; off < SPLIT; off <<= 1) o += __shfl_xor_sync(0xffffffffu, o, off);
+            if (active && part == 0) a.out[(static_cast<size_t>(t) * a.nv + h) * a.dv + col] = o;
+            buf ^= 1;
+        }
     }
 }
 
@@ -369,6 +516,13 @@ void launch_rmsnorm(int act, const float *x, int ldx, const float *w_eff, float 
 
 void launch_delta_prep(const DeltaPrepArgs &a, cudaStream_t s) {
     if (a.n <= 0) return;
+    if (a.dk == 128 && a.dv == 128 && a.taps == 4 && a.nv <= 32 && (a.ldp % 4) == 0) {
+        constexpr int TB = 16;
+        const long warps = static_cast<long>((a.n + TB - 1) / TB) * (2 * a.nk + a.nv + 1);
+        delta_prep_vec_kernel<TB><<<ceil_div(warps, 8), 256, 0, s>>>(a);
+        HK_LAUNCH_CHECK();
+        return;
+    }
     const size_t smem = sizeof(float) * (2 * a.nk * a.dk + a.nv * a.dv);
     HK_CUDA(cudaFuncSetAttribute(delta_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem)));
@@ -378,6 +532,11 @@ void launch_delta_prep(const DeltaPrepArgs &a, cudaStream_t s) {
 
 template <int DK>
 static void launch_rec_dk(const DeltaRecArgs &a, cudaStream_t s) {
+    if (DK == 128 && !a.exact && a.dv <= 128) {
+        dim3 grid(a.n_rows, a.nv);
+        delta_recurrent_split_kernel<128, 4, 4><<<grid, 512, 0, s>>>(a);
+        return;
+    }
     const int threads = a.dv <= 32 ? 32 : (a.dv <= 64 ? 64 : 128);
     dim3 grid(a.n_rows, a.nv);
     if (a.exact)
@@ -388,6 +547,10 @@ static void launch_rec_dk(const DeltaRecArgs &a, cudaStream_t s) {
 
 void launch_delta_recurrent(const DeltaRecArgs &a, cudaStream_t s) {
     if (a.n_rows <= 0) return;
+    if (!a.exact && delta_chunk_supported(a)) {
+        launch_delta_chunk(a, s);
+        return;
+    }
     if (a.dv > 128) throw CudaError("delta recurrence supports value heads up to 128 wide");
     switch (a.dk) {
         case 4: launch_rec_dk<4>(a, s); break;
@@ -427,6 +590,10 @@ void launch_attn_prep(int act, const AttnPrepArgs &a, cudaStream_t s) {
 void launch_attention(int act, const AttnArgs &a, cudaStream_t s) {
     if (a.n <= 0) return;
     if (a.hd > 256) throw CudaError("attention supports head_dim up to 256");
+    if (act == kActF16 && attention_tc_supported(a.hd)) {
+        launch_attention_tc(a, s);
+        return;
+    }
     const int grid = ceil_div(static_cast<long>(a.n) * a.nh, 8);
     if (act == kActF32)
         attn_simt_kernel<float><<<grid, 256, 0, s>>>(a);

@@ -52,6 +52,10 @@ struct DeltaRecArgs {
     int exact;
 };
 void launch_delta_recurrent(const DeltaRecArgs &a, cudaStream_t s);
+// The chunked tensor-core form behind launch_delta_recurrent (non-exact mode,
+// 128-wide heads).
+bool delta_chunk_supported(const DeltaRecArgs &a);
+void launch_delta_chunk(const DeltaRecArgs &a, cudaStream_t s);
 
 // out[t, h*dv + j] = rms(o)[j] * w[j] * silu(z[t, h, j]) (qwen3_5.rs:193-201,
 // 934-938); o and z fp32, out in the activation type (the out_proj input).
@@ -86,6 +90,9 @@ struct AttnArgs {
     int ldo;
 };
 void launch_attention(int act, const AttnArgs &a, cudaStream_t s);
+// The tensor-core (fp16) kernel behind launch_attention for head_dim 64/128/256.
+bool attention_tc_supported(int hd);
+void launch_attention_tc(const AttnArgs &a, cudaStream_t s);
 
 // out[t, j] = silu(gu[t, j]) * gu[t, F + j] (qwen3_5.rs:1020-1031); gu fp32.
 void launch_swiglu(int act, const float *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s);
