@@ -176,6 +176,8 @@ def main():
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--requests", type=int, default=None,
+                    help="requests per GPU (default: the config's); smaller cases are for profiling")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -213,7 +215,8 @@ def main():
     if rank == 0:
         synth.write_model(d, name, args.seed, store)
     barrier()
-    wl = synth.make_workload(args.config, synth.SPECS[name]["vocab_size"], seed=args.seed + rank)
+    wl = synth.make_workload(args.config, synth.SPECS[name]["vocab_size"], seed=args.seed + rank,
+                             n_requests=args.requests)
     max_len = max(len(r) for r in wl.rows)
     backend = KevBackend(d, device=local, dtype=dtype, max_context=max(8192, max_len))
 

@@ -14,11 +14,15 @@
 //   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and
 //               issues tcgen05.mma (M=128, N=256, K=16) from one thread;
 //   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp its 32-lane
-//               quarter), apply scale / residual / SwiGLU, store to global.
+//               quarter), apply scale / SwiGLU, stage 32-row x 128-byte slabs
+//               in 128B-swizzled shared memory (two buffers per warp) and write
+//               them with TMA bulk-tensor stores -- or TMA reduce-add into the
+//               fp32 residual stream -- so global writes are full lines.
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
 // No cluster multicast is used; every CTA loads its own tiles.
 #include <cuda.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "gemm.cuh"
@@ -32,7 +36,9 @@ constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
 constexpr int TMEM_COLS = 2 * BN;           // double-buffered accumulator
 constexpr int THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 + 256;
+constexpr int EPI_BUF_BYTES = 32 * 128;  // one warp's 32-row x 128-byte staging slab
+constexpr int EPI_BYTES = 4 * 2 * EPI_BUF_BYTES;
+constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + EPI_BYTES + 1024 + 256;
 
 struct TcParams {
     int M, N, K;
@@ -41,39 +47,31 @@ struct TcParams {
     int ldo;
     const float *scale;
     int vec_ok;  // out pointer / ldo allow 16-byte vector stores
+    int tma_out; // the output goes through the TMA store tensor map
     uint32_t *err;
 };
 
-__device__ __forceinline__ void store_half_32(__half *dst, const float (&v)[32], int valid, bool vec) {
-    if (vec && valid >= 32) {
-        uint4 pk[4];
-        uint32_t *w = reinterpret_cast<uint32_t *>(pk);
+// Write one thread's 128-byte row (8 chunks of 16 bytes) into a 128B-swizzled
+// staging slab: chunk c of row r lands in physical chunk c ^ (r & 7).
+__device__ __forceinline__ void stage_row(uint8_t *slab, int r, const uint4 (&chunks)[8]) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-            w[i] = *reinterpret_cast<uint32_t *>(&h);
-        }
-        uint4 *d = reinterpret_cast<uint4 *>(dst);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) d[i] = pk[i];
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-            if (i < valid) dst[i] = __float2half_rn(v[i]);
-    }
+    for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4 *>(slab + r * 128 + ((c ^ (r & 7)) << 4)) = chunks[c];
 }
 
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
-                        const __grid_constant__ CUtensorMap tm_w, TcParams p) {
+                        const __grid_constant__ CUtensorMap tm_w,
+                        const __grid_constant__ CUtensorMap tm_o, TcParams p) {
     using namespace sm100;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * A_STAGE_BYTES;
-    uint64_t *full = reinterpret_cast<uint64_t *>(sB + STAGES * B_STAGE_BYTES);
+    uint8_t *sE = sB + STAGES * B_STAGE_BYTES;  // epilogue staging, 1024-aligned
+    uint64_t *full = reinterpret_cast<uint64_t *>(sE + EPI_BYTES);
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;
     uint64_t *tempty = tfull + 2;
@@ -192,8 +190,29 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else {
         // ---------------------------------------------------- epilogue
         const int quarter = warp & 3;  // TMEM lanes this warp may access
+        uint8_t *const slab0 = sE + (warp - 2) * 2 * EPI_BUF_BYTES;
+        int sb = 0;  // staging buffer to fill next
+        auto slab = [&]() { return slab0 + sb * EPI_BUF_BYTES; };
         int acc = 0;
         uint32_t acc_phase = 0;
+        // Hand a filled slab to the TMA unit (lane 0), keeping at most one older
+        // store in flight on the other buffer.
+        auto issue = [&](int x, int y) {
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                if (EPI == kEpiResidual)
+                    tma_reduce_add_2d(&tm_o, slab(), x, y);
+                else
+                    tma_store_2d(&tm_o, slab(), x, y);
+                bulk_commit();
+            }
+            sb ^= 1;
+        };
+        auto reuse_wait = [&]() {
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+        };
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             if (!mbar_wait(&tfull[acc], acc_phase)) {
                 set_error(p.err, kErrWaitTimeout);
@@ -203,33 +222,87 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (*abort_flag) break;
             tc_fence_after();
             const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
-            const int row = m_blk * BM + quarter * 32 + lane;
+            const int row0 = m_blk * BM + quarter * 32;
+            const int row = row0 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
             const bool row_ok = row < p.M;
+            const bool slab_ok = row0 < p.M;
             if (EPI == kEpiSwiGLU) {
-                // Tile columns [0,128) are gate rows, [128,256) the matching up rows.
+                // Tile columns [0,128) are gate rows, [128,256) the matching up rows;
+                // each round produces 64 fp16 outputs per row.
 #pragma unroll 1
-                for (int c = 0; c < BN / 2; c += 32) {
-                    float g[32], u[32];
-                    tmem_ld32(t_row + c, g);
-                    tmem_ld32(t_row + BN / 2 + c, u);
-                    const int wcol = n_blk * BN + c;  // weight row of g[0]
-                    if (p.scale) {
+                for (int c = 0; c < BN / 2; c += 64) {
+                    uint32_t packed[32];
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            g[i] *= __ldg(p.scale + wcol + i);
-                            u[i] *= __ldg(p.scale + wcol + BN / 2 + i);
+                    for (int hh = 0; hh < 2; ++hh) {
+                        float g[32], u[32];
+                        tmem_ld32(t_row + c + 32 * hh, g);
+                        tmem_ld32(t_row + BN / 2 + c + 32 * hh, u);
+                        const int wcol = n_blk * BN + c + 32 * hh;  // weight row of g[0]
+                        if (p.scale) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                g[i] *= __ldg(p.scale + wcol + i);
+                                u[i] *= __ldg(p.scale + wcol + BN / 2 + i);
+                            }
+                        }
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            __half2 h2 = __floats2half2_rn(silu_f(g[2 * i]) * u[2 * i], silu_f(g[2 * i + 1]) * u[2 * i + 1]);
+                            packed[16 * hh + i] = *reinterpret_cast<uint32_t *>(&h2);
                         }
                     }
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) g[i] = silu_f(g[i]) * u[i];
                     const int ocol = n_blk * (BN / 2) + c;
-                    if (row_ok) {
+                    if (p.tma_out) {
+                        if (!slab_ok || ocol >= p.N / 2) continue;
+                        reuse_wait();
+                        uint4 ch[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) ch[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                        stage_row(slab(), lane, ch);
+                        issue(ocol, row0);
+                    } else if (row_ok) {
                         __half *dst = reinterpret_cast<__half *>(p.out) + static_cast<size_t>(row) * p.ldo + ocol;
-                        store_half_32(dst, g, p.N / 2 - ocol, p.vec_ok);
+                        const __half *hv = reinterpret_cast<const __half *>(packed);
+                        for (int i = 0; i < 64 && ocol + i < p.N / 2; ++i) dst[i] = hv[i];
+                    }
+                }
+            } else if (EPI == kEpiStore) {
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 64) {
+                    const int col = n_blk * BN + c;
+                    uint32_t packed[32];
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        float v[32];
+                        tmem_ld32(t_row + c + 32 * hh, v);
+                        if (p.scale) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (col + 32 * hh + i < p.N) v[i] *= __ldg(p.scale + col + 32 * hh + i);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            __half2 h2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+                            packed[16 * hh + i] = *reinterpret_cast<uint32_t *>(&h2);
+                        }
+                    }
+                    if (p.tma_out) {
+                        if (!slab_ok || col >= p.N) continue;
+                        reuse_wait();
+                        uint4 ch[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) ch[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                        stage_row(slab(), lane, ch);
+                        issue(col, row0);
+                    } else if (row_ok) {
+                        __half *dst = reinterpret_cast<__half *>(p.out) + static_cast<size_t>(row) * p.ldo + col;
+                        const __half *hv = reinterpret_cast<const __half *>(packed);
+                        for (int i = 0; i < 64 && col + i < p.N; ++i) dst[i] = hv[i];
                     }
                 }
             } else {
+                // fp32 outputs: store, or add into the residual stream.
 #pragma unroll 1
                 for (int c = 0; c < BN; c += 32) {
                     float v[32];
@@ -241,31 +314,21 @@ __global__ void __launch_bounds__(THREADS, 1)
                         for (int i = 0; i < 32; ++i)
                             if (i < valid) v[i] *= __ldg(p.scale + col + i);
                     }
-                    if (!row_ok || valid <= 0) continue;
-                    if (EPI == kEpiStore) {
-                        __half *dst = reinterpret_cast<__half *>(p.out) + static_cast<size_t>(row) * p.ldo + col;
-                        store_half_32(dst, v, valid, p.vec_ok);
-                    } else {
+                    if (p.tma_out) {
+                        if (!slab_ok || valid <= 0) continue;
+                        reuse_wait();
+                        uint4 ch[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            ch[i] = make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]),
+                                               __float_as_uint(v[4 * i + 2]), __float_as_uint(v[4 * i + 3]));
+                        stage_row(slab(), lane, ch);
+                        issue(col, row0);
+                    } else if (row_ok && valid > 0) {
                         float *dst = reinterpret_cast<float *>(p.out) + static_cast<size_t>(row) * p.ldo + col;
-                        if (p.vec_ok && valid >= 32) {
-                            float4 *d4 = reinterpret_cast<float4 *>(dst);
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                                if (EPI == kEpiResidual) {
-                                    const float4 r = d4[i];
-                                    o.x += r.x;
-                                    o.y += r.y;
-                                    o.z += r.z;
-                                    o.w += r.w;
-                                }
-                                d4[i] = o;
-                            }
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < 32; ++i)
-                                if (i < valid) dst[i] = (EPI == kEpiResidual) ? dst[i] + v[i] : v[i];
-                        }
+                        for (int i = 0; i < 32; ++i)
+                            if (i < valid) dst[i] = (EPI == kEpiResidual) ? dst[i] + v[i] : v[i];
                     }
                 }
             }
@@ -275,6 +338,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             acc ^= 1;
             if (acc == 0) acc_phase ^= 1;
         }
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -325,6 +390,23 @@ CUtensorMap make_map(const void *base, int rows, int inner, int ld, int box_rows
     return m;
 }
 
+// Output tensor map for the epilogue's TMA stores: box of 32 rows x 128 bytes
+// (32 fp32 or 64 fp16 columns), 128B swizzle. Returns false when the output
+// does not meet TMA's alignment rules (the epilogue then stores directly).
+bool make_out_map(CUtensorMap &m, const void *base, int rows, int cols, int ld, bool f32) {
+    const int esz = f32 ? 4 : 2;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (static_cast<long>(ld) * esz) % 16) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * esz};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esz), 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                             const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 template <int EPI>
 void launch(const GemmArgs &a, cudaStream_t s, int num_sms) {
     static bool attr_set[64] = {};  // the attribute is per device
@@ -350,9 +432,14 @@ void launch(const GemmArgs &a, cudaStream_t s, int num_sms) {
     const int elem = (EPI == kEpiStore || EPI == kEpiSwiGLU) ? 2 : 4;
     p.vec_ok = ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0) && ((a.ldo * elem) % 16 == 0);
     p.err = a.err;
+    CUtensorMap to;
+    std::memset(&to, 0, sizeof(to));
+    const bool f32 = (EPI == kEpiResidual || EPI == kEpiStoreF32);
+    const int out_cols = (EPI == kEpiSwiGLU) ? a.N / 2 : a.N;
+    p.tma_out = make_out_map(to, a.out, a.M, out_cols, a.ldo, f32) ? 1 : 0;
     const int tiles = p.m_tiles * p.n_tiles;
     const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_f16_tc_kernel<EPI><<<grid, THREADS, SMEM_BYTES, s>>>(tx, tw, p);
+    gemm_f16_tc_kernel<EPI><<<grid, THREADS, SMEM_BYTES, s>>>(tx, tw, to, p);
     HK_LAUNCH_CHECK();
 }
 
