@@ -13,15 +13,23 @@
 //     S_C    = gam_C S0 + (diag(e^{G_C - G_s}) K)^T D
 // which is exact algebra; only the rounding differs from the per-token loop.
 //
-// One CTA of 4 warps owns one (row, value head) and walks its chunks in order,
+// One CTA of 8 warps owns one (row, value head) and walks its chunks in order,
 // keeping the fp32 state S (128 x 128) in registers as the accumulator of the
-// state update (warp w owns key rows 32w..32w+31). Products run on tensor
+// state update (warp w owns key rows 16w..16w+15). Products run on tensor
 // cores (mma.sync m16n8k16, fp16 operands, fp32 accumulation); the operands
 // whose rounding moves the calibrated probabilities (q, k, b*v, D and Mq) are
 // split into fp16 hi + lo parts so each product carries ~22 bits, while S, W,
 // T and the decayed keys use single fp16. T comes from fp32 forward
 // substitution. Padding rows of a short last chunk are zero (g = 0, b = 0), so
 // they change neither the outputs nor the carried state.
+//
+// In the fused form (FROM_PROJ) the kernel also does the layer's input stage
+// from the fp32 projection rows -- causal depthwise conv (4 taps, in-row
+// history only) + SiLU, L2 norm of q and k (q scaled by 1/sqrt(128)), beta =
+// sigmoid(b), g = -exp(A_log) softplus(a + dt_bias) (qwen3_5.rs:817-925) --
+// and, with GATED_OUT, the gated RMSNorm rms(o) * w * silu(z) into the fp16
+// input of out_proj (qwen3_5.rs:193-201, 934-938); q, k, v and o then never
+// leave the SM.
 #include <math.h>
 
 #include "common.cuh"
@@ -34,7 +42,8 @@ constexpr int C = 32;        // chunk length
 constexpr int D = 128;       // key = value head width
 constexpr int LDH = D + 8;   // padded fp16 row (conflict-free ldmatrix)
 constexpr int LDC = C + 8;
-constexpr int THREADS = 128;
+constexpr int THREADS = 256;  // 8 warps
+constexpr int WARPS = THREADS / 32;
 
 struct Smem {
     __half S[D][LDH];       // fp16 copy of the state (B operand)
@@ -46,6 +55,7 @@ struct Smem {
     __half T[C][LDC];
     __half Mh[C][LDC], Ml[C][LDC];
     float G[C], gam[C], beta[C];
+    float red[WARPS][C];  // per-warp partial sums of squares (gated norm)
 };
 
 __device__ __forceinline__ uint32_t sa(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -99,7 +109,38 @@ __device__ __forceinline__ void split_store(__half *hi, __half *lo, float v) {
     *lo = __float2half_rn(v - __half2float(h));
 }
 
-__global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(DeltaRecArgs a) {
+// Four consecutive fp16 values as one 8-byte store (hi and lo parts of v).
+__device__ __forceinline__ void split_store4(__half *hi, __half *lo, const float (&v)[4]) {
+    __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
+    const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+    __half2 l0 = __floats2half2_rn(v[0] - f0.x, v[1] - f0.y), l1 = __floats2half2_rn(v[2] - f1.x, v[3] - f1.y);
+    *reinterpret_cast<uint2 *>(hi) = make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1));
+    *reinterpret_cast<uint2 *>(lo) = make_uint2(*reinterpret_cast<uint32_t *>(&l0), *reinterpret_cast<uint32_t *>(&l1));
+}
+__device__ __forceinline__ void store4(__half *dst, const float (&v)[4]) {
+    __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
+    *reinterpret_cast<uint2 *>(dst) = make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1));
+}
+
+struct ChunkArgs {
+    // Pre-computed inputs (!FROM_PROJ): q, k [n, nk, 128], v [n, nv, 128], g, beta [n, nv].
+    const float *q, *k, *v, *g, *beta;
+    // Fused input stage (FROM_PROJ): projection rows and the layer's parameters.
+    const float *proj;
+    int ldp;
+    const float *conv_w, *base_g, *dt_bias;
+    const int32_t *cu_seqlens;
+    int n_rows, nk, nv;
+    float *out;           // !GATED_OUT: o [n, nv, 128] fp32
+    const float *norm_w;  // GATED_OUT: gated-norm weight [128]
+    float eps;
+    __half *mix;  // GATED_OUT: out_proj input [n, ldmix]
+    int ldmix;
+};
+
+
+template <bool FROM_PROJ, bool GATED_OUT>
+__global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(ChunkArgs a) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
     const int row = blockIdx.x, h = blockIdx.y;
@@ -108,22 +149,30 @@ __global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(DeltaRecArgs a)
     const int kh = h / (a.nv / a.nk);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g4 = lane >> 2, t4 = lane & 3;
+    const int key_dim = a.nk * D, value_dim = a.nv * D, conv_dim = 2 * key_dim + value_dim;
 
-    // State accumulator: key rows 32*warp + 16*mt + {g4, g4+8}, value cols 8*nt + 2*t4 + {0,1}.
-    float S[2][16][4];
+    // State accumulator: key rows 16*warp + {g4, g4+8}, value cols 8*nt + 2*t4 + {0,1}.
+    float S[16][4];
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int nt = 0; nt < 16; ++nt) S[mt][nt][0] = S[mt][nt][1] = S[mt][nt][2] = S[mt][nt][3] = 0.f;
+    for (int nt = 0; nt < 16; ++nt) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0.f;
     for (int i = tid; i < D * LDH; i += THREADS) (&sm.S[0][0])[i] = __float2half_rn(0.f);
 
     for (int c0 = start; c0 < end; c0 += C) {
         const int n = min(C, end - c0);
         // ---- P0: gates. Warp 0 scans g; padding rows get g = 0, b = 0.
         if (warp == 0) {
-            const int t = c0 + lane;
-            float gv = lane < n ? a.g[static_cast<size_t>(t) * a.nv + h] : 0.f;
-            const float bv = lane < n ? a.beta[static_cast<size_t>(t) * a.nv + h] : 0.f;
+            const size_t t = static_cast<size_t>(c0 + lane);
+            float gv = 0.f, bv = 0.f;
+            if (lane < n) {
+                if (FROM_PROJ) {
+                    const float *pr = a.proj + t * a.ldp + conv_dim + value_dim;
+                    bv = sigmoid_f(pr[h]);
+                    gv = a.base_g[h] * logf(expf(pr[a.nv + h] + a.dt_bias[h]) + 1.0f);
+                } else {
+                    gv = a.g[t * a.nv + h];
+                    bv = a.beta[t * a.nv + h];
+                }
+            }
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const float up = __shfl_up_sync(0xffffffffu, gv, o);
@@ -134,58 +183,96 @@ __global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(DeltaRecArgs a)
             sm.beta[lane] = bv;
         }
         __syncthreads();
-        // ---- P0b: operands. 32 rows x 128 cols of q, k, v; 4 columns per thread step.
-        for (int e = tid; e < C * (D / 4); e += THREADS) {
-            const int r = e / (D / 4), c = (e % (D / 4)) * 4;
-            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f), k4 = q4, v4 = q4;
+        // ---- P0b: operands. Warp w fills rows w, w+8, ...; lane l owns cols 4l..4l+3.
+        for (int r = warp; r < C; r += WARPS) {
+            float qv[4] = {0.f, 0.f, 0.f, 0.f}, kv[4] = {0.f, 0.f, 0.f, 0.f}, vv[4] = {0.f, 0.f, 0.f, 0.f};
             if (r < n) {
                 const size_t t = static_cast<size_t>(c0 + r);
-                q4 = *reinterpret_cast<const float4 *>(a.q + (t * a.nk + kh) * D + c);
-                k4 = *reinterpret_cast<const float4 *>(a.k + (t * a.nk + kh) * D + c);
-                v4 = *reinterpret_cast<const float4 *>(a.v + (t * a.nv + h) * D + c);
+                if (FROM_PROJ) {
+                    const int pos = c0 + r - start;
+                    const int bases[3] = {kh * D, key_dim + kh * D, 2 * key_dim + h * D};
+                    float *dsts[3] = {qv, kv, vv};
+#pragma unroll
+                    for (int j = 0; j < 3; ++j) {
+                        const int cb = bases[j] + 4 * lane;
+                        float4 xs[4];  // x[t-3], x[t-2], x[t-1], x[t]
+#pragma unroll
+                        for (int sh = 3; sh >= 0; --sh)
+                            xs[3 - sh] = pos >= sh ? *reinterpret_cast<const float4 *>(a.proj + (t - sh) * a.ldp + cb)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const float4 w0 = *reinterpret_cast<const float4 *>(a.conv_w + (cb + 0) * 4);
+                        const float4 w1 = *reinterpret_cast<const float4 *>(a.conv_w + (cb + 1) * 4);
+                        const float4 w2 = *reinterpret_cast<const float4 *>(a.conv_w + (cb + 2) * 4);
+                        const float4 w3 = *reinterpret_cast<const float4 *>(a.conv_w + (cb + 3) * 4);
+                        const float wc[4][4] = {{w0.x, w0.y, w0.z, w0.w}, {w1.x, w1.y, w1.z, w1.w},
+                                                {w2.x, w2.y, w2.z, w2.w}, {w3.x, w3.y, w3.z, w3.w}};
+                        const float xc[4][4] = {{xs[0].x, xs[1].x, xs[2].x, xs[3].x}, {xs[0].y, xs[1].y, xs[2].y, xs[3].y},
+                                                {xs[0].z, xs[1].z, xs[2].z, xs[3].z}, {xs[0].w, xs[1].w, xs[2].w, xs[3].w}};
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            float acc = 0.f;  // taps in ascending order, separately rounded products
+#pragma unroll
+                            for (int tap = 0; tap < 4; ++tap) acc = __fadd_rn(acc, __fmul_rn(wc[c][tap], xc[c][tap]));
+                            dsts[j][c] = silu_f(acc);
+                        }
+                    }
+                    const float qs = warp_sum(qv[0] * qv[0] + qv[1] * qv[1] + qv[2] * qv[2] + qv[3] * qv[3]);
+                    const float ks = warp_sum(kv[0] * kv[0] + kv[1] * kv[1] + kv[2] * kv[2] + kv[3] * kv[3]);
+                    const float qi = 1.0f / sqrtf(qs + 1e-6f), ki = 1.0f / sqrtf(ks + 1e-6f);
+                    const float qscale = 1.0f / sqrtf(static_cast<float>(D));
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        qv[c] = (qv[c] * qi) * qscale;
+                        kv[c] = kv[c] * ki;
+                    }
+                } else {
+                    const float4 q4 = *reinterpret_cast<const float4 *>(a.q + (t * a.nk + kh) * D + 4 * lane);
+                    const float4 k4 = *reinterpret_cast<const float4 *>(a.k + (t * a.nk + kh) * D + 4 * lane);
+                    const float4 v4 = *reinterpret_cast<const float4 *>(a.v + (t * a.nv + h) * D + 4 * lane);
+                    qv[0] = q4.x; qv[1] = q4.y; qv[2] = q4.z; qv[3] = q4.w;
+                    kv[0] = k4.x; kv[1] = k4.y; kv[2] = k4.z; kv[3] = k4.w;
+                    vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
+                }
+            } else if (FROM_PROJ) {
+                // keep the warp reductions uniform for padding rows
+                (void)warp_sum(0.f);
+                (void)warp_sum(0.f);
             }
             const float b = sm.beta[r], bg = sm.beta[r] * sm.gam[r];
-            const float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w},
-                        vv[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                split_store(&sm.Qh[r][c + u], &sm.Ql[r][c + u], qv[u]);
-                split_store(&sm.Kh[r][c + u], &sm.Kl[r][c + u], kv[u]);
-                split_store(&sm.Vh[r][c + u], &sm.Vl[r][c + u], b * vv[u]);
-                sm.BK[r][c + u] = __float2half_rn(bg * kv[u]);
-            }
+            const float bvv[4] = {b * vv[0], b * vv[1], b * vv[2], b * vv[3]};
+            const float bkk[4] = {bg * kv[0], bg * kv[1], bg * kv[2], bg * kv[3]};
+            split_store4(&sm.Qh[r][4 * lane], &sm.Ql[r][4 * lane], qv);
+            split_store4(&sm.Kh[r][4 * lane], &sm.Kl[r][4 * lane], kv);
+            split_store4(&sm.Vh[r][4 * lane], &sm.Vl[r][4 * lane], bvv);
+            store4(&sm.BK[r][4 * lane], bkk);
         }
         __syncthreads();
-        // ---- P1: K K^T (warps 0,1) and Q K^T (warps 2,3), rows 16*(warp&1).., all 32 cols.
+        // ---- P1: K K^T (warps 0-3) and Q K^T (warps 4-7); 16 rows x 16 cols per warp.
         {
-            const int mt = warp & 1;
-            const bool kk = warp < 2;
-            float acc[4][4];
+            const bool kk = warp < 4;
+            const int mt = (warp >> 1) & 1, n0 = (warp & 1) * 16;
+            float acc[2][4];
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+            for (int nt = 0; nt < 2; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
 #pragma unroll
             for (int k0 = 0; k0 < D; k0 += 16) {
-                uint32_t ah[4], al[4];
+                uint32_t ah[4], al[4], bh[4], bl[4];
                 frag_a<LDH>(ah, kk ? sm.Kh : sm.Qh, mt * 16, k0, lane);
                 frag_a<LDH>(al, kk ? sm.Kl : sm.Ql, mt * 16, k0, lane);
-#pragma unroll
-                for (int n0 = 0; n0 < C; n0 += 16) {
-                    uint32_t bh[4], bl[4];
-                    frag_b_nk<LDH>(bh, sm.Kh, k0, n0, lane);
-                    frag_b_nk<LDH>(bl, sm.Kl, k0, n0, lane);
-                    mma(acc[n0 / 8], ah, bh[0], bh[1]);
-                    mma(acc[n0 / 8 + 1], ah, bh[2], bh[3]);
-                    mma(acc[n0 / 8], ah, bl[0], bl[1]);
-                    mma(acc[n0 / 8 + 1], ah, bl[2], bl[3]);
-                    mma(acc[n0 / 8], al, bh[0], bh[1]);
-                    mma(acc[n0 / 8 + 1], al, bh[2], bh[3]);
-                }
+                frag_b_nk<LDH>(bh, sm.Kh, k0, n0, lane);
+                frag_b_nk<LDH>(bl, sm.Kl, k0, n0, lane);
+                mma(acc[0], ah, bh[0], bh[1]);
+                mma(acc[1], ah, bh[2], bh[3]);
+                mma(acc[0], ah, bl[0], bl[1]);
+                mma(acc[1], ah, bl[2], bl[3]);
+                mma(acc[0], al, bh[0], bh[1]);
+                mma(acc[1], al, bh[2], bh[3]);
             }
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt)
+            for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const int t = mt * 16 + g4 + (e >> 1) * 8, s = nt * 8 + 2 * t4 + (e & 1);
+                    const int t = mt * 16 + g4 + (e >> 1) * 8, s = n0 + nt * 8 + 2 * t4 + (e & 1);
                     const float dec = expf(sm.G[t] - sm.G[s]);
                     if (kk) {
                         sm.A[t][s] = s < t ? sm.beta[t] * dec * acc[nt][e] : 0.f;
@@ -214,43 +301,40 @@ __global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(DeltaRecArgs a)
             }
         }
         __syncthreads();
-        // ---- P3: U = T (b v) (hi+lo) and W = T (b gam k); warp w owns value/key cols 32w..32w+31.
-        float u[2][4][4];
+        // ---- P3: U = T (b v) (hi+lo), W = T (b gam k); warp w owns cols 16w..16w+15.
+        const int nb = warp * 16;
+        float u[2][2][4];
         {
-            const int nb = warp * 32;
-            float w[2][4][4];
+            float w[2][2][4];
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt)
+                for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) u[mt][nt][e] = w[mt][nt][e] = 0.f;
 #pragma unroll
             for (int k0 = 0; k0 < C; k0 += 16) {
+                uint32_t vh[4], vl[4], bk[4];
+                frag_b_kn<LDH>(vh, sm.Vh, k0, nb, lane);
+                frag_b_kn<LDH>(vl, sm.Vl, k0, nb, lane);
+                frag_b_kn<LDH>(bk, sm.BK, k0, nb, lane);
 #pragma unroll
                 for (int mt = 0; mt < 2; ++mt) {
                     uint32_t at[4];
                     frag_a<LDC>(at, sm.T, mt * 16, k0, lane);
-#pragma unroll
-                    for (int n0 = 0; n0 < 32; n0 += 16) {
-                        uint32_t vh[4], vl[4], bk[4];
-                        frag_b_kn<LDH>(vh, sm.Vh, k0, nb + n0, lane);
-                        frag_b_kn<LDH>(vl, sm.Vl, k0, nb + n0, lane);
-                        frag_b_kn<LDH>(bk, sm.BK, k0, nb + n0, lane);
-                        mma(u[mt][n0 / 8], at, vh[0], vh[1]);
-                        mma(u[mt][n0 / 8 + 1], at, vh[2], vh[3]);
-                        mma(u[mt][n0 / 8], at, vl[0], vl[1]);
-                        mma(u[mt][n0 / 8 + 1], at, vl[2], vl[3]);
-                        mma(w[mt][n0 / 8], at, bk[0], bk[1]);
-                        mma(w[mt][n0 / 8 + 1], at, bk[2], bk[3]);
-                    }
+                    mma(u[mt][0], at, vh[0], vh[1]);
+                    mma(u[mt][1], at, vh[2], vh[3]);
+                    mma(u[mt][0], at, vl[0], vl[1]);
+                    mma(u[mt][1], at, vl[2], vl[3]);
+                    mma(w[mt][0], at, bk[0], bk[1]);
+                    mma(w[mt][1], at, bk[2], bk[3]);
                 }
             }
             __syncwarp();
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt)
+                for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                     for (int hf = 0; hf < 2; ++hf) {
                         const int t = mt * 16 + g4 + hf * 8, c = nb + nt * 8 + 2 * t4;
@@ -259,51 +343,43 @@ __global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(DeltaRecArgs a)
                     }
         }
         __syncthreads();
-        // ---- P4: D = U + (-W) S0 and O = diag(gam) Q S0 (q hi+lo); warp w owns value cols 32w..
-        float o[2][4][4];
+        // ---- P4: D = U + (-W) S0 and O = diag(gam) Q S0 (q hi+lo); warp w owns cols 16w..
+        float o[2][2][4];
         {
-            const int nb = warp * 32;
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt)
+                for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.f;
-#pragma unroll 2
+#pragma unroll 4
             for (int k0 = 0; k0 < D; k0 += 16) {
-                uint32_t sb[2][4];
-                frag_b_kn<LDH>(sb[0], sm.S, k0, nb, lane);
-                frag_b_kn<LDH>(sb[1], sm.S, k0, nb + 16, lane);
+                uint32_t sb[4];
+                frag_b_kn<LDH>(sb, sm.S, k0, nb, lane);
 #pragma unroll
                 for (int mt = 0; mt < 2; ++mt) {
                     uint32_t aw[4], qh[4], ql[4];
                     frag_a<LDH>(aw, sm.BK, mt * 16, k0, lane);
                     frag_a<LDH>(qh, sm.Qh, mt * 16, k0, lane);
                     frag_a<LDH>(ql, sm.Ql, mt * 16, k0, lane);
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        mma(u[mt][2 * j], aw, sb[j][0], sb[j][1]);
-                        mma(u[mt][2 * j + 1], aw, sb[j][2], sb[j][3]);
-                        mma(o[mt][2 * j], qh, sb[j][0], sb[j][1]);
-                        mma(o[mt][2 * j + 1], qh, sb[j][2], sb[j][3]);
-                        mma(o[mt][2 * j], ql, sb[j][0], sb[j][1]);
-                        mma(o[mt][2 * j + 1], ql, sb[j][2], sb[j][3]);
-                    }
+                    mma(u[mt][0], aw, sb[0], sb[1]);
+                    mma(u[mt][1], aw, sb[2], sb[3]);
+                    mma(o[mt][0], qh, sb[0], sb[1]);
+                    mma(o[mt][1], qh, sb[2], sb[3]);
+                    mma(o[mt][0], ql, sb[0], sb[1]);
+                    mma(o[mt][1], ql, sb[2], sb[3]);
                 }
             }
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt)
+                for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int t = mt * 16 + g4 + (e >> 1) * 8;
-                        o[mt][nt][e] *= sm.gam[t];
-                    }
+                    for (int e = 0; e < 4; ++e) o[mt][nt][e] *= sm.gam[mt * 16 + g4 + (e >> 1) * 8];
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt)
+                for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int t = mt * 16 + g4 + (e >> 1) * 8, c = nb + nt * 8 + 2 * t4 + (e & 1);
@@ -311,112 +387,206 @@ __global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(DeltaRecArgs a)
                     }
         }
         __syncthreads();
-        // ---- P5: O += Mq D (3 split products), store O; decayed keys into Qh.
+        // ---- P5: O += Mq D (3 split products); write O (or its gated norm); decayed keys.
         {
-            const int nb = warp * 32;
 #pragma unroll
             for (int k0 = 0; k0 < C; k0 += 16) {
+                uint32_t dh[4], dl[4];
+                frag_b_kn<LDH>(dh, sm.Vh, k0, nb, lane);
+                frag_b_kn<LDH>(dl, sm.Vl, k0, nb, lane);
 #pragma unroll
                 for (int mt = 0; mt < 2; ++mt) {
                     uint32_t mh[4], ml[4];
                     frag_a<LDC>(mh, sm.Mh, mt * 16, k0, lane);
                     frag_a<LDC>(ml, sm.Ml, mt * 16, k0, lane);
-#pragma unroll
-                    for (int n0 = 0; n0 < 32; n0 += 16) {
-                        uint32_t dh[4], dl[4];
-                        frag_b_kn<LDH>(dh, sm.Vh, k0, nb + n0, lane);
-                        frag_b_kn<LDH>(dl, sm.Vl, k0, nb + n0, lane);
-                        mma(o[mt][n0 / 8], mh, dh[0], dh[1]);
-                        mma(o[mt][n0 / 8 + 1], mh, dh[2], dh[3]);
-                        mma(o[mt][n0 / 8], mh, dl[0], dl[1]);
-                        mma(o[mt][n0 / 8 + 1], mh, dl[2], dl[3]);
-                        mma(o[mt][n0 / 8], ml, dh[0], dh[1]);
-                        mma(o[mt][n0 / 8 + 1], ml, dh[2], dh[3]);
-                    }
+                    mma(o[mt][0], mh, dh[0], dh[1]);
+                    mma(o[mt][1], mh, dh[2], dh[3]);
+                    mma(o[mt][0], mh, dl[0], dl[1]);
+                    mma(o[mt][1], mh, dl[2], dl[3]);
+                    mma(o[mt][0], ml, dh[0], dh[1]);
+                    mma(o[mt][1], ml, dh[2], dh[3]);
                 }
             }
+            if (!GATED_OUT) {
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
+                for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt)
+                    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                        for (int hf = 0; hf < 2; ++hf) {
+                            const int t = mt * 16 + g4 + hf * 8;
+                            if (t < n) {
+                                const int c = nb + nt * 8 + 2 * t4;
+                                *reinterpret_cast<float2 *>(a.out + (static_cast<size_t>(c0 + t) * a.nv + h) * D + c) =
+                                    make_float2(o[mt][nt][2 * hf], o[mt][nt][2 * hf + 1]);
+                            }
+                        }
+            } else {
+                // Row sums of squares: this warp's 16 columns, reduced over the 4 lanes
+                // of a row group, then over the 8 warps in a fixed order.
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
                     for (int hf = 0; hf < 2; ++hf) {
-                        const int t = mt * 16 + g4 + hf * 8;
-                        if (t < n) {
-                            const int c = nb + nt * 8 + 2 * t4;
-                            *reinterpret_cast<float2 *>(a.out + (static_cast<size_t>(c0 + t) * a.nv + h) * D + c) =
-                                make_float2(o[mt][nt][2 * hf], o[mt][nt][2 * hf + 1]);
-                        }
+                        float ss = 0.f;
+#pragma unroll
+                        for (int nt = 0; nt < 2; ++nt)
+                            ss += o[mt][nt][2 * hf] * o[mt][nt][2 * hf] + o[mt][nt][2 * hf + 1] * o[mt][nt][2 * hf + 1];
+                        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                        if (t4 == 0) sm.red[warp][mt * 16 + g4 + hf * 8] = ss;
                     }
+            }
             const float gl = sm.G[C - 1];
-            for (int e = tid; e < C * D; e += THREADS) {
-                const int r = e / D, c = e % D;
-                const float kv = __half2float(sm.Kh[r][c]) + __half2float(sm.Kl[r][c]);
-                sm.Qh[r][c] = __float2half_rn(expf(gl - sm.G[r]) * kv);
+            for (int e = tid; e < C * (D / 4); e += THREADS) {
+                const int r = e / (D / 4), c = (e % (D / 4)) * 4;
+                float kd[4];
+                const float dec = expf(gl - sm.G[r]);
+#pragma unroll
+                for (int u2 = 0; u2 < 4; ++u2)
+                    kd[u2] = dec * (__half2float(sm.Kh[r][c + u2]) + __half2float(sm.Kl[r][c + u2]));
+                store4(&sm.Qh[r][c], kd);
             }
         }
         __syncthreads();
-        // ---- P6: S = gam_C S + Kdec^T D (D hi+lo); warp w owns key rows 32w..32w+31.
-        {
-            const float gc = sm.gam[C - 1];
+        if (GATED_OUT) {
+            // rms(o) * w * silu(z) -> fp16 out_proj input.
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int nt = 0; nt < 16; ++nt)
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int t = mt * 16 + g4 + hf * 8;
+                    if (t >= n) continue;
+                    float ss = 0.f;
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) S[mt][nt][e] *= gc;
+                    for (int w8 = 0; w8 < WARPS; ++w8) ss += sm.red[w8][t];
+                    const float denom = sqrtf(ss / static_cast<float>(D) + a.eps);
+                    const size_t tok = static_cast<size_t>(c0 + t);
+                    const float *z = a.proj + tok * a.ldp + conv_dim + h * D;
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        const int c = nb + nt * 8 + 2 * t4;
+                        const float2 zz = *reinterpret_cast<const float2 *>(z + c);
+                        const float y0 = ((o[mt][nt][2 * hf] / denom) * a.norm_w[c]) * silu_f(zz.x);
+                        const float y1 = ((o[mt][nt][2 * hf + 1] / denom) * a.norm_w[c + 1]) * silu_f(zz.y);
+                        *reinterpret_cast<__half2 *>(a.mix + tok * a.ldmix + h * D + c) = __floats2half2_rn(y0, y1);
+                    }
+                }
+        }
+        // ---- P6: S = gam_C S + Kdec^T D (D hi+lo); warp w owns key rows 16w..16w+15.
+        {
+            const float gc = sm.gam[C - 1];
+#pragma unroll
+            for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) S[nt][e] *= gc;
 #pragma unroll
             for (int k0 = 0; k0 < C; k0 += 16) {
-                uint32_t ak[2][4];
-                frag_at<LDH>(ak[0], sm.Qh, warp * 32, k0, lane);
-                frag_at<LDH>(ak[1], sm.Qh, warp * 32 + 16, k0, lane);
+                uint32_t ak[4];
+                frag_at<LDH>(ak, sm.Qh, warp * 16, k0, lane);
 #pragma unroll
                 for (int n0 = 0; n0 < D; n0 += 16) {
                     uint32_t dh[4], dl[4];
                     frag_b_kn<LDH>(dh, sm.Vh, k0, n0, lane);
                     frag_b_kn<LDH>(dl, sm.Vl, k0, n0, lane);
-#pragma unroll
-                    for (int mt = 0; mt < 2; ++mt) {
-                        mma(S[mt][n0 / 8], ak[mt], dh[0], dh[1]);
-                        mma(S[mt][n0 / 8 + 1], ak[mt], dh[2], dh[3]);
-                        mma(S[mt][n0 / 8], ak[mt], dl[0], dl[1]);
-                        mma(S[mt][n0 / 8 + 1], ak[mt], dl[2], dl[3]);
-                    }
+                    mma(S[n0 / 8], ak, dh[0], dh[1]);
+                    mma(S[n0 / 8 + 1], ak, dh[2], dh[3]);
+                    mma(S[n0 / 8], ak, dl[0], dl[1]);
+                    mma(S[n0 / 8 + 1], ak, dl[2], dl[3]);
                 }
             }
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
+            for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
-                for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-                        const int r = warp * 32 + mt * 16 + g4 + hf * 8, c = nt * 8 + 2 * t4;
-                        *reinterpret_cast<__half2 *>(&sm.S[r][c]) =
-                            __floats2half2_rn(S[mt][nt][2 * hf], S[mt][nt][2 * hf + 1]);
-                    }
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int r = warp * 16 + g4 + hf * 8, c = nt * 8 + 2 * t4;
+                    *reinterpret_cast<__half2 *>(&sm.S[r][c]) = __floats2half2_rn(S[nt][2 * hf], S[nt][2 * hf + 1]);
+                }
         }
         __syncthreads();
     }
+}
+
+template <bool FP, bool GO>
+void launch_kernel(const ChunkArgs &a, cudaStream_t s) {
+    const size_t smem = sizeof(Smem);
+    static bool set[64] = {};
+    int dev = 0;
+    HK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !set[dev]) {
+        HK_CUDA(cudaFuncSetAttribute(delta_chunk_kernel<FP, GO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)));
+        if (dev >= 0 && dev < 64) set[dev] = true;
+    }
+    dim3 grid(a.n_rows, a.nv);
+    delta_chunk_kernel<FP, GO><<<grid, THREADS, smem, s>>>(a);
+    HK_LAUNCH_CHECK();
 }
 
 }  // namespace
 
 bool delta_chunk_supported(const DeltaRecArgs &a) { return a.dk == D && a.dv == D && (a.nv % a.nk) == 0; }
 
-void launch_delta_chunk(const DeltaRecArgs &a, cudaStream_t s) {
-    if (a.n_rows <= 0) return;
-    const size_t smem = sizeof(Smem);
-    static bool set[64] = {};
-    int dev = 0;
-    HK_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(delta_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(smem)));
-        if (dev >= 0 && dev < 64) set[dev] = true;
-    }
-    dim3 grid(a.n_rows, a.nv);
-    delta_chunk_kernel<<<grid, THREADS, smem, s>>>(a);
-    HK_LAUNCH_CHECK();
+void launch_delta_chunk(const DeltaRecArgs &r, cudaStream_t s) {
+    if (r.n_rows <= 0) return;
+    ChunkArgs a{};
+    a.q = r.q;
+    a.k = r.k;
+    a.v = r.v;
+    a.g = r.g;
+    a.beta = r.beta;
+    a.cu_seqlens = r.cu_seqlens;
+    a.n_rows = r.n_rows;
+    a.nk = r.nk;
+    a.nv = r.nv;
+    a.out = r.out;
+    launch_kernel<false, false>(a, s);
+}
+
+void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp, const float *norm_w, float eps,
+                              __half *mix, int ldmix, cudaStream_t s) {
+    if (r.n_rows <= 0) return;
+    ChunkArgs a{};
+    a.q = r.q;
+    a.k = r.k;
+    a.v = r.v;
+    a.g = r.g;
+    a.beta = r.beta;
+    a.proj = proj;
+    a.ldp = ldp;
+    a.cu_seqlens = r.cu_seqlens;
+    a.n_rows = r.n_rows;
+    a.nk = r.nk;
+    a.nv = r.nv;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    a.mix = mix;
+    a.ldmix = ldmix;
+    launch_kernel<false, true>(a, s);
+}
+
+bool delta_layer_fused_supported(const DeltaPrepArgs &p) {
+    return p.dk == D && p.dv == D && p.taps == 4 && (p.nv % p.nk) == 0 && (p.ldp % 4) == 0;
+}
+
+void launch_delta_layer_fused(const DeltaPrepArgs &p, const int32_t *cu_seqlens, int n_rows, const float *norm_w,
+                              float eps, __half *mix, int ldmix, cudaStream_t s) {
+    if (n_rows <= 0) return;
+    ChunkArgs a{};
+    a.proj = p.proj;
+    a.ldp = p.ldp;
+    a.conv_w = p.conv_w;
+    a.base_g = p.base_g;
+    a.dt_bias = p.dt_bias;
+    a.cu_seqlens = cu_seqlens;
+    a.n_rows = n_rows;
+    a.nk = p.nk;
+    a.nv = p.nv;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    a.mix = mix;
+    a.ldmix = ldmix;
+    launch_kernel<true, true>(a, s);
 }
 
 }  // namespace hk

@@ -651,6 +651,12 @@ struct Model {
         prof_end(ev, 0, 2.0 * M * W.rows * W.cols);
     }
 
+    // Algorithmic FLOPs of the chunked delta rule (chunk 32) for n tokens of one layer.
+    static double delta_chunk_flops(int n, const KevConfig &c) {
+        const double C = 32.0;
+        return static_cast<double>(c.nv) * n * (2.0 * C * (c.dk + c.dv) + 6.0 * c.dk * c.dv);
+    }
+
     // The forward over a packed batch whose description is already on the
     // device in `meta` (layout: see MetaLayout).
     void forward(int n_rows, int n_tok, int max_len, int n_opt, const uint32_t *ids,
@@ -686,30 +692,54 @@ struct Model {
                 d.v = dvv;
                 d.g = dg;
                 d.beta = db;
-                ev = prof_begin();
-                launch_delta_prep(d, stream);
-                prof_end(ev, 3, 0);
-                DeltaRecArgs r;
-                r.q = dq;
-                r.k = dkk;
-                r.v = dvv;
-                r.g = dg;
-                r.beta = db;
-                r.cu_seqlens = cu_seqlens;
-                r.n_rows = n_rows;
-                r.nk = c.nk;
-                r.nv = c.nv;
-                r.dk = c.dk;
-                r.dv = c.dv;
-                r.out = dout;
-                r.exact = dtype == HK_DTYPE_FP32;
-                ev = prof_begin();
-                launch_delta_recurrent(r, stream);
-                prof_end(ev, 1, 4.0 * n_tok * c.nv * c.dk * c.dv);
-                ev = prof_begin();
-                launch_gated_norm(A, dout, proj + c.conv_dim(), ldp, L.gnorm_w, c.eps, n_tok, c.nv, c.dv, mix, ldmix,
-                                  stream);
-                prof_end(ev, 4, 0);
+                if (dtype != HK_DTYPE_FP32 && delta_layer_fused_supported(d)) {
+                    // Input stage, then the chunked recurrence with the gated norm fused.
+                    ev = prof_begin();
+                    launch_delta_prep(d, stream);
+                    prof_end(ev, 3, 0);
+                    DeltaRecArgs r;
+                    r.q = dq;
+                    r.k = dkk;
+                    r.v = dvv;
+                    r.g = dg;
+                    r.beta = db;
+                    r.cu_seqlens = cu_seqlens;
+                    r.n_rows = n_rows;
+                    r.nk = c.nk;
+                    r.nv = c.nv;
+                    r.dk = c.dk;
+                    r.dv = c.dv;
+                    r.out = dout;
+                    r.exact = 0;
+                    ev = prof_begin();
+                    launch_delta_chunk_gated(r, proj, ldp, L.gnorm_w, c.eps, static_cast<__half *>(mix), ldmix, stream);
+                    prof_end(ev, 1, delta_chunk_flops(n_tok, c));
+                } else {
+                    ev = prof_begin();
+                    launch_delta_prep(d, stream);
+                    prof_end(ev, 3, 0);
+                    DeltaRecArgs r;
+                    r.q = dq;
+                    r.k = dkk;
+                    r.v = dvv;
+                    r.g = dg;
+                    r.beta = db;
+                    r.cu_seqlens = cu_seqlens;
+                    r.n_rows = n_rows;
+                    r.nk = c.nk;
+                    r.nv = c.nv;
+                    r.dk = c.dk;
+                    r.dv = c.dv;
+                    r.out = dout;
+                    r.exact = dtype == HK_DTYPE_FP32;
+                    ev = prof_begin();
+                    launch_delta_recurrent(r, stream);
+                    prof_end(ev, 1, 4.0 * n_tok * c.nv * c.dk * c.dv);
+                    ev = prof_begin();
+                    launch_gated_norm(A, dout, proj + c.conv_dim(), ldp, L.gnorm_w, c.eps, n_tok, c.nv, c.dv, mix, ldmix,
+                                      stream);
+                    prof_end(ev, 4, 0);
+                }
             } else {
                 AttnPrepArgs p;
                 p.proj = proj;
