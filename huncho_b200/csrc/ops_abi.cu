@@ -1,5 +1,6 @@
 // Kernel-level C entry points (include/huncho_kev_ops.h) for per-kernel
 // parity tests and timing.
+#include <cmath>
 #include <string>
 
 #include "../../include/huncho_kev.h"
@@ -102,6 +103,32 @@ int hk_op_attention(int act, const void *q, const void *k, const void *v, const 
         a.out = out;
         a.ldo = ldo;
         hk::launch_attention(act, a, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int hk_op_readout(const float *x, int hidden, const float *final_w, float eps, const int32_t *idx,
+                  const int32_t *opt_dec, int n_dec, int n_opt, const float *wq, const float *bq, const float *wk,
+                  const float *bk, int dp, float *hn, float *proj, float *logits, void *stream) {
+    return op_guard([&] {
+        hk::ReadoutArgs a;
+        a.x = x;
+        a.hidden = hidden;
+        a.final_w = final_w;
+        a.eps = eps;
+        a.idx = idx;
+        a.opt_dec = opt_dec;
+        a.n_dec = n_dec;
+        a.n_opt = n_opt;
+        a.wq = wq;
+        a.bq = bq;
+        a.wk = wk;
+        a.bk = bk;
+        a.dp = dp;
+        a.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dp)));
+        a.hn = hn;
+        a.proj = proj;
+        a.logits = logits;
+        hk::launch_readout(a, static_cast<cudaStream_t>(stream));
     });
 }
 

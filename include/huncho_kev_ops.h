@@ -40,6 +40,18 @@ int hk_op_attention(int act, const void *q, const void *k, const void *v, const 
                     const int32_t *cu_seqlens, const int32_t *tok_row, int n, int n_rows, int max_len,
                     int nh, int nkv, int hd, void *out, int ldo, void *stream);
 
+/* Pointer-head readout (qwen3_5.rs:3196-3255, kev.rs:169-173) over device
+ * buffers: rows idx[0..n_dec) are decision tokens and idx[n_dec..n_dec+n_opt)
+ * option tokens of the fp32 residual stream x [*, hidden] (before the final
+ * norm); each row is RMS-normalised with final_w (effective weight), decision
+ * rows projected by wq/bq and option rows by wk/bk ([dp, hidden], [dp], fp32),
+ * and logits[j] = k_j . q_{opt_dec[j]} / sqrt(dp). Scratch (caller-owned):
+ * hn [n_dec + n_opt, hidden] and proj [n_dec + n_opt, dp], fp32. */
+int hk_op_readout(const float *x, int hidden, const float *final_w, float eps, const int32_t *idx,
+                  const int32_t *opt_dec, int n_dec, int n_opt, const float *wq, const float *bq,
+                  const float *wk, const float *bk, int dp, float *hn, float *proj, float *logits,
+                  void *stream);
+
 /* Number of SMs the GEMM grid is sized for on the current device. */
 int hk_op_num_sms(void);
 

@@ -219,3 +219,40 @@ def test_attention_vs_torch(lib, act, hd):
     ref = _attn_ref(q.float(), k.float(), v.float(), proj.float()[:, :, hd:], lens, nh, nkv)
     tol = 1e-5 if act == 0 else 5e-3
     torch.testing.assert_close(out.float(), ref, rtol=tol, atol=tol)
+
+
+def _readout_inputs(g, n_tok, hidden, dp, n_dec, n_opt):
+    x = torch.randn(n_tok, hidden, device="cuda", generator=g)
+    w = 1.0 + 0.1 * torch.rand(hidden, device="cuda", generator=g)
+    wq = torch.randn(dp, hidden, device="cuda", generator=g) * 0.02
+    wk = torch.randn(dp, hidden, device="cuda", generator=g) * 0.02
+    bq = torch.randn(dp, device="cuda", generator=g) * 0.02
+    bk = torch.randn(dp, device="cuda", generator=g) * 0.02
+    idx = torch.randint(0, n_tok, (n_dec + n_opt,), device="cuda", generator=g, dtype=torch.int64).int()
+    opt_dec = torch.randint(0, n_dec, (n_opt,), device="cuda", generator=g, dtype=torch.int64).int()
+    return x, w, wq, bq, wk, bk, idx, opt_dec
+
+
+def _readout_ref(x, w, wq, bq, wk, bk, idx, opt_dec, n_dec, eps, dp):
+    rows = x[idx.long()]
+    hn = rows / torch.sqrt((rows * rows).mean(-1, keepdim=True) + eps) * w
+    q = hn[:n_dec] @ wq.T + bq
+    k = hn[n_dec:] @ wk.T + bk
+    return (k * q[opt_dec.long()]).sum(-1) / dp ** 0.5
+
+
+def test_readout_vs_torch(lib):
+    g = torch.Generator(device="cuda").manual_seed(21)
+    n_tok, hidden, dp, n_dec, n_opt = 700, 1024, 256, 40, 150
+    x, w, wq, bq, wk, bk, idx, opt_dec = _readout_inputs(g, n_tok, hidden, dp, n_dec, n_opt)
+    hn = torch.empty(n_dec + n_opt, hidden, device="cuda")
+    proj = torch.empty(n_dec + n_opt, dp, device="cuda")
+    logits = torch.empty(n_opt, device="cuda")
+    lib.hk_op_readout.argtypes = ([ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_float] + [ctypes.c_void_p] * 2
+                                  + [ctypes.c_int] * 2 + [ctypes.c_void_p] * 4 + [ctypes.c_int] + [ctypes.c_void_p] * 4)
+    rc = lib.hk_op_readout(_p(x), hidden, _p(w), 1e-6, _p(idx), _p(opt_dec), n_dec, n_opt, _p(wq), _p(bq), _p(wk),
+                           _p(bk), dp, _p(hn), _p(proj), _p(logits), None)
+    assert rc == 0, lib.hk_op_last_error()
+    torch.cuda.synchronize()
+    ref = _readout_ref(x, w, wq, bq, wk, bk, idx, opt_dec, n_dec, 1e-6, dp)
+    torch.testing.assert_close(logits, ref, rtol=1e-4, atol=1e-5)
