@@ -82,4 +82,7 @@ __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf
 
 inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }
 
+// Sets the message hk_op_last_error() returns on the calling thread.
+void set_op_error(const std::string &msg);
+
 }  // namespace hk

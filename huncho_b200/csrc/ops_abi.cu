@@ -33,6 +33,11 @@ int current_sms() {
 }
 }  // namespace
 
+namespace hk {
+// Record the calling thread's kernel-level entry-point error (hk_op_last_error).
+void set_op_error(const std::string &msg) { tl_op_error = msg; }
+}  // namespace hk
+
 extern "C" {
 
 int hk_op_gemm(int dtype, int epilogue, int M, int N, int K, const void *x, int ldx, const void *w, int ldw,

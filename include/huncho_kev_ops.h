@@ -52,6 +52,22 @@ int hk_op_readout(const float *x, int hidden, const float *final_w, float eps, c
                   const float *wk, const float *bk, int dp, float *hn, float *proj, float *logits,
                   void *stream);
 
+/* hk_op_readout without scratch arguments and without allocating: for callers
+ * that cannot call cudaMalloc (a host that hands this library only device
+ * memory planned ahead from its own pool, or a latency-critical serving loop
+ * where cudaMalloc's implicit device synchronisation would stall other GPU
+ * work). Its scratch is a library-owned 16 MiB __device__ array that every GPU
+ * loading the library holds until exit; limits: n_dec + n_opt <= 1024,
+ * hidden <= 3584, dp <= 512 (beyond them: HK_ERR_ARGUMENT, message in
+ * hk_op_last_error). The first call on each device looks up the array's
+ * device address (call it before any stream capture). All calls share the
+ * array, so calls that overlap on the GPU race. No counterpart in the
+ * reference (its readout is a CPU/candle tensor expression). */
+int hk_op_readout_noalloc(const float *x, int hidden, const float *final_w, float eps,
+                          const int32_t *idx, const int32_t *opt_dec, int n_dec, int n_opt,
+                          const float *wq, const float *bq, const float *wk, const float *bk,
+                          int dp, float *logits, void *stream);
+
 /* Number of SMs the GEMM grid is sized for on the current device. */
 int hk_op_num_sms(void);
 
