@@ -97,6 +97,16 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+WORKLOADS = {
+    1: "cfg1: Kev-0.8B {dtype}, {n} request x 256 tokens, one 4-option choice",
+    2: "cfg2: Kev-0.8B {dtype}, {n} requests per GPU x 3 questions (choice-4, noul, score-5), lengths U[64,512], "
+       "packed varlen",
+    3: "cfg3: Kev-0.8B int8 per-channel weights, {n} requests per GPU x 1024 tokens, 8-option choice",
+    4: "cfg4: Kev-0.8B {dtype}, {n} requests per GPU x 8192 tokens, noul; KV in 16-token pages, shuffled block table",
+    5: "cfg5: Kev-4B {dtype}, {n} requests per GPU, lengths log-uniform [32, 2048], mixed questions",
+}
+
+
 def groups_of(rows, limit=64):
     """Split rows into the fewest native batches of at most `limit` rows, equal-sized."""
     n = len(rows)
@@ -219,6 +229,8 @@ def main():
                              n_requests=args.requests)
     max_len = max(len(r) for r in wl.rows)
     backend = KevBackend(d, device=local, dtype=dtype, max_context=max(8192, max_len))
+    if args.config == 4:
+        backend.with_kv_page_tokens(16, shuffle_seed=1 + rank)  # 16-token pages, shuffled block table
 
     groups = groups_of(wl.rows, backend.batch_limits().max_rows)
     packed = []
@@ -229,7 +241,10 @@ def main():
         packed.append((g, tok, cu, pos, cup, dev))
     n_tok = wl.n_tokens
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
-    stream = torch.cuda.current_stream()
+    # A dedicated stream: the forward, the L2 flush and the timing events all
+    # run on it (the legacy default stream has no handle to pass).
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
 
     def device_step():
         for g, tok, cu, pos, cup, dev in packed:
@@ -316,9 +331,9 @@ def main():
         "prompt_tokens_per_s": toks_all * args.steps / dev_total_s,
         "p50_request_latency_ms": statistics.median(step_ms),
         "p50_single_request_latency_ms": 1000.0 * statistics.median(lat),
-        "config": {"workload": f"cfg{args.config}: Kev-{name[4:]} {dtype}, {wl.n_requests} requests per GPU x "
-                               f"{len(wl.rows) // wl.n_requests} questions (choice-4, noul, score-5), lengths "
-                               "U[64,512], packed varlen", "model": name, "rows_per_step": len(wl.rows) * world,
+        "step_ms": [round(x, 3) for x in step_ms],
+        "config": {"workload": WORKLOADS[args.config].format(n=wl.n_requests, dtype=dtype), "model": name,
+                   "rows_per_step": len(wl.rows) * world,
                    "tokens_per_step": toks_all, "native_batches_per_step": len(groups),
                    "l2": "flushed between steps (256 MiB write, outside the timed events); weights 1 GB > L2",
                    "parallelism": f"replicas x{world}"},

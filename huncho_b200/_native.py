@@ -22,7 +22,8 @@ HK_MAX_ROWS = 64
 
 EXPORTED = (
     "hk_create", "hk_replica", "hk_capabilities_get", "hk_score", "hk_score_device",
-    "hk_synchronize", "hk_kernel_launches", "hk_profile_enable", "hk_profile_read", "hk_last_error",
+    "hk_synchronize", "hk_kernel_launches", "hk_set_kv_page_tokens", "hk_profile_enable", "hk_profile_read",
+    "hk_last_error",
     "hk_create_error", "hk_destroy",
 )
 
@@ -64,6 +65,8 @@ def load(path: Path | None = None) -> ctypes.CDLL:
     lib.hk_synchronize.restype = i32
     lib.hk_kernel_launches.argtypes = [vp]
     lib.hk_kernel_launches.restype = ctypes.c_uint64
+    lib.hk_set_kv_page_tokens.argtypes = [vp, i32, ctypes.c_uint64]
+    lib.hk_set_kv_page_tokens.restype = i32
     lib.hk_profile_enable.argtypes = [vp, i32]
     lib.hk_profile_enable.restype = i32
     lib.hk_profile_read.argtypes = [vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),

@@ -135,6 +135,12 @@ class KevBackend:
         KevBackend.__init__(r, self.model_dir, dev, self.dtype, self.max_context, _handle=h)
         return r
 
+    def with_kv_page_tokens(self, tokens: int, shuffle_seed: int = 0) -> "KevBackend":
+        """Qwen3_5Backend::with_kv_page_tokens (qwen3_5.rs:1773-1809): 0 or a power
+        of two in 16..256; a nonzero seed shuffles the pages' block table."""
+        self._check(self._lib.hk_set_kv_page_tokens(self._h, int(tokens), int(shuffle_seed)))
+        return self
+
     def supports_batch(self) -> bool:
         return True
 

@@ -8,6 +8,8 @@
 // query rows; key/value tiles of 64 keys stream through shared memory with
 // cp.async; scores, online softmax state and the output accumulator stay in
 // registers. Rows are packed (cu_seqlens), so no padding is ever computed.
+// Keys and values are read through kv_slot(): flat, or fixed-size pages in
+// block-table order (the same math, kv_pages.rs:36-103).
 #include <math.h>
 
 #include "common.cuh"
@@ -100,7 +102,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(AttnArgs a) {
             const int r = i / CH, c = i % CH;
             const int ki = kv0 + r;
             const bool ok = ki < len;
-            const size_t off = (static_cast<size_t>(start + (ok ? ki : 0)) * a.nkv + kh) * HD + c * 8;
+            const int kvs = kv_slot(a.pages, row, start, ok ? ki : 0);
+            const size_t off = (static_cast<size_t>(kvs) * a.nkv + kh) * HD + c * 8;
             cp_async16(sK + r * LD + c * 8, K + off, ok);
             cp_async16(sV + r * LD + c * 8, V + off, ok);
         }

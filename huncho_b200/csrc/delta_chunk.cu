@@ -130,6 +130,7 @@ struct ChunkArgs {
     int ldp;
     const float *conv_w, *base_g, *dt_bias;
     const int32_t *cu_seqlens;
+    const int32_t *row_order;  // CTA x handles row row_order[x] (longest rows first), or x
     int n_rows, nk, nv;
     float *out;           // !GATED_OUT: o [n, nv, 128] fp32
     const float *norm_w;  // GATED_OUT: gated-norm weight [128]
@@ -143,7 +144,9 @@ template <bool FROM_PROJ, bool GATED_OUT>
 __global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(ChunkArgs a) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
-    const int row = blockIdx.x, h = blockIdx.y;
+    // Rows run longest first (row_order), so the grid's last wave is made of
+    // the shortest rows.
+    const int row = a.row_order ? a.row_order[blockIdx.x] : blockIdx.x, h = blockIdx.y;
     const int start = a.cu_seqlens[row], end = a.cu_seqlens[row + 1];
     if (start >= end) return;
     const int kh = h / (a.nv / a.nk);
@@ -536,6 +539,7 @@ void launch_delta_chunk(const DeltaRecArgs &r, cudaStream_t s) {
     a.g = r.g;
     a.beta = r.beta;
     a.cu_seqlens = r.cu_seqlens;
+    a.row_order = r.row_order;
     a.n_rows = r.n_rows;
     a.nk = r.nk;
     a.nv = r.nv;
@@ -555,6 +559,7 @@ void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp,
     a.proj = proj;
     a.ldp = ldp;
     a.cu_seqlens = r.cu_seqlens;
+    a.row_order = r.row_order;
     a.n_rows = r.n_rows;
     a.nk = r.nk;
     a.nv = r.nv;

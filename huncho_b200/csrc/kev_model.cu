@@ -336,6 +336,34 @@ struct Model {
     void *pinned = nullptr;
     size_t pinned_cap = 0;
     int ld_xn = 0, ldp = 0, ldmix = 0, ldf = 0;
+    // KV pages (0 = flat K/V) and the page-order shuffle seed (0 = in order).
+    int kv_page_tokens = 0;
+    uint64_t kv_shuffle_seed = 0;
+    int kv_slot_cap = 0;  // K/V slots the ak/av buffers hold
+    std::vector<int32_t> row_order;  // host copy of the last batch's row order
+    // Pinned host staging for the small per-batch uploads of the device-input
+    // path (a ring, so a buffer is reused only after its copy has completed).
+    struct HostStage {
+        uint8_t *p = nullptr;
+        size_t cap = 0;
+        cudaEvent_t done = nullptr;
+    };
+    HostStage stages[4];
+    int stage_next = 0;
+    HostStage &stage_acquire(size_t bytes) {
+        HostStage &st = stages[stage_next];
+        stage_next = (stage_next + 1) % 4;
+        if (st.done) HK_CUDA(cudaEventSynchronize(st.done));
+        if (bytes > st.cap) {
+            if (st.p) cudaFreeHost(st.p);
+            st.p = nullptr;
+            st.cap = 0;
+            HK_CUDA(cudaHostAlloc(reinterpret_cast<void **>(&st.p), bytes * 2, cudaHostAllocDefault));
+            st.cap = bytes * 2;
+        }
+        if (!st.done) HK_CUDA(cudaEventCreateWithFlags(&st.done, cudaEventDisableTiming));
+        return st;
+    }
     uint64_t launches = 0;
     std::string last_error;
 
@@ -391,6 +419,10 @@ struct Model {
             cudaEventDestroy(r.b);
         }
         for (auto e : prof_pool) cudaEventDestroy(e);
+        for (auto &st : stages) {
+            if (st.p) cudaFreeHost(st.p);
+            if (st.done) cudaEventDestroy(st.done);
+        }
         for (void *p : ws) cudaFree(p);
         for (void *p : allocs) cudaFree(p);
         if (pinned) cudaFreeHost(pinned);
@@ -620,12 +652,14 @@ struct Model {
         db = dev_alloc<float>(N * c.nv, ws);
         dout = dev_alloc<float>(N * c.value_dim(), ws);
         aq = dev_alloc<uint8_t>(N * c.nh * c.hd * e, ws);
-        ak = dev_alloc<uint8_t>(N * c.nkv * c.hd * e, ws);
-        av = dev_alloc<uint8_t>(N * c.nkv * c.hd * e, ws);
+        // Paged K/V needs up to page_tokens - 1 padding slots per row.
+        kv_slot_cap = static_cast<int>(N) + cap_rows * std::max(kv_page_tokens, 1);
+        ak = dev_alloc<uint8_t>(static_cast<size_t>(kv_slot_cap) * c.nkv * c.hd * e, ws);
+        av = dev_alloc<uint8_t>(static_cast<size_t>(kv_slot_cap) * c.nkv * c.hd * e, ws);
         hn = dev_alloc<float>(R * c.hidden, ws);
         rproj = dev_alloc<float>(R * dp, ws);
         logits = dev_alloc<float>(R, ws);
-        meta_cap = 4 * N + 4 * static_cast<size_t>(cap_rows) + 4 * R + 64;
+        meta_cap = 4 * N + 6 * static_cast<size_t>(cap_rows) + 4 * R + 64 + N;  // + block table
         meta = dev_alloc<int32_t>(meta_cap, ws);
     }
 
@@ -661,7 +695,8 @@ struct Model {
     // device in `meta` (layout: see MetaLayout).
     void forward(int n_rows, int n_tok, int max_len, int n_opt, const uint32_t *ids,
                  const int32_t *cu_seqlens, const int32_t *pos, const int32_t *tok_row,
-                 const int32_t *ridx, const int32_t *opt_dec, float *out_logits) {
+                 const int32_t *ridx, const int32_t *opt_dec, float *out_logits, const KvPages &pages,
+                 const int32_t *row_order) {
         const KevConfig &c = cfg;
         const int A = act();
         const size_t e = esz();
@@ -704,6 +739,7 @@ struct Model {
                     r.g = dg;
                     r.beta = db;
                     r.cu_seqlens = cu_seqlens;
+                    r.row_order = row_order;
                     r.n_rows = n_rows;
                     r.nk = c.nk;
                     r.nv = c.nv;
@@ -725,6 +761,7 @@ struct Model {
                     r.g = dg;
                     r.beta = db;
                     r.cu_seqlens = cu_seqlens;
+                    r.row_order = row_order;
                     r.n_rows = n_rows;
                     r.nk = c.nk;
                     r.nv = c.nv;
@@ -745,6 +782,8 @@ struct Model {
                 p.proj = proj;
                 p.ldp = ldp;
                 p.pos = pos;
+                p.tok_row = tok_row;
+                p.pages = pages;
                 p.n = n_tok;
                 p.nh = c.nh;
                 p.nkv = c.nkv;
@@ -776,6 +815,7 @@ struct Model {
                 at.hd = c.hd;
                 at.out = mix;
                 at.ldo = ldmix;
+                at.pages = pages;
                 ev = prof_begin();
                 launch_attention(A, at, stream);
                 prof_end(ev, 2, 0);
@@ -824,8 +864,8 @@ struct Model {
 //   pos[N] | tok_row[N] | ridx[R + P] | opt_dec[P]                  (derived)
 // ridx lists the decision token of every row, then every option token.
 struct MetaLayout {
-    size_t ids, cu, positions, cu_pos, pos, tok_row, ridx, opt_dec, total;
-    MetaLayout(int rows, int n, int p) {
+    size_t ids, cu, positions, cu_pos, pos, tok_row, ridx, opt_dec, row_order, cu_pages, table, total;
+    MetaLayout(int rows, int n, int p, int n_pages = 0) {
         ids = 0;
         cu = ids + n;
         positions = cu + rows + 1;
@@ -834,9 +874,42 @@ struct MetaLayout {
         tok_row = pos + n;
         ridx = tok_row + n;
         opt_dec = ridx + rows + p;
-        total = opt_dec + p;
+        row_order = opt_dec + p;
+        cu_pages = row_order + rows;
+        table = cu_pages + rows + 1;
+        total = table + n_pages;
     }
 };
+
+// Host-side page plan for a batch: per-row page offsets and a block table that
+// places every page of every row in a distinct pool page. With a nonzero
+// seed the pool order is a deterministic pseudo-random permutation (the
+// shuffled block table of the long-context stress configuration).
+struct PagePlan {
+    std::vector<int32_t> cu_pages, table;
+};
+PagePlan plan_pages(const int32_t *cu_h, int n_rows, int page_tokens, uint64_t seed) {
+    PagePlan pp;
+    pp.cu_pages.assign(n_rows + 1, 0);
+    for (int r = 0; r < n_rows; ++r) {
+        const int len = cu_h[r + 1] - cu_h[r];
+        pp.cu_pages[r + 1] = pp.cu_pages[r] + (len + page_tokens - 1) / page_tokens;
+    }
+    const int n = pp.cu_pages[n_rows];
+    pp.table.resize(n);
+    for (int i = 0; i < n; ++i) pp.table[i] = i;
+    if (seed) {
+        uint64_t x = seed * 0x9E3779B97F4A7C15ull + 1;
+        for (int i = n - 1; i > 0; --i) {
+            x ^= x << 13;
+            x ^= x >> 7;
+            x ^= x << 17;
+            const int j = static_cast<int>(x % static_cast<uint64_t>(i + 1));
+            std::swap(pp.table[i], pp.table[j]);
+        }
+    }
+    return pp;
+}
 
 namespace {
 
@@ -985,12 +1058,49 @@ static int score_device_impl(hk::Model &m, int n_rows, const int32_t *cu_h, cons
     const int n = cu_h[n_rows], p = cup_h[n_rows];
     int max_len = 0;
     for (int r = 0; r < n_rows; ++r) max_len = std::max(max_len, cu_h[r + 1] - cu_h[r]);
-    hk::MetaLayout L(n_rows, n, p);
+    hk::KvPages pages;
+    hk::PagePlan plan;
+    if (m.kv_page_tokens > 0) plan = hk::plan_pages(cu_h, n_rows, m.kv_page_tokens, m.kv_shuffle_seed);
+    const int n_pages = static_cast<int>(plan.table.size());
+    hk::MetaLayout L(n_rows, n, p, n_pages);
+    if (m.kv_page_tokens > 0) {
+        if (static_cast<long>(n_pages) * m.kv_page_tokens > m.kv_slot_cap)
+            throw hk::ApiError(HK_ERR_BACKEND, "paged K/V pool too small for the batch");
+        pages.block_table = m.meta + L.table;
+        pages.cu_pages = m.meta + L.cu_pages;
+        pages.page_tokens = m.kv_page_tokens;
+    }
+    // Longest rows first for the per-row recurrence kernels.
+    m.row_order.resize(n_rows);
+    for (int r = 0; r < n_rows; ++r) m.row_order[r] = r;
+    std::stable_sort(m.row_order.begin(), m.row_order.end(),
+                     [&](int a, int b) { return cu_h[a + 1] - cu_h[a] > cu_h[b + 1] - cu_h[b]; });
+    // Host-built parts of the batch description, through pinned staging:
+    // cu_positions, then the contiguous row order | cu_pages | block table.
+    {
+        const size_t w_cup = static_cast<size_t>(n_rows) + 1;
+        const size_t w_tail = L.total - L.row_order;
+        hk::Model::HostStage &st = m.stage_acquire((w_cup + w_tail) * 4);
+        int32_t *h = reinterpret_cast<int32_t *>(st.p);
+        std::memcpy(h, cup_h, w_cup * 4);
+        int32_t *t = h + w_cup;
+        std::memcpy(t, m.row_order.data(), static_cast<size_t>(n_rows) * 4);
+        if (n_pages) {
+            std::memcpy(t + n_rows, plan.cu_pages.data(), plan.cu_pages.size() * 4);
+            std::memcpy(t + n_rows + n_rows + 1, plan.table.data(), plan.table.size() * 4);
+        }
+        HK_CUDA(cudaMemcpyAsync(m.meta + L.cu_pos, h, w_cup * 4, cudaMemcpyHostToDevice, m.stream));
+        HK_CUDA(cudaMemcpyAsync(m.meta + L.row_order, t, (n_pages ? w_tail : static_cast<size_t>(n_rows)) * 4,
+                                cudaMemcpyHostToDevice, m.stream));
+        HK_CUDA(cudaEventRecord(st.done, m.stream));
+    }
     const uint64_t before = hk::tl_launches;
     hk::build_meta_kernel<<<std::min(hk::ceil_div(L.total, 256), 1024), 256, 0, m.stream>>>(m.meta, n_rows, n, p, L);
     HK_LAUNCH_CHECK();
     m.forward(n_rows, n, max_len, p, reinterpret_cast<const uint32_t *>(m.meta + L.ids), m.meta + L.cu,
-              m.meta + L.pos, m.meta + L.tok_row, m.meta + L.ridx, m.meta + L.opt_dec, m.logits);
+              m.meta + L.pos, m.meta + L.tok_row, m.meta + L.ridx, m.meta + L.opt_dec, m.logits, pages,
+              m.meta + L.row_order);
+
     m.launches += hk::tl_launches - before;
     return HK_OK;
 }
@@ -1079,8 +1189,6 @@ int hk_score_device(hk_model *h, int n_rows, const int32_t *cu_seqlens_host, con
         if (p)
             HK_CUDA(cudaMemcpyAsync(m.meta + L.positions, d_positions, static_cast<size_t>(p) * 4,
                                     cudaMemcpyDeviceToDevice, s));
-        HK_CUDA(cudaMemcpyAsync(m.meta + L.cu_pos, cu_positions_host, static_cast<size_t>(n_rows + 1) * 4,
-                                cudaMemcpyHostToDevice, s));
         int rc;
         try {
             rc = score_device_impl(m, n_rows, cu_seqlens_host, cu_positions_host, s);
@@ -1112,6 +1220,19 @@ int hk_synchronize(hk_model *h) {
 }
 
 uint64_t hk_kernel_launches(const hk_model *h) { return (h && h->m) ? h->m->launches : 0; }
+
+int hk_set_kv_page_tokens(hk_model *h, int page_tokens, uint64_t shuffle_seed) {
+    if (!h || !h->m) return HK_ERR_ARGUMENT;
+    hk::Model &m = *h->m;
+    if (page_tokens != 0 && (page_tokens < 16 || page_tokens > 256 || (page_tokens & (page_tokens - 1)) != 0))
+        return fail(h, HK_ERR_ARGUMENT, "KV page tokens must be 0 or a power of two in 16..256");
+    if (page_tokens != m.kv_page_tokens) {
+        m.kv_page_tokens = page_tokens;
+        m.cap_tokens = m.cap_rows = m.cap_readouts = 0;  // re-size the K/V pool on the next call
+    }
+    m.kv_shuffle_seed = shuffle_seed;
+    return HK_OK;
+}
 
 int hk_profile_enable(hk_model *h, int enable) {
     if (!h || !h->m) return HK_ERR_ARGUMENT;

@@ -345,7 +345,9 @@ __global__ void attn_prep_kernel(AttnPrepArgs a) {
     if (slot >= a.nh + a.nkv) {  // value head: convert
         const int h = slot - a.nh - a.nkv;
         const float *src = proj + a.nh * 2 * a.hd + a.nkv * a.hd + h * a.hd;
-        T *dst = static_cast<T *>(a.v) + (static_cast<size_t>(t) * a.nkv + h) * a.hd;
+        const int row = a.tok_row[t];
+        const int kvs = kv_slot(a.pages, row, t - a.pos[t], a.pos[t]);
+        T *dst = static_cast<T *>(a.v) + (static_cast<size_t>(kvs) * a.nkv + h) * a.hd;
         for (int i = lane; i < a.hd; i += 32) dst[i] = Act<T>::from_f(src[i]);
         return;
     }
@@ -361,8 +363,9 @@ __global__ void attn_prep_kernel(AttnPrepArgs a) {
     __syncwarp();
     const float p = static_cast<float>(a.pos[t]);
     const int half = a.rd / 2;
+    const int kvs = is_q ? t : kv_slot(a.pages, a.tok_row[t], t - a.pos[t], a.pos[t]);
     T *dst = (is_q ? static_cast<T *>(a.q) + (static_cast<size_t>(t) * a.nh + h) * a.hd
-                   : static_cast<T *>(a.k) + (static_cast<size_t>(t) * a.nkv + h) * a.hd);
+                   : static_cast<T *>(a.k) + (static_cast<size_t>(kvs) * a.nkv + h) * a.hd);
     for (int i = lane; i < a.hd; i += 32) {
         float r = buf[i];
         if (i < a.rd) {
@@ -402,7 +405,8 @@ __global__ void attn_simt_kernel(AttnArgs a) {
     const float scale = 1.0f / sqrtf(static_cast<float>(a.hd));
     float m = -INFINITY, l = 0.f;
     for (int s = start; s <= t; ++s) {
-        const T *k = static_cast<const T *>(a.k) + (static_cast<size_t>(s) * a.nkv + kh) * a.hd;
+        const int kvs = kv_slot(a.pages, row, start, s - start);
+        const T *k = static_cast<const T *>(a.k) + (static_cast<size_t>(kvs) * a.nkv + kh) * a.hd;
         float dot = 0.f;
 #pragma unroll
         for (int e = 0; e < MAXE; ++e) {
@@ -414,7 +418,7 @@ __global__ void attn_simt_kernel(AttnArgs a) {
         const float corr = expf(m - mn);
         const float pw = expf(dot - mn);
         l = l * corr + pw;
-        const T *v = static_cast<const T *>(a.v) + (static_cast<size_t>(s) * a.nkv + kh) * a.hd;
+        const T *v = static_cast<const T *>(a.v) + (static_cast<size_t>(kvs) * a.nkv + kh) * a.hd;
 #pragma unroll
         for (int e = 0; e < MAXE; ++e) {
             const int i = lane + 32 * e;

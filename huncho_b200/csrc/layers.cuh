@@ -47,6 +47,7 @@ void launch_delta_prep(const DeltaPrepArgs &a, cudaStream_t s);
 struct DeltaRecArgs {
     const float *q, *k, *v, *g, *beta;
     const int32_t *cu_seqlens;
+    const int32_t *row_order = nullptr;  // CTA i processes row row_order[i] (longest first), or i
     int n_rows, nk, nv, dk, dv;
     float *out;  // [n, nv, dv]
     int exact;
@@ -76,22 +77,40 @@ void launch_gated_norm(int act, const float *o, const float *z, int ldz, const f
 // Full-attention input stage (qwen3_5.rs:596-615): split q | gate per head,
 // q_norm / k_norm (zero-centred weights, fp32), partial RoPE on the first
 // rotary_dim dims at each token's in-row position.
+// Where a row's keys and values live. Flat (page_tokens == 0): key j of the row
+// starting at token `start` is slot start + j. Paged: slot
+// block_table[cu_pages[row] + j / page_tokens] * page_tokens + j % page_tokens,
+// i.e. fixed-size pages in any order (the reference's PagedKv page list,
+// kv_pages.rs:19-40, as a device block table).
+struct KvPages {
+    const int32_t *block_table = nullptr;
+    const int32_t *cu_pages = nullptr;  // [n_rows + 1] offsets into block_table
+    int page_tokens = 0;
+};
+
+__device__ __forceinline__ int kv_slot(const KvPages &p, int row, int start, int j) {
+    if (p.page_tokens == 0) return start + j;
+    return p.block_table[p.cu_pages[row] + j / p.page_tokens] * p.page_tokens + j % p.page_tokens;
+}
+
 struct AttnPrepArgs {
     const float *proj;  // [n, ldp] fp32: per q head [q(hd) | gate(hd)], then k (nkv*hd), v (nkv*hd)
     int ldp;
     const int32_t *pos;
+    const int32_t *tok_row;  // row of each token (paged K/V)
     int n, nh, nkv, hd, rd;
     const float *qn_w, *kn_w;  // effective norm weights [hd]
     const float *inv_freq;     // [rd/2]
     float eps;
-    void *q, *k, *v;  // [n, nh, hd], [n, nkv, hd], [n, nkv, hd]
+    void *q, *k, *v;  // q [n, nh, hd]; k, v [slots, nkv, hd] at kv_slot()
+    KvPages pages;
 };
 void launch_attn_prep(int act, const AttnPrepArgs &a, cudaStream_t s);
 
 // Causal softmax(q k^T / sqrt(hd)) v per row with GQA (qwen3_5.rs:669-714),
 // multiplied by sigmoid(gate) and written token-major [n, nh*hd].
 struct AttnArgs {
-    const void *q, *k, *v;  // [n, nh, hd], [n, nkv, hd], [n, nkv, hd]
+    const void *q, *k, *v;  // q [n, nh, hd]; k, v [slots, nkv, hd] at kv_slot()
     const float *proj;      // gate source (fp32): proj[t, h*2*hd + hd + i]
     int ldp;
     const int32_t *cu_seqlens;
@@ -99,6 +118,7 @@ struct AttnArgs {
     int n, n_rows, max_len, nh, nkv, hd;
     void *out;
     int ldo;
+    KvPages pages;
 };
 void launch_attention(int act, const AttnArgs &a, cudaStream_t s);
 // The tensor-core (fp16) kernel behind launch_attention for head_dim 64/128/256.

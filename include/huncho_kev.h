@@ -118,6 +118,16 @@ int hk_score_device(hk_model *m, int n_rows, const int32_t *cu_seqlens_host,
                     const int32_t *d_cu_seqlens, const int32_t *d_positions,
                     float *d_out_logits, void *stream);
 
+/*
+ * Store each attention layer's keys and values in pages of `page_tokens`
+ * tokens (0 = flat), placed through a per-batch block table; a nonzero
+ * `shuffle_seed` permutes the pages' pool order pseudo-randomly (deterministic
+ * per seed). Results equal the flat layout. Replaces
+ * Qwen3_5Backend::with_kv_page_tokens (qwen3_5.rs:1773-1809; same accepted
+ * values: 0 or a power of two in 16..256, else HK_ERR_ARGUMENT).
+ */
+int hk_set_kv_page_tokens(hk_model *m, int page_tokens, uint64_t shuffle_seed);
+
 /* Block until the handle's queued work is done; report a device-side error flag. */
 int hk_synchronize(hk_model *m);
 

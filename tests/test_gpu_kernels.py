@@ -256,3 +256,23 @@ def test_readout_vs_torch(lib):
     torch.cuda.synchronize()
     ref = _readout_ref(x, w, wq, bq, wk, bk, idx, opt_dec, n_dec, 1e-6, dp)
     torch.testing.assert_close(logits, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_delta_chunked_long_context_stress(lib):
+    """The long-context stress configuration at the delta-rule kernel boundary:
+    8192-token rows, log-decay g uniform in [-0.1, 0] (a state that remembers
+    hundreds of tokens) and beta uniform in (0, 1), chunked tensor-core kernel
+    vs the per-token fp32 recurrence."""
+    rng = np.random.default_rng(8)
+    nk = nv = 16
+    n = 2 * 8192
+    q = (ko.l2norm(rng.standard_normal((n, nk, 128), dtype=np.float32)) * np.float32(128 ** -0.5)).astype(np.float32)
+    k = ko.l2norm(rng.standard_normal((n, nk, 128), dtype=np.float32)).astype(np.float32)
+    v = rng.standard_normal((n, nv, 128), dtype=np.float32)
+    g = (-rng.random((n, nv), dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    b = rng.uniform(1e-6, 1.0, (n, nv)).astype(np.float32)
+    cu = np.array([0, 8192, n], np.int32)
+    got = _run_delta(lib, q, k, v, g, b, cu, nk, nv, 0)
+    ref = _delta_oracle(q, k, v, g, b, cu, nk, nv)
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() <= 2e-3 * np.abs(ref).max()

@@ -217,3 +217,30 @@ def test_full_size_batch_invariance(native_lib):
             assert np.abs(pa - pb).max() <= 1e-4
             assert calibration.argmax(pa.tolist()) == calibration.argmax(pb.tolist())
         k += len(p)
+
+
+@pytest.mark.parametrize("name,dtype,store", [("tiny", "fp32", None), ("tiny", "bf16", None),
+                                              ("kev-mini", "bf16", "bf16"), ("kev-0.8b-l4", "bf16", "bf16")])
+def test_paged_kv_equals_flat(native_lib, synth_root, name, dtype, store):
+    """16-token KV pages in a shuffled block table give the flat result bit for
+    bit (the reference's pages-vs-flat parity, tests/kv_pages.rs:36-103)."""
+    d = GOLDEN if name == "tiny" else _synth(synth_root, name, store)
+    b = _backend(d, dtype, max_context=4096)
+    vocab = b.vocab_size
+    wl = synth.make_workload(2, vocab, seed=3, n_requests=3)
+    args = pack_rows(wl.rows, wl.positions)
+    flat = b.score_packed(*args)
+    b.with_kv_page_tokens(16, shuffle_seed=7)
+    paged = b.score_packed(*args)
+    assert np.array_equal(flat, paged)
+    b.with_kv_page_tokens(64, shuffle_seed=0)
+    assert np.array_equal(flat, b.score_packed(*args))
+    b.with_kv_page_tokens(0)
+    assert np.array_equal(flat, b.score_packed(*args))
+
+
+def test_kv_page_tokens_validation(tiny_fp32):
+    from huncho_b200.errors import BackendError
+    for bad in (8, 48, 512, -16):
+        with pytest.raises(BackendError):
+            tiny_fp32.with_kv_page_tokens(bad)
