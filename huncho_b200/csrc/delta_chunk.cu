@@ -23,13 +23,12 @@
 // substitution. Padding rows of a short last chunk are zero (g = 0, b = 0), so
 // they change neither the outputs nor the carried state.
 //
-// In the fused form (FROM_PROJ) the kernel also does the layer's input stage
-// from the fp32 projection rows -- causal depthwise conv (4 taps, in-row
-// history only) + SiLU, L2 norm of q and k (q scaled by 1/sqrt(128)), beta =
-// sigmoid(b), g = -exp(A_log) softplus(a + dt_bias) (qwen3_5.rs:817-925) --
-// and, with GATED_OUT, the gated RMSNorm rms(o) * w * silu(z) into the fp16
-// input of out_proj (qwen3_5.rs:193-201, 934-938); q, k, v and o then never
-// leave the SM.
+// The next chunk's inputs (q, k, v rows, g, beta, and z for the gated output)
+// stream into shared memory with cp.async while the current chunk computes,
+// so global latency stays off the serial chunk-to-chunk path. With GATED_OUT
+// the gated RMSNorm rms(o) * w * silu(z) (qwen3_5.rs:193-201, 934-938) is
+// applied to each chunk's output in the kernel and written as the fp16 input
+// of out_proj, so o never leaves the SM.
 #include <math.h>
 
 #include "common.cuh"
@@ -56,6 +55,10 @@ struct Smem {
     __half Mh[C][LDC], Ml[C][LDC];
     float G[C], gam[C], beta[C];
     float red[WARPS][C];  // per-warp partial sums of squares (gated norm)
+    // cp.async staging of the next chunk's fp32 inputs
+    float sq[C][D], sk[C][D], sv[C][D];
+    float sz[C][D];  // z rows of the chunk whose gated output is pending
+    float sg[C], sb[C];
 };
 
 __device__ __forceinline__ uint32_t sa(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -103,6 +106,17 @@ __device__ __forceinline__ void frag_b_kn(uint32_t (&r)[4], const __half (*m)[LD
     ldsm_x4_t(r, &m[k0 + i + (j & 1) * 8][n0 + (j >> 1) * 8]);
 }
 
+__device__ __forceinline__ void cp16(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa(dst)), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp4(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(sa(dst)), "l"(src), "r"(valid ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void split_store(__half *hi, __half *lo, float v) {
     const __half h = __float2half_rn(v);
     *hi = h;
@@ -123,12 +137,11 @@ __device__ __forceinline__ void store4(__half *dst, const float (&v)[4]) {
 }
 
 struct ChunkArgs {
-    // Pre-computed inputs (!FROM_PROJ): q, k [n, nk, 128], v [n, nv, 128], g, beta [n, nv].
+    // Inputs: q, k [n, nk, 128], v [n, nv, 128], g, beta [n, nv] (fp32).
     const float *q, *k, *v, *g, *beta;
-    // Fused input stage (FROM_PROJ): projection rows and the layer's parameters.
+    // GATED_OUT: z is read from the fp32 projection rows proj[t, zoff + h*128 + j].
     const float *proj;
-    int ldp;
-    const float *conv_w, *base_g, *dt_bias;
+    int ldp, zoff;
     const int32_t *cu_seqlens;
     const int32_t *row_order;  // CTA x handles row row_order[x] (longest rows first), or x
     int n_rows, nk, nv;
@@ -140,8 +153,8 @@ struct ChunkArgs {
 };
 
 
-template <bool FROM_PROJ, bool GATED_OUT>
-__global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(ChunkArgs a) {
+template <bool GATED_OUT>
+__global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
     // Rows run longest first (row_order), so the grid's last wave is made of
@@ -152,30 +165,59 @@ __global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(ChunkArgs a) {
     const int kh = h / (a.nv / a.nk);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g4 = lane >> 2, t4 = lane & 3;
-    const int key_dim = a.nk * D, value_dim = a.nv * D, conv_dim = 2 * key_dim + value_dim;
+
+    // Asynchronous loads of a chunk's inputs into the staging buffers; rows
+    // past the row's end are zero-filled (so they carry g = 0, beta = 0).
+    auto prefetch_qkv = [&](int c0) {
+        const int nn = min(C, end - c0);
+        for (int i = tid; i < 3 * C * (D / 4); i += THREADS) {
+            const int which = i / (C * (D / 4)), rem = i % (C * (D / 4));
+            const int r = rem / (D / 4), c = (rem % (D / 4)) * 4;
+            const bool ok = r < nn;
+            const size_t t = static_cast<size_t>(c0 + (ok ? r : 0));
+            const float *src = which == 0 ? a.q + (t * a.nk + kh) * D + c
+                                          : which == 1 ? a.k + (t * a.nk + kh) * D + c : a.v + (t * a.nv + h) * D + c;
+            float *dst = which == 0 ? &sm.sq[r][c] : which == 1 ? &sm.sk[r][c] : &sm.sv[r][c];
+            cp16(dst, src, ok);
+        }
+        if (tid < 2 * C) {
+            const int r = tid % C;
+            const bool ok = r < nn;
+            const size_t t = static_cast<size_t>(c0 + (ok ? r : 0));
+            if (tid < C)
+                cp4(&sm.sg[r], a.g + t * a.nv + h, ok);
+            else
+                cp4(&sm.sb[r], a.beta + t * a.nv + h, ok);
+        }
+    };
+    auto prefetch_z = [&](int c0) {
+        if (!GATED_OUT) return;
+        const int nn = min(C, end - c0);
+        for (int i = tid; i < C * (D / 4); i += THREADS) {
+            const int r = i / (D / 4), c = (i % (D / 4)) * 4;
+            const bool ok = r < nn;
+            const size_t t = static_cast<size_t>(c0 + (ok ? r : 0));
+            cp16(&sm.sz[r][c], a.proj + t * a.ldp + a.zoff + h * D + c, ok);
+        }
+    };
 
     // State accumulator: key rows 16*warp + {g4, g4+8}, value cols 8*nt + 2*t4 + {0,1}.
     float S[16][4];
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0.f;
     for (int i = tid; i < D * LDH; i += THREADS) (&sm.S[0][0])[i] = __float2half_rn(0.f);
+    prefetch_qkv(start);
+    prefetch_z(start);
+    cp_commit();
 
     for (int c0 = start; c0 < end; c0 += C) {
         const int n = min(C, end - c0);
-        // ---- P0: gates. Warp 0 scans g; padding rows get g = 0, b = 0.
+        cp_wait_all();
+        __syncthreads();  // this chunk's inputs are in the staging buffers
+        // ---- P0: gates. Warp 0 scans g (padding rows carry g = 0, beta = 0).
         if (warp == 0) {
-            const size_t t = static_cast<size_t>(c0 + lane);
-            float gv = 0.f, bv = 0.f;
-            if (lane < n) {
-                if (FROM_PROJ) {
-                    const float *pr = a.proj + t * a.ldp + conv_dim + value_dim;
-                    bv = sigmoid_f(pr[h]);
-                    gv = a.base_g[h] * logf(expf(pr[a.nv + h] + a.dt_bias[h]) + 1.0f);
-                } else {
-                    gv = a.g[t * a.nv + h];
-                    bv = a.beta[t * a.nv + h];
-                }
-            }
+            float gv = sm.sg[lane];
+            const float bv = sm.sb[lane];
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const float up = __shfl_up_sync(0xffffffffu, gv, o);
@@ -186,63 +228,15 @@ __global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(ChunkArgs a) {
             sm.beta[lane] = bv;
         }
         __syncthreads();
-        // ---- P0b: operands. Warp w fills rows w, w+8, ...; lane l owns cols 4l..4l+3.
+        // ---- P0b: operands from the staging buffers. Warp w fills rows w, w+8, ...
+#pragma unroll
         for (int r = warp; r < C; r += WARPS) {
-            float qv[4] = {0.f, 0.f, 0.f, 0.f}, kv[4] = {0.f, 0.f, 0.f, 0.f}, vv[4] = {0.f, 0.f, 0.f, 0.f};
-            if (r < n) {
-                const size_t t = static_cast<size_t>(c0 + r);
-                if (FROM_PROJ) {
-                    const int pos = c0 + r - start;
-                    const int bases[3] = {kh * D, key_dim + kh * D, 2 * key_dim + h * D};
-                    float *dsts[3] = {qv, kv, vv};
-#pragma unroll
-                    for (int j = 0; j < 3; ++j) {
-                        const int cb = bases[j] + 4 * lane;
-                        float4 xs[4];  // x[t-3], x[t-2], x[t-1], x[t]
-#pragma unroll
-                        for (int sh = 3; sh >= 0; --sh)
-                            xs[3 - sh] = pos >= sh ? *reinterpret_cast<const float4 *>(a.proj + (t - sh) * a.ldp + cb)
-                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-                        const float4 w0 = *reinterpret_cast<const float4 *>(a.conv_w + (cb + 0) * 4);
-                        const float4 w1 = *reinterpret_cast<const float4 *>(a.conv_w + (cb + 1) * 4);
-                        const float4 w2 = *reinterpret_cast<const float4 *>(a.conv_w + (cb + 2) * 4);
-                        const float4 w3 = *reinterpret_cast<const float4 *>(a.conv_w + (cb + 3) * 4);
-                        const float wc[4][4] = {{w0.x, w0.y, w0.z, w0.w}, {w1.x, w1.y, w1.z, w1.w},
-                                                {w2.x, w2.y, w2.z, w2.w}, {w3.x, w3.y, w3.z, w3.w}};
-                        const float xc[4][4] = {{xs[0].x, xs[1].x, xs[2].x, xs[3].x}, {xs[0].y, xs[1].y, xs[2].y, xs[3].y},
-                                                {xs[0].z, xs[1].z, xs[2].z, xs[3].z}, {xs[0].w, xs[1].w, xs[2].w, xs[3].w}};
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            float acc = 0.f;  // taps in ascending order, separately rounded products
-#pragma unroll
-                            for (int tap = 0; tap < 4; ++tap) acc = __fadd_rn(acc, __fmul_rn(wc[c][tap], xc[c][tap]));
-                            dsts[j][c] = silu_f(acc);
-                        }
-                    }
-                    const float qs = warp_sum(qv[0] * qv[0] + qv[1] * qv[1] + qv[2] * qv[2] + qv[3] * qv[3]);
-                    const float ks = warp_sum(kv[0] * kv[0] + kv[1] * kv[1] + kv[2] * kv[2] + kv[3] * kv[3]);
-                    const float qi = 1.0f / sqrtf(qs + 1e-6f), ki = 1.0f / sqrtf(ks + 1e-6f);
-                    const float qscale = 1.0f / sqrtf(static_cast<float>(D));
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        qv[c] = (qv[c] * qi) * qscale;
-                        kv[c] = kv[c] * ki;
-                    }
-                } else {
-                    const float4 q4 = *reinterpret_cast<const float4 *>(a.q + (t * a.nk + kh) * D + 4 * lane);
-                    const float4 k4 = *reinterpret_cast<const float4 *>(a.k + (t * a.nk + kh) * D + 4 * lane);
-                    const float4 v4 = *reinterpret_cast<const float4 *>(a.v + (t * a.nv + h) * D + 4 * lane);
-                    qv[0] = q4.x; qv[1] = q4.y; qv[2] = q4.z; qv[3] = q4.w;
-                    kv[0] = k4.x; kv[1] = k4.y; kv[2] = k4.z; kv[3] = k4.w;
-                    vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
-                }
-            } else if (FROM_PROJ) {
-                // keep the warp reductions uniform for padding rows
-                (void)warp_sum(0.f);
-                (void)warp_sum(0.f);
-            }
+            const float4 q4 = *reinterpret_cast<const float4 *>(&sm.sq[r][4 * lane]);
+            const float4 k4 = *reinterpret_cast<const float4 *>(&sm.sk[r][4 * lane]);
+            const float4 v4 = *reinterpret_cast<const float4 *>(&sm.sv[r][4 * lane]);
+            const float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
             const float b = sm.beta[r], bg = sm.beta[r] * sm.gam[r];
-            const float bvv[4] = {b * vv[0], b * vv[1], b * vv[2], b * vv[3]};
+            const float bvv[4] = {b * v4.x, b * v4.y, b * v4.z, b * v4.w};
             const float bkk[4] = {bg * kv[0], bg * kv[1], bg * kv[2], bg * kv[3]};
             split_store4(&sm.Qh[r][4 * lane], &sm.Ql[r][4 * lane], qv);
             split_store4(&sm.Kh[r][4 * lane], &sm.Kl[r][4 * lane], kv);
@@ -250,6 +244,9 @@ __global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(ChunkArgs a) {
             store4(&sm.BK[r][4 * lane], bkk);
         }
         __syncthreads();
+        // The staging buffers are free again: fetch the next chunk's q, k, v, g, beta.
+        if (c0 + C < end) prefetch_qkv(c0 + C);
+        cp_commit();
         // ---- P1: K K^T (warps 0-3) and Q K^T (warps 4-7); 16 rows x 16 cols per warp.
         {
             const bool kk = warp < 4;
@@ -465,16 +462,20 @@ __global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(ChunkArgs a) {
                     for (int w8 = 0; w8 < WARPS; ++w8) ss += sm.red[w8][t];
                     const float denom = sqrtf(ss / static_cast<float>(D) + a.eps);
                     const size_t tok = static_cast<size_t>(c0 + t);
-                    const float *z = a.proj + tok * a.ldp + conv_dim + h * D;
 #pragma unroll
                     for (int nt = 0; nt < 2; ++nt) {
                         const int c = nb + nt * 8 + 2 * t4;
-                        const float2 zz = *reinterpret_cast<const float2 *>(z + c);
+                        const float2 zz = *reinterpret_cast<const float2 *>(&sm.sz[t][c]);
                         const float y0 = ((o[mt][nt][2 * hf] / denom) * a.norm_w[c]) * silu_f(zz.x);
                         const float y1 = ((o[mt][nt][2 * hf + 1] / denom) * a.norm_w[c + 1]) * silu_f(zz.y);
                         *reinterpret_cast<__half2 *>(a.mix + tok * a.ldmix + h * D + c) = __floats2half2_rn(y0, y1);
                     }
                 }
+        }
+        if (GATED_OUT) {
+            __syncthreads();  // every thread has read sz
+            if (c0 + C < end) prefetch_z(c0 + C);
+            cp_commit();
         }
         // ---- P6: S = gam_C S + Kdec^T D (D hi+lo); warp w owns key rows 16w..16w+15.
         {
@@ -510,19 +511,19 @@ __global__ void __launch_bounds__(THREADS, 2) delta_chunk_kernel(ChunkArgs a) {
     }
 }
 
-template <bool FP, bool GO>
+template <bool GO>
 void launch_kernel(const ChunkArgs &a, cudaStream_t s) {
     const size_t smem = sizeof(Smem);
     static bool set[64] = {};
     int dev = 0;
     HK_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64 || !set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(delta_chunk_kernel<FP, GO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        HK_CUDA(cudaFuncSetAttribute(delta_chunk_kernel<GO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
         if (dev >= 0 && dev < 64) set[dev] = true;
     }
     dim3 grid(a.n_rows, a.nv);
-    delta_chunk_kernel<FP, GO><<<grid, THREADS, smem, s>>>(a);
+    delta_chunk_kernel<GO><<<grid, THREADS, smem, s>>>(a);
     HK_LAUNCH_CHECK();
 }
 
@@ -544,11 +545,11 @@ void launch_delta_chunk(const DeltaRecArgs &r, cudaStream_t s) {
     a.nk = r.nk;
     a.nv = r.nv;
     a.out = r.out;
-    launch_kernel<false, false>(a, s);
+    launch_kernel<false>(a, s);
 }
 
-void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp, const float *norm_w, float eps,
-                              __half *mix, int ldmix, cudaStream_t s) {
+void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp, int zoff, const float *norm_w,
+                              float eps, __half *mix, int ldmix, cudaStream_t s) {
     if (r.n_rows <= 0) return;
     ChunkArgs a{};
     a.q = r.q;
@@ -558,6 +559,7 @@ void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp,
     a.beta = r.beta;
     a.proj = proj;
     a.ldp = ldp;
+    a.zoff = zoff;
     a.cu_seqlens = r.cu_seqlens;
     a.row_order = r.row_order;
     a.n_rows = r.n_rows;
@@ -567,31 +569,7 @@ void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp,
     a.eps = eps;
     a.mix = mix;
     a.ldmix = ldmix;
-    launch_kernel<false, true>(a, s);
-}
-
-bool delta_layer_fused_supported(const DeltaPrepArgs &p) {
-    return p.dk == D && p.dv == D && p.taps == 4 && (p.nv % p.nk) == 0 && (p.ldp % 4) == 0;
-}
-
-void launch_delta_layer_fused(const DeltaPrepArgs &p, const int32_t *cu_seqlens, int n_rows, const float *norm_w,
-                              float eps, __half *mix, int ldmix, cudaStream_t s) {
-    if (n_rows <= 0) return;
-    ChunkArgs a{};
-    a.proj = p.proj;
-    a.ldp = p.ldp;
-    a.conv_w = p.conv_w;
-    a.base_g = p.base_g;
-    a.dt_bias = p.dt_bias;
-    a.cu_seqlens = cu_seqlens;
-    a.n_rows = n_rows;
-    a.nk = p.nk;
-    a.nv = p.nv;
-    a.norm_w = norm_w;
-    a.eps = eps;
-    a.mix = mix;
-    a.ldmix = ldmix;
-    launch_kernel<true, true>(a, s);
+    launch_kernel<true>(a, s);
 }
 
 }  // namespace hk

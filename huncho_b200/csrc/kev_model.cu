@@ -727,7 +727,7 @@ struct Model {
                 d.v = dvv;
                 d.g = dg;
                 d.beta = db;
-                if (dtype != HK_DTYPE_FP32 && delta_layer_fused_supported(d)) {
+                if (dtype != HK_DTYPE_FP32 && c.dk == 128 && c.dv == 128 && c.taps == 4 && c.nv <= 32) {
                     // Input stage, then the chunked recurrence with the gated norm fused.
                     ev = prof_begin();
                     launch_delta_prep(d, stream);
@@ -748,7 +748,9 @@ struct Model {
                     r.out = dout;
                     r.exact = 0;
                     ev = prof_begin();
-                    launch_delta_chunk_gated(r, proj, ldp, L.gnorm_w, c.eps, static_cast<__half *>(mix), ldmix, stream);
+                    r.err = err;
+                    launch_delta_chunk_gated(r, proj, ldp, c.conv_dim(), L.gnorm_w, c.eps, static_cast<__half *>(mix),
+                                             ldmix, stream);
                     prof_end(ev, 1, delta_chunk_flops(n_tok, c));
                 } else {
                     ev = prof_begin();

@@ -551,8 +551,8 @@ static void launch_rec_dk(const DeltaRecArgs &a, cudaStream_t s) {
 
 void launch_delta_recurrent(const DeltaRecArgs &a, cudaStream_t s) {
     if (a.n_rows <= 0) return;
-    if (!a.exact && delta_chunk_supported(a)) {
-        launch_delta_chunk(a, s);
+    if (!a.exact && delta_tc_supported(a)) {
+        launch_delta_tc(a, s);
         return;
     }
     if (a.dv > 128) throw CudaError("delta recurrence supports value heads up to 128 wide");

@@ -51,22 +51,23 @@ struct DeltaRecArgs {
     int n_rows, nk, nv, dk, dv;
     float *out;  // [n, nv, dv]
     int exact;
+    uint32_t *err = nullptr;  // device error word (bounded waits)
 };
 void launch_delta_recurrent(const DeltaRecArgs &a, cudaStream_t s);
-// The chunked tensor-core form behind launch_delta_recurrent (non-exact mode,
-// 128-wide heads).
+// The chunked tcgen05 form behind launch_delta_recurrent (non-exact mode,
+// 128-wide heads), and its variant with the gated RMSNorm fused into the
+// output (z from the fp32 projection rows at column zoff + h*128).
+bool delta_tc_supported(const DeltaRecArgs &r);
+void launch_delta_tc(const DeltaRecArgs &r, cudaStream_t s);
+void launch_delta_tc_gated(const DeltaRecArgs &r, const float *proj, int ldp, int zoff, const float *norm_w, float eps,
+                           __half *mix, int ldmix, cudaStream_t s);
+// The chunked mma.sync form (32-token chunks, 128-wide heads).
 bool delta_chunk_supported(const DeltaRecArgs &a);
 void launch_delta_chunk(const DeltaRecArgs &a, cudaStream_t s);
-// The whole Gated DeltaNet mixer between its two projections in one kernel
-// (half-precision models, 128-wide heads, 4 taps): input stage from the fp32
-// projection rows, chunked recurrence, gated RMSNorm into the fp16 out_proj
-// input `mix`.
-// The chunked recurrence with the gated RMSNorm fused into its output
-// (z read from the fp32 projection rows); q, k, v, g, beta pre-computed.
-void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp, const float *norm_w, float eps,
-                              __half *mix, int ldmix, cudaStream_t s);
-bool delta_layer_fused_supported(const DeltaPrepArgs &p);
-void launch_delta_layer_fused(const DeltaPrepArgs &p, const int32_t *cu_seqlens, int n_rows, const float *norm_w,
+// The chunked mma.sync recurrence with the gated RMSNorm fused into its output
+// (z read from the fp32 projection rows at column zoff + h*128); q, k, v, g,
+// beta pre-computed.
+void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp, int zoff, const float *norm_w,
                               float eps, __half *mix, int ldmix, cudaStream_t s);
 
 // out[t, h*dv + j] = rms(o)[j] * w[j] * silu(z[t, h, j]) (qwen3_5.rs:193-201,

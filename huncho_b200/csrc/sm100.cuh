@@ -140,11 +140,38 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
     return d;
 }
 
+// Shared-memory descriptor of a 128B-swizzled operand with explicit strides
+// (bytes). K-major: lbo unused (16), sbo = stride between 8-row groups.
+// MN-major (the operand stored [K rows][MN contiguous], 64 MN elements per
+// 128-byte row): lbo = stride between 64-element MN blocks, sbo = stride
+// between groups of 8 K rows. Adding (bytes >> 4) to the result moves the
+// start address as long as it stays inside shared memory.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
 // Instruction descriptor for kind::f16 with fp16 A/B (format 0 in bits 7-9 and
 // 10-12; both operands always the same type), fp32 accumulation (D format 1
 // in bits 4-5), both operands K-major, N>>3 in bits 17-22, M>>4 in bits 24-28.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
     return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Instruction descriptor for kind::f16, fp16 A/B, fp32 D, both K-major, with
+// A optionally negated (bit 13): D (+)= (-A) B^T.
+__host__ __device__ constexpr uint32_t idesc_f16_f32_neg(int M, int N, bool neg_a) {
+    return idesc_f16_f32(M, N) | (neg_a ? (1u << 13) : 0u);
+}
+
+// As idesc_f16_f32_neg, with either operand MN-major (A bit 15, B bit 16).
+__host__ __device__ constexpr uint32_t idesc_f16_f32_mj(int M, int N, bool a_mn, bool b_mn, bool neg_a = false) {
+    return idesc_f16_f32_neg(M, N, neg_a) | (a_mn ? (1u << 15) : 0u) | (b_mn ? (1u << 16) : 0u);
 }
 
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
@@ -186,6 +213,35 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
         : "memory");
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Each thread of the warp writes 32 consecutive fp32 columns of its TMEM lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n"
+        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
+// Byte offset of fp16 element (r, k) in a K-major operand stored as 128B-swizzled
+// tiles of R rows x 64 elements (TMA SWIZZLE_128B layout; tile kt = k / 64 at
+// kt * R * 128 bytes; the tile base must be 1024-byte aligned).
+__host__ __device__ __forceinline__ uint32_t sw128_off(int R, int r, int k) {
+    const int kt = k >> 6, kk = k & 63;
+    return static_cast<uint32_t>(kt * R * 128 + r * 128 + ((((kk >> 3) ^ (r & 7))) << 4) + ((kk & 7) << 1));
 }
 
 }  // namespace sm100
