@@ -23,12 +23,14 @@
 // into hi + lo halves and multiplied twice; S^T, W^T, T and the decayed keys
 // are single fp16.
 //
-// T = (I + A)^-1 comes from fp32 block forward substitution on all 256
+// T = (I + A)^-1 comes from fp32 block forward substitution on the CTA's
 // threads: the four 16x16 diagonal blocks by substitution, then three levels
 // T_IJ = -T_II sum_K A_IK T_KJ. T's strictly lower part is kept transposed in
 // the unused upper triangle of the A buffer (T[t][s] at A[s][t]).
 //
-// One CTA (8 warps) per (row, value head); rows are taken longest first.
+// One CTA (16 warps) per (row, value head); rows are taken longest first.
+// Warp w reads TMEM lanes 32*(w%4).. and takes column slice w/4 of each
+// accumulator.
 // The next chunk's q/k/v/g/b are loaded into registers while the current
 // chunk computes. All mbarrier waits are bounded: on a timeout the kernel
 // records an error bit, lets the MMAs it issued finish, frees its tensor
@@ -44,7 +46,7 @@ namespace {
 
 using namespace sm100;
 
-constexpr int C = 64, D = 128, THREADS = 256;
+constexpr int C = 64, D = 128, THREADS = 512;
 // Tensor-memory columns.
 constexpr uint32_t TM_S = 0, TM_D1 = 128, TM_O = 192, TM_U = 256, TM_W = 320, TM_COLS = 512;
 // Shared-memory operand tiles (byte offsets; every tile 1024-aligned).
@@ -153,7 +155,9 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
     if (start >= end) return;
     const int kh = h / (a.nv / a.nk);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quarter = warp & 3, half = warp >> 2;  // TMEM lanes 32*quarter.., column half
+    // TMEM lanes 32*quarter.. ; column slice `part` (16 of a 64-column
+    // accumulator, 32 of the 128-column state).
+    const int quarter = warp & 3, part = warp >> 2;
     const uint32_t s_base = smem_addr(sm);
 
     if (tid == 0) {
@@ -171,25 +175,24 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    if (half == 0) {  // the state starts at zero
+    {  // the state starts at zero
         float z[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) z[i] = 0.f;
-#pragma unroll
-        for (int c = 0; c < 128; c += 32) tmem_st32(lane_base + TM_S + c, z);
+        tmem_st32(lane_base + TM_S + part * 32, z);
     }
 
-    // ---- register prefetch of a chunk's inputs: warp w holds rows w + 8i of
-    // q, k and v (j = 8 * tensor + i), lane = 4-column group (coalesced rows).
-    float4 pf[24];
+    // ---- register prefetch of a chunk's inputs: warp w holds rows w + 16i of
+    // q, k and v (j = 4 * tensor + i), lane = 4-column group (coalesced rows).
+    float4 pf[12];
     float pg = 0.f;
-    float pz[32];
+    float pz[16];
     const int c4 = lane * 4;
     auto load_qkvg = [&](int c0) {
         const int nn = min(C, end - c0);
 #pragma unroll
-        for (int j = 0; j < 24; ++j) {
-            const int which = j >> 3, r = warp + 8 * (j & 7);
+        for (int j = 0; j < 12; ++j) {
+            const int which = j >> 2, r = warp + 16 * (j & 3);
             float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
             if (r < nn) {
                 const size_t t = static_cast<size_t>(c0 + r);
@@ -211,8 +214,8 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
         const int nn = min(C, end - c0);
         const int dv = quarter * 32 + lane;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const int t = half * 32 + i;
+        for (int i = 0; i < 16; ++i) {
+            const int t = part * 16 + i;
             pz[i] = t < nn ? a.proj[static_cast<size_t>(c0 + t) * a.ldp + a.zoff + h * D + dv] : 0.f;
         }
     };
@@ -224,6 +227,17 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
         if (!mbar_wait(bar, parity)) {
             set_error(a.err, kErrWaitTimeout);
             *abort_flag = 1;
+        }
+    };
+    // 16 consecutive entries of a small per-token array (broadcast loads).
+    auto ld16 = [&](const float *src, float (&dst)[16]) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+            const float4 x = reinterpret_cast<const float4 *>(src)[q4];
+            dst[4 * q4] = x.x;
+            dst[4 * q4 + 1] = x.y;
+            dst[4 * q4 + 2] = x.z;
+            dst[4 * q4 + 3] = x.w;
         }
     };
 
@@ -256,8 +270,8 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
         __syncthreads();
         // ---- L2: operands into the swizzled tiles, each row as it was loaded.
 #pragma unroll
-        for (int j = 0; j < 24; ++j) {
-            const int which = j >> 3, r = warp + 8 * (j & 7);
+        for (int j = 0; j < 12; ++j) {
+            const int which = j >> 2, r = warp + 16 * (j & 3);
             const float4 x = pf[j];
             if (which == 0) {
                 st4_split(sm + XK_H, sm + XK_L, sw128_off(128, 64 + r, c4), x);
@@ -290,19 +304,20 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
         wait(bar_d1, ph);
         tc_fence_after();
         {
-            float v[32];
-            tmem_ld32(lane_base + TM_D1 + half * 32, v);
+            float v[16], gs[16];
+            tmem_ld16(lane_base + TM_D1 + part * 16, v);
+            ld16(G + part * 16, gs);
             if (quarter < 2) {
                 const int t = quarter * 32 + lane;
                 const float bt = beta[t], gt = G[t];
-                float4 *dst = reinterpret_cast<float4 *>(sA + t * LA + half * 32);
+                float4 *dst = reinterpret_cast<float4 *>(sA + t * LA + part * 16);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
+                for (int c = 0; c < 4; ++c) {
                     float e[4];
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const int s = half * 32 + 4 * c + u;
-                        e[u] = s < t ? bt * expf(gt - G[s]) * v[4 * c + u] : 0.f;
+                        const int i = 4 * c + u, s2 = part * 16 + i;
+                        e[u] = s2 < t ? bt * expf(gt - gs[i]) * v[i] : 0.f;
                     }
                     dst[c] = make_float4(e[0], e[1], e[2], e[3]);
                 }
@@ -310,17 +325,17 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
                 const int t = (quarter - 2) * 32 + lane;
                 const float gt = G[t];
 #pragma unroll
-                for (int c8 = 0; c8 < 4; ++c8) {
+                for (int c8 = 0; c8 < 2; ++c8) {
                     float hv[8], lv[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
-                        const int s = half * 32 + c8 * 8 + e;
-                        const float mq = s <= t ? expf(gt - G[s]) * v[c8 * 8 + e] : 0.f;
+                        const int i = c8 * 8 + e, s2 = part * 16 + i;
+                        const float mq = s2 <= t ? expf(gt - gs[i]) * v[i] : 0.f;
                         const float2 hl = hi_lo(mq);
                         hv[e] = hl.x;
                         lv[e] = hl.y;
                     }
-                    const uint32_t off = sw128_off(64, t, half * 32 + c8 * 8);
+                    const uint32_t off = sw128_off(64, t, part * 16 + c8 * 8);
                     st8(sm + MQ_H, off, hv);
                     st8(sm + MQ_L, off, lv);
                 }
@@ -365,71 +380,77 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
         __syncthreads();
         // Off-diagonal blocks, level I: X_IJ = sum_{K=J}^{I-1} A_IK T_KJ (kept
         // transposed, X[J][b][a]), then T_IJ = -T_II X_IJ, stored transposed at
-        // A[16J + b][16I + a].
+        // A[16J + b][16I + a]. The two 8-warp groups take different J.
+        {
+            const int grp = tid >> 8, ra = (tid >> 4) & 15, cb = tid & 15;
 #pragma unroll
-        for (int I = 1; I < 4; ++I) {
-            const int ra = tid >> 4, cb = tid & 15;
+            for (int I = 1; I < 4; ++I) {
 #pragma unroll
-            for (int J = 0; J < I; ++J) {
-                float acc0 = 0.f, acc1 = 0.f;
+                for (int J = 0; J < I; ++J) {
+                    if (grp != (I == 3 ? (J == 0 ? 0 : 1) : (J & 1))) continue;
+                    float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
-                for (int K = J; K < I; ++K) {
-                    const float4 *arow = reinterpret_cast<const float4 *>(sA + (16 * I + ra) * LA + 16 * K);
-                    const float4 *tcol = reinterpret_cast<const float4 *>(sA + (16 * J + cb) * LA + 16 * K);
+                    for (int K = J; K < I; ++K) {
+                        const float4 *arow = reinterpret_cast<const float4 *>(sA + (16 * I + ra) * LA + 16 * K);
+                        const float4 *tcol = reinterpret_cast<const float4 *>(sA + (16 * J + cb) * LA + 16 * K);
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        const float4 av = arow[q4], tv4 = tcol[q4];
-                        const float ae[4] = {av.x, av.y, av.z, av.w}, te[4] = {tv4.x, tv4.y, tv4.z, tv4.w};
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            const float4 av = arow[q4], tv4 = tcol[q4];
+                            const float ae[4] = {av.x, av.y, av.z, av.w}, te[4] = {tv4.x, tv4.y, tv4.z, tv4.w};
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int c = 4 * q4 + e;
-                            // T_JJ is unit lower: its upper part in storage holds A_JJ.
-                            const float tv = K == J ? (c == cb ? 1.f : (c > cb ? te[e] : 0.f)) : te[e];
-                            if (e & 1)
-                                acc1 = fmaf(ae[e], tv, acc1);
-                            else
-                                acc0 = fmaf(ae[e], tv, acc0);
+                            for (int e = 0; e < 4; ++e) {
+                                const int c = 4 * q4 + e;
+                                // T_JJ is unit lower: its upper part in storage holds A_JJ.
+                                const float tv = K == J ? (c == cb ? 1.f : (c > cb ? te[e] : 0.f)) : te[e];
+                                if (e & 1)
+                                    acc1 = fmaf(ae[e], tv, acc1);
+                                else
+                                    acc0 = fmaf(ae[e], tv, acc0);
+                            }
                         }
                     }
+                    sX[(J * 16 + cb) * LX + ra] = acc0 + acc1;
                 }
-                sX[(J * 16 + cb) * LX + ra] = acc0 + acc1;
-            }
-            __syncthreads();
+                __syncthreads();
 #pragma unroll
-            for (int J = 0; J < I; ++J) {
-                const float4 *xr = reinterpret_cast<const float4 *>(sX + (J * 16 + cb) * LX);
-                const float4 *tr = reinterpret_cast<const float4 *>(sTd + (I * 16 + ra) * 16);
-                float acc0 = sX[(J * 16 + cb) * LX + ra], acc1 = 0.f;
+                for (int J = 0; J < I; ++J) {
+                    if (grp != (I == 3 ? (J == 0 ? 0 : 1) : (J & 1))) continue;
+                    const float4 *xr = reinterpret_cast<const float4 *>(sX + (J * 16 + cb) * LX);
+                    const float4 *tr = reinterpret_cast<const float4 *>(sTd + (I * 16 + ra) * 16);
+                    float acc0 = sX[(J * 16 + cb) * LX + ra], acc1 = 0.f;
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    const float4 xv = xr[q4], tv = tr[q4];
-                    acc0 = fmaf(tv.x, xv.x, acc0);
-                    acc1 = fmaf(tv.y, xv.y, acc1);
-                    acc0 = fmaf(tv.z, xv.z, acc0);
-                    acc1 = fmaf(tv.w, xv.w, acc1);
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const float4 xv = xr[q4], tv = tr[q4];
+                        acc0 = fmaf(tv.x, xv.x, acc0);
+                        acc1 = fmaf(tv.y, xv.y, acc1);
+                        acc0 = fmaf(tv.z, xv.z, acc0);
+                        acc1 = fmaf(tv.w, xv.w, acc1);
+                    }
+                    sA[(16 * J + cb) * LA + 16 * I + ra] = -(acc0 + acc1);
                 }
-                sA[(16 * J + cb) * LA + 16 * I + ra] = -(acc0 + acc1);
+                __syncthreads();
             }
-            __syncthreads();
         }
         // T diag(b) and T diag(b gam) as fp16 K-major [t][s] tiles.
         {
-            const int t = tid & 63;
+            const int t = tid & 63, ch = tid >> 6;
+            const float4 b0 = reinterpret_cast<const float4 *>(beta + 8 * ch)[0],
+                         b1 = reinterpret_cast<const float4 *>(beta + 8 * ch)[1];
+            const float4 g0 = reinterpret_cast<const float4 *>(gam + 8 * ch)[0],
+                         g1 = reinterpret_cast<const float4 *>(gam + 8 * ch)[1];
+            const float bs[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+            const float gs[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            float vb[8], vg[8];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int ch = (tid >> 6) + 4 * u;
-                float vb[8], vg[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int s2 = 8 * ch + e;
-                    const float tv = s2 < t ? sA[s2 * LA + t] : (s2 == t ? 1.f : 0.f);
-                    vb[e] = tv * beta[s2];
-                    vg[e] = vb[e] * gam[s2];
-                }
-                const uint32_t off = sw128_off(64, t, 8 * ch);
-                st8(sm + TB, off, vb);
-                st8(sm + TBG, off, vg);
+            for (int e = 0; e < 8; ++e) {
+                const int s2 = 8 * ch + e;
+                const float tv = s2 < t ? sA[s2 * LA + t] : (s2 == t ? 1.f : 0.f);
+                vb[e] = tv * bs[e];
+                vg[e] = vb[e] * gs[e];
             }
+            const uint32_t off = sw128_off(64, t, 8 * ch);
+            st8(sm + TB, off, vb);
+            st8(sm + TBG, off, vg);
         }
         fence_async_smem();
         tc_fence_before();
@@ -452,15 +473,16 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
         wait(bar_o, ph);
         tc_fence_after();
         {
-            float v[32];
-            tmem_ld32(lane_base + TM_W + half * 32, v);
+            float v[16], gs[16];
+            tmem_ld16(lane_base + TM_W + part * 16, v);
             const int dk = quarter * 32 + lane;
 #pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) st8(sm + V_H, sw128_off(128, dk, half * 32 + c8 * 8), v + c8 * 8);
-            tmem_ld32(lane_base + TM_O + half * 32, v);
+            for (int c8 = 0; c8 < 2; ++c8) st8(sm + V_H, sw128_off(128, dk, part * 16 + c8 * 8), v + c8 * 8);
+            tmem_ld16(lane_base + TM_O + part * 16, v);
+            ld16(gam + part * 16, gs);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] *= gam[half * 32 + i];
-            tmem_st32(lane_base + TM_O + half * 32, v);
+            for (int i = 0; i < 16; ++i) v[i] *= gs[i];
+            tmem_st16(lane_base + TM_O + part * 16, v);
         }
         fence_async_smem();
         tc_fence_before();
@@ -478,11 +500,11 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
         wait(bar_d, ph);
         tc_fence_after();
         {
-            float v[32];
-            tmem_ld32(lane_base + TM_U + half * 32, v);
+            float v[16];
+            tmem_ld16(lane_base + TM_U + part * 16, v);
             const int dv = quarter * 32 + lane;
 #pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
+            for (int c8 = 0; c8 < 2; ++c8) {
                 float hv[8], lv[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
@@ -490,18 +512,16 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
                     hv[e] = hl.x;
                     lv[e] = hl.y;
                 }
-                const uint32_t off = sw128_off(128, dv, half * 32 + c8 * 8);
+                const uint32_t off = sw128_off(128, dv, part * 16 + c8 * 8);
                 st8(sm + DT_H, off, hv);
                 st8(sm + DT_L, off, lv);
             }
             const float gc = gam[C - 1];
+            float w[32];
+            tmem_ld32(lane_base + TM_S + part * 32, w);
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                tmem_ld32(lane_base + TM_S + half * 64 + cc * 32, v);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] *= gc;
-                tmem_st32(lane_base + TM_S + half * 64 + cc * 32, v);
-            }
+            for (int i = 0; i < 32; ++i) w[i] *= gc;
+            tmem_st32(lane_base + TM_S + part * 32, w);
         }
         fence_async_smem();
         tc_fence_before();
@@ -525,16 +545,16 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
         tc_fence_after();
         {
             const int dv = quarter * 32 + lane;
-            float v[32];
-            tmem_ld32(lane_base + TM_O + half * 32, v);  // v[i] = O[t = 32*half + i][dv]
+            float v[16];
+            tmem_ld16(lane_base + TM_O + part * 16, v);  // v[i] = O[t = 16*part + i][dv]
             if (GATED) {
                 // Sum of squares over this quarter's 32 value columns for each of the
-                // 32 rows, by a transposing butterfly (lane l ends with row 32*half + l).
-                float sq[32];
+                // 16 rows, by a transposing butterfly (lane l ends with row l & 15).
+                float sq[16];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) sq[i] = v[i] * v[i];
+                for (int i = 0; i < 16; ++i) sq[i] = v[i] * v[i];
 #pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) {
+                for (int off = 8; off >= 1; off >>= 1) {
                     const bool upper = (lane & off) != 0;
 #pragma unroll
                     for (int i = 0; i < off; ++i) {
@@ -543,33 +563,32 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
                         sq[i] = (upper ? sq[i + off] : sq[i]) + got;
                     }
                 }
-                red[quarter * C + half * 32 + lane] = sq[0];
+                sq[0] += __shfl_xor_sync(0xffffffffu, sq[0], 16);
+                if (lane < 16) red[quarter * C + part * 16 + lane] = sq[0];
                 __syncthreads();
-                // Lane l forms the denominator of row 32*half + l; rows are then
+                // Lane l forms the denominator of row 16*part + (l & 15); rows are then
                 // broadcast across the warp.
-                const int tl = half * 32 + lane;
+                const int tl = part * 16 + (lane & 15);
                 const float ss = red[tl] + red[C + tl] + red[2 * C + tl] + red[3 * C + tl];
                 const float denom_l = sqrtf(ss / static_cast<float>(D) + a.eps);
-                __half *mrow = a.mix + static_cast<size_t>(c0 + half * 32) * a.ldmix + h * D + dv;
+                __half *mrow = a.mix + static_cast<size_t>(c0 + part * 16) * a.ldmix + h * D + dv;
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
+                for (int i = 0; i < 16; ++i) {
                     const float denom = __shfl_sync(0xffffffffu, denom_l, i);
                     const float y = ((v[i] / denom) * nw) * silu_f(pz[i]);
-                    if (half * 32 + i < n) mrow[static_cast<size_t>(i) * a.ldmix] = __float2half_rn(y);
+                    if (part * 16 + i < n) mrow[static_cast<size_t>(i) * a.ldmix] = __float2half_rn(y);
                 }
             } else {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int t = half * 32 + i;
+                for (int i = 0; i < 16; ++i) {
+                    const int t = part * 16 + i;
                     if (t < n) a.out[(static_cast<size_t>(c0 + t) * a.nv + h) * D + dv] = v[i];
                 }
             }
+            float w[32];
+            tmem_ld32(lane_base + TM_S + part * 32, w);
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                tmem_ld32(lane_base + TM_S + half * 64 + cc * 32, v);
-#pragma unroll
-                for (int c8 = 0; c8 < 4; ++c8) st8(sm + ST, sw128_off(128, dv, half * 64 + cc * 32 + c8 * 8), v + c8 * 8);
-            }
+            for (int c8 = 0; c8 < 4; ++c8) st8(sm + ST, sw128_off(128, dv, part * 32 + c8 * 8), w + c8 * 8);
         }
         if (c0 + C < end) load_z(c0 + C);
         fence_async_smem();
