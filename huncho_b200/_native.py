@@ -19,9 +19,11 @@ HK_ERR_ARGUMENT = -5
 
 HK_DTYPE = {"fp32": 0, "bf16": 1, "int8w": 2, "fp16": 3}
 HK_MAX_ROWS = 64
+HK_CACHE_BRANCH, HK_CACHE_CONTINUE, HK_CACHE_PREFILL = 0, 1, 2
 
 EXPORTED = (
-    "hk_create", "hk_replica", "hk_capabilities_get", "hk_score", "hk_score_device",
+    "hk_create", "hk_replica", "hk_capabilities_get", "hk_score", "hk_score_device", "hk_score_cached",
+    "hk_prefill", "hk_fork", "hk_release_cache", "hk_cache_info",
     "hk_synchronize", "hk_kernel_launches", "hk_set_kv_page_tokens", "hk_profile_enable", "hk_profile_read",
     "hk_last_error",
     "hk_create_error", "hk_destroy",
@@ -61,6 +63,17 @@ def load(path: Path | None = None) -> ctypes.CDLL:
     lib.hk_score.restype = i32
     lib.hk_score_device.argtypes = [vp, i32, pi32, pi32, vp, vp, vp, vp, vp]
     lib.hk_score_device.restype = i32
+    pu64, u64 = ctypes.POINTER(ctypes.c_uint64), ctypes.c_uint64
+    lib.hk_score_cached.argtypes = [vp, i32, pu64, i32, pu32, pi32, pi32, pi32, pf, pu64]
+    lib.hk_score_cached.restype = i32
+    lib.hk_prefill.argtypes = [vp, i32, pu32, pi32, pu64]
+    lib.hk_prefill.restype = i32
+    lib.hk_fork.argtypes = [vp, u64, pu64]
+    lib.hk_fork.restype = i32
+    lib.hk_release_cache.argtypes = [vp, u64]
+    lib.hk_release_cache.restype = i32
+    lib.hk_cache_info.argtypes = [vp, u64, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int64)]
+    lib.hk_cache_info.restype = i32
     lib.hk_synchronize.argtypes = [vp]
     lib.hk_synchronize.restype = i32
     lib.hk_kernel_launches.argtypes = [vp]

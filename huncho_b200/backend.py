@@ -117,7 +117,7 @@ class KevBackend:
     def capabilities(self) -> Capabilities:
         """qwen3_5.rs:2541-2653 (families [F2], dtype, max_context, device)."""
         return Capabilities(
-            id=self.id(), dtype=self.dtype, max_context=self.max_context, supports_fork=False,
+            id=self.id(), dtype=self.dtype, max_context=self.max_context, supports_fork=True,
             supports_lora=True, families=["F2"],
             extra={"device": f"cuda:{self.device}", "native_execution": "b200-kev-sm100a-v1",
                    "pointer_head_dtype": "fp32", "recurrent_state_dtype": "fp32",
@@ -148,30 +148,44 @@ class KevBackend:
         return True
 
     def supports_fork(self) -> bool:
-        return False
+        return True
+
+    def supports_fork_batch(self) -> bool:
+        return True
+
+    def supports_padded_fork_batch(self) -> bool:
+        return True
 
     def batch_limits(self) -> BatchLimits:
         return BatchLimits()
 
+    def fork_batch_limits(self) -> BatchLimits:
+        return BatchLimits()
+
     def forward(self, inp: ForwardInput) -> ForwardOutput:
-        """Backend::forward for one row (qwen3_5.rs:2655-2753)."""
+        """Backend::forward for one row (qwen3_5.rs:2655-2753). With `fork_from`,
+        the tokens continue that branch, positions are relative to them, and
+        the branch advances to the continued state once the call succeeds."""
         if inp.retain_cache:
             raise UnsupportedError("use prefill to obtain an explicit cache handle")
         tokens = list(inp.tokens)
         if any(int(t) < 0 or int(t) >= self.vocab_size for t in tokens):
             raise BackendError("Qwen3.5 token ID is outside the vocabulary")
-        if inp.fork_from is not None:
-            raise BackendError("unknown Qwen3.5 cache handle")
+        prefix = self.cache_tokens(inp.fork_from) if inp.fork_from is not None else 0
         positions = [int(p) for p in inp.positions]
         if any(p < 0 or p >= len(tokens) for p in positions):
             raise BackendError("Qwen3.5 readout position is outside the token sequence")
-        if len(tokens) > self.max_context:
-            raise BackendError(f"sequence length {len(tokens)} exceeds max_context {self.max_context}")
-        if not positions:
+        if prefix + len(tokens) > self.max_context:
+            raise BackendError(f"sequence length {prefix + len(tokens)} exceeds max_context {self.max_context}")
+        if not positions and inp.fork_from is None:
             return ForwardOutput(positions=[], values=np.zeros((0, 1), np.float32))
         if not tokens:
             raise BackendError("cached continuation requires nonempty suffix tokens")
-        return self._run([tokens], [positions])[0]
+        if inp.fork_from is None:
+            return self._run([tokens], [positions])[0]
+        logits, _ = self.score_cached(*pack_rows([tokens], [positions]), parents=[int(inp.fork_from)],
+                                      mode=_native.HK_CACHE_CONTINUE)
+        return ForwardOutput(positions=positions, values=logits.reshape(-1, 1).copy())
 
     def forward_batch(self, inputs: Sequence[ForwardInput]) -> list:
         """Equal-length independent rows (qwen3_5.rs:2759-2761 -> 3138-3194)."""
@@ -181,11 +195,105 @@ class KevBackend:
         """Mixed-length rows; padding is invisible (qwen3_5.rs:2806-2816 -> 3138-3194)."""
         return self._independent(inputs, padded=True)
 
-    def prefill(self, tokens):
-        raise UnsupportedError("prefix caches are not supported by the B200 Kev backend")
+    # ---------------------------------------------------------------- caches
+    def prefill(self, tokens) -> int:
+        """Backend::prefill (qwen3_5.rs:2833-2835): a handle for the state after `tokens`."""
+        return self.prefill_batch([tokens])[0]
 
-    def fork(self, handle):
-        raise UnsupportedError("prefix forks are not supported by the B200 Kev backend")
+    def prefill_batch(self, rows) -> list:
+        """Prefill up to 64 prefixes in one native call; one handle per row."""
+        rows = [list(r) for r in rows]
+        if not rows or len(rows) > _native.HK_MAX_ROWS:
+            raise BackendError("Qwen3.5 batch must contain 1..=64 independent rows")
+        tokens, cu, _, _ = pack_rows(rows, [[] for _ in rows])
+        handles = np.zeros(len(rows), np.uint64)
+        self._check(self._lib.hk_prefill(
+            self._h, len(rows), tokens.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)),
+            cu.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), handles.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))))
+        return [int(h) for h in handles]
+
+    def fork(self, handle: int) -> int:
+        """Backend::fork (qwen3_5.rs:2818-2831): an isolated branch of the same state."""
+        out = ctypes.c_uint64()
+        self._check(self._lib.hk_fork(self._h, ctypes.c_uint64(int(handle)), ctypes.byref(out)))
+        return int(out.value)
+
+    def release_cache(self, handle: int) -> None:
+        """Backend::release_cache (qwen3_5.rs:2837-2846); forks of it stay valid."""
+        self._check(self._lib.hk_release_cache(self._h, ctypes.c_uint64(int(handle))))
+
+    def cache_tokens(self, handle: int) -> int:
+        tokens, nbytes = ctypes.c_int(), ctypes.c_int64()
+        if self._lib.hk_cache_info(self._h, ctypes.c_uint64(int(handle)), ctypes.byref(tokens),
+                                   ctypes.byref(nbytes)) != _native.HK_OK:
+            raise BackendError("unknown Qwen3.5 cache handle")
+        return int(tokens.value)
+
+    def cache_bytes(self, handle: int) -> int:
+        tokens, nbytes = ctypes.c_int(), ctypes.c_int64()
+        if self._lib.hk_cache_info(self._h, ctypes.c_uint64(int(handle)), ctypes.byref(tokens),
+                                   ctypes.byref(nbytes)) != _native.HK_OK:
+            raise BackendError("unknown Qwen3.5 cache handle")
+        return int(nbytes.value)
+
+    def forward_fork_batch(self, parent: int, inputs: Sequence[ForwardInput], work=None) -> list:
+        """Equal-length suffixes of one parent (qwen3_5.rs:2780-2791 -> forward_cached_batch)."""
+        return self._fork_batch(parent, inputs, padded=False, work=work)
+
+    def forward_padded_fork_batch(self, parent: int, inputs: Sequence[ForwardInput], work=None) -> list:
+        """Mixed-length suffixes of one parent (qwen3_5.rs:2793-2804)."""
+        return self._fork_batch(parent, inputs, padded=True, work=work)
+
+    def _fork_batch(self, parent, inputs, padded: bool, work) -> list:
+        inputs = list(inputs)
+        try:
+            prefix = self.cache_tokens(parent)
+        except BackendError:
+            raise BackendError("unknown Qwen3.5 cache handle") from None
+        seq = max((len(i.tokens) for i in inputs), default=0)
+        bad = (prefix == 0 or not inputs or len(inputs) > _native.HK_MAX_ROWS or seq == 0
+               or prefix + seq > self.max_context)
+        for i in inputs:
+            if (len(i.tokens) == 0 or (not padded and len(i.tokens) != seq) or i.fork_from is not None
+                    or i.retain_cache or i.logit_codes is not None or len(i.positions) == 0
+                    or any(int(p) < 0 or int(p) >= len(i.tokens) for p in i.positions)
+                    or any(int(t) < 0 or int(t) >= self.vocab_size for t in i.tokens)):
+                bad = True
+        if bad:
+            raise BackendError("Kev branch batches require a complete parent, 1..=64 nonempty valid suffixes "
+                               "(equal lengths without padding)")
+        rows = [list(i.tokens) for i in inputs]
+        pos = [[int(p) for p in i.positions] for i in inputs]
+        logits, _ = self.score_cached(*pack_rows(rows, pos), parents=[int(parent)] * len(rows),
+                                      mode=_native.HK_CACHE_BRANCH)
+        if work is not None:
+            work.cache_forks = getattr(work, "cache_forks", 0) + len(rows)
+            work.forward_calls = getattr(work, "forward_calls", 0) + 1
+        out, k = [], 0
+        for p in pos:
+            out.append(ForwardOutput(positions=list(p), values=logits[k:k + len(p)].reshape(-1, 1).copy()))
+            k += len(p)
+        return out
+
+    def score_cached(self, tokens, cu_seqlens, positions, cu_positions, parents=None,
+                     mode: int = _native.HK_CACHE_BRANCH):
+        """hk_score_cached: rows that may each continue a cached prefix (any
+        number of parents per call). Returns (logits, new handles or None)."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint32)
+        cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        cup = np.ascontiguousarray(cu_positions, dtype=np.int32)
+        n = len(cu) - 1
+        par = None if parents is None else np.ascontiguousarray(parents, dtype=np.uint64)
+        handles = np.zeros(max(n, 1), np.uint64)
+        out = np.empty(max(int(cup[-1]), 1), np.float32)
+        self._check(self._lib.hk_score_cached(
+            self._h, n, None if par is None else par.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), int(mode),
+            tokens.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)), cu.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+            pos.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), cup.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+            out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), handles.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))))
+        new = [int(h) for h in handles[:n]] if mode == _native.HK_CACHE_PREFILL else None
+        return out[:int(cup[-1])], new
 
     def _independent(self, inputs, padded: bool) -> list:
         inputs = list(inputs)

@@ -77,6 +77,11 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(AttnArgs a) {
     const __half *Q = static_cast<const __half *>(a.q);
     const __half *K = static_cast<const __half *>(a.k);
     const __half *V = static_cast<const __half *>(a.v);
+    // A continued row's first P keys are its cached prefix; key indices below
+    // are absolute (prefix first), queries are the row's own tokens.
+    const int P = a.pre_len ? a.pre_len[row] : 0;
+    const __half *CK = P ? reinterpret_cast<const __half *>(a.kv_in[row]) : nullptr;
+    const __half *CV = P ? CK + static_cast<size_t>(P) * a.nkv * HD : nullptr;
     constexpr int CH = HD / 8;  // 16-byte chunks per row
 
     // Q tile.
@@ -94,18 +99,24 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(AttnArgs a) {
     float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
     const float sl2 = 1.4426950408889634f / sqrtf(static_cast<float>(HD));  // log2(e) / sqrt(hd)
     const int qrow0 = q0 + warp * 16 + g;  // this thread's rows: qrow0, qrow0 + 8
-    const int kv_end = min(len, q0 + BQ);   // causal: keys below the last query of the tile
+    const int kv_end = P + min(len, q0 + BQ);  // causal: keys below the last query of the tile
 
     for (int kv0 = 0; kv0 < kv_end; kv0 += BKV) {
         __syncthreads();  // previous tile fully consumed
         for (int i = tid; i < BKV * CH; i += THREADS) {
             const int r = i / CH, c = i % CH;
             const int ki = kv0 + r;
-            const bool ok = ki < len;
-            const int kvs = kv_slot(a.pages, row, start, ok ? ki : 0);
-            const size_t off = (static_cast<size_t>(kvs) * a.nkv + kh) * HD + c * 8;
-            cp_async16(sK + r * LD + c * 8, K + off, ok);
-            cp_async16(sV + r * LD + c * 8, V + off, ok);
+            const bool ok = ki < P + len;
+            if (ki < P) {
+                const size_t off = (static_cast<size_t>(ki) * a.nkv + kh) * HD + c * 8;
+                cp_async16(sK + r * LD + c * 8, CK + off, true);
+                cp_async16(sV + r * LD + c * 8, CV + off, true);
+            } else {
+                const int kvs = kv_slot(a.pages, row, start, ok ? ki - P : 0);
+                const size_t off = (static_cast<size_t>(kvs) * a.nkv + kh) * HD + c * 8;
+                cp_async16(sK + r * LD + c * 8, K + off, ok);
+                cp_async16(sV + r * LD + c * 8, V + off, ok);
+            }
         }
         cp_async_wait_all();
         __syncthreads();
@@ -132,7 +143,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(AttnArgs a) {
         }
 
         // Mask (causal and row end), online softmax in base 2.
-        const bool diag = kv0 + BKV > q0;
+        const bool diag = kv0 + BKV > P + q0;
         float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
         for (int n = 0; n < BKV / 8; ++n)
@@ -141,7 +152,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(AttnArgs a) {
                 const int key = kv0 + n * 8 + 2 * t4 + (e & 1);
                 const int q = qrow0 + (e >> 1) * 8;
                 float v = s[n][e] * sl2;
-                if (key >= len || (diag && key > q)) v = -INFINITY;
+                if (key >= P + len || (diag && key > P + q)) v = -INFINITY;
                 s[n][e] = v;
                 mx[e >> 1] = fmaxf(mx[e >> 1], v);
             }

@@ -150,6 +150,8 @@ struct ChunkArgs {
     float eps;
     __half *mix;  // GATED_OUT: out_proj input [n, ldmix]
     int ldmix;
+    // Per-row addresses of the initial / final state [nv][128][128] fp32, or 0.
+    const uint64_t *state_in, *state_out;
 };
 
 
@@ -203,9 +205,23 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
 
     // State accumulator: key rows 16*warp + {g4, g4+8}, value cols 8*nt + 2*t4 + {0,1}.
     float S[16][4];
+    const float *st_in = reinterpret_cast<const float *>(a.state_in ? a.state_in[row] : 0);
+    if (st_in) {  // a continued row starts from its cached prefix's state
+        const float *sh = st_in + static_cast<size_t>(h) * D * D;
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0.f;
-    for (int i = tid; i < D * LDH; i += THREADS) (&sm.S[0][0])[i] = __float2half_rn(0.f);
+        for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                S[nt][e] = sh[(warp * 16 + g4 + (e >> 1) * 8) * D + nt * 8 + 2 * t4 + (e & 1)];
+        for (int i = tid; i < D * LDH; i += THREADS) {
+            const int r = i / LDH, c = i % LDH;
+            (&sm.S[0][0])[i] = __float2half_rn(c < D ? sh[r * D + c] : 0.f);
+        }
+    } else {
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0.f;
+        for (int i = tid; i < D * LDH; i += THREADS) (&sm.S[0][0])[i] = __float2half_rn(0.f);
+    }
     prefetch_qkv(start);
     prefetch_z(start);
     cp_commit();
@@ -509,6 +525,13 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
         }
         __syncthreads();
     }
+    if (a.state_out && a.state_out[row]) {
+        float *sh = reinterpret_cast<float *>(a.state_out[row]) + static_cast<size_t>(h) * D * D;
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sh[(warp * 16 + g4 + (e >> 1) * 8) * D + nt * 8 + 2 * t4 + (e & 1)] = S[nt][e];
+    }
 }
 
 template <bool GO>
@@ -545,6 +568,8 @@ void launch_delta_chunk(const DeltaRecArgs &r, cudaStream_t s) {
     a.nk = r.nk;
     a.nv = r.nv;
     a.out = r.out;
+    a.state_in = r.state_in;
+    a.state_out = r.state_out;
     launch_kernel<false>(a, s);
 }
 
@@ -569,6 +594,8 @@ void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp,
     a.eps = eps;
     a.mix = mix;
     a.ldmix = ldmix;
+    a.state_in = r.state_in;
+    a.state_out = r.state_out;
     launch_kernel<true>(a, s);
 }
 

@@ -367,6 +367,64 @@ struct Model {
     uint64_t launches = 0;
     std::string last_error;
 
+    // ------------------------------------------------------------ prefix caches
+    // A cached prefix (the reference's LayerCache / ModelCache behind prefill
+    // and fork, qwen3_5.rs:1111-1125): the model state after `tokens` tokens,
+    // in one device buffer. Per delta layer, in layer order: the recurrent
+    // state [nv][dk][dv] fp32, then the conv inputs of the last taps-1 tokens
+    // [taps-1][conv_dim] fp32 (oldest first, zero before the sequence start).
+    // Then per attention layer: K then V [tokens][nkv][hd] in the activation
+    // type. A snapshot is immutable once written and handles share it, so a
+    // fork is a reference; a continued branch gets a new snapshot.
+    struct Snapshot {
+        int tokens = 0;
+        void *buf = nullptr;
+        int device = 0;
+        cudaStream_t stream = nullptr;
+        ~Snapshot() {
+            if (buf) {
+                cudaSetDevice(device);
+                cudaFreeAsync(buf, stream);
+            }
+        }
+    };
+    std::unordered_map<uint64_t, std::shared_ptr<Snapshot>> caches;
+    // Handle ids come from one process-wide counter, so a handle is never
+    // valid in another loaded model (the reference's next_cache_handle).
+    static uint64_t next_cache_id() {
+        static std::atomic<uint64_t> next{1};
+        return next.fetch_add(1);
+    }
+    std::vector<int> layer_slot;  // index among the delta layers, or among the attention layers
+    int n_delta = 0, n_attn = 0;
+    // Device table of a cached batch: 4 x [layers][HK_MAX_ROWS] addresses (in
+    // state|K, in conv history, out state|K, out conv history), then the
+    // per-row prefix lengths.
+    uint64_t *cache_meta = nullptr;
+
+    static size_t r256(size_t v) { return (v + 255) / 256 * 256; }
+    size_t delta_state_bytes() const { return static_cast<size_t>(cfg.nv) * cfg.dk * cfg.dv * 4; }
+    size_t delta_block() const {
+        return r256(delta_state_bytes() + static_cast<size_t>(cfg.taps - 1) * cfg.conv_dim() * 4);
+    }
+    size_t kv_block(int tokens) const { return r256(2 * static_cast<size_t>(tokens) * cfg.nkv * cfg.hd * esz()); }
+    size_t snapshot_bytes(int tokens) const { return n_delta * delta_block() + n_attn * kv_block(tokens); }
+    // Layer li's piece of a snapshot: delta state (conv history right after
+    // it), or attention K (V right after it).
+    uint64_t piece(const Snapshot &sn, int li) const {
+        const uint64_t b = reinterpret_cast<uint64_t>(sn.buf);
+        if (!layers[li].full) return b + layer_slot[li] * delta_block();
+        return b + n_delta * delta_block() + layer_slot[li] * kv_block(sn.tokens);
+    }
+    std::shared_ptr<Snapshot> new_snapshot(int tokens) {
+        auto sn = std::make_shared<Snapshot>();
+        sn->tokens = tokens;
+        sn->device = device;
+        sn->stream = stream;
+        HK_CUDA(cudaMallocAsync(&sn->buf, std::max<size_t>(snapshot_bytes(tokens), 256), stream));
+        return sn;
+    }
+
     // Optional per-class device timing of the forward's launches (CUDA events
     // on the handle's stream): 0 GEMM, 1 delta recurrence, 2 attention,
     // 3 delta input stage, 4 everything else.
@@ -414,6 +472,8 @@ struct Model {
 
     ~Model() {
         if (device >= 0) cudaSetDevice(device);
+        caches.clear();
+        if (stream) cudaStreamSynchronize(stream);
         for (auto &r : prof_recs) {
             cudaEventDestroy(r.a);
             cudaEventDestroy(r.b);
@@ -625,6 +685,8 @@ struct Model {
         ldf = round_up(c.ffn, 8);
         err = dev_alloc<uint32_t>(1, allocs);
         HK_CUDA(cudaMemset(err, 0, 4));
+        for (const Layer &L : layers) layer_slot.push_back(L.full ? n_attn++ : n_delta++);
+        cache_meta = dev_alloc<uint64_t>(4 * layers.size() * HK_MAX_ROWS + HK_MAX_ROWS, allocs);
     }
 
     void ensure_workspace(int tokens, int rows, int readouts) {
@@ -693,17 +755,31 @@ struct Model {
 
     // The forward over a packed batch whose description is already on the
     // device in `meta` (layout: see MetaLayout).
+    // Device view of a cached batch: per-row prefix lengths and, per layer,
+    // per-row snapshot addresses (see cache_meta); null arrays when unused.
+    struct CacheRefs {
+        const int32_t *pre_len = nullptr;
+        const uint64_t *in_a = nullptr, *in_b = nullptr, *out_a = nullptr, *out_b = nullptr;
+    };
+
     void forward(int n_rows, int n_tok, int max_len, int n_opt, const uint32_t *ids,
                  const int32_t *cu_seqlens, const int32_t *pos, const int32_t *tok_row,
                  const int32_t *ridx, const int32_t *opt_dec, float *out_logits, const KvPages &pages,
-                 const int32_t *row_order) {
+                 const int32_t *row_order, const CacheRefs *cr = nullptr) {
         const KevConfig &c = cfg;
         const int A = act();
         const size_t e = esz();
         cudaEvent_t ev = prof_begin();
         launch_embed(A, ids, n_tok, embed, c.hidden, x, stream);
         prof_end(ev, 4, 0);
-        for (const Layer &L : layers) {
+        auto at_layer = [&](const uint64_t *arr, int li) -> const uint64_t * {
+            return arr ? arr + static_cast<size_t>(li) * n_rows : nullptr;
+        };
+        for (size_t li = 0; li < layers.size(); ++li) {
+            const Layer &L = layers[li];
+            const uint64_t *in_a = cr ? at_layer(cr->in_a, li) : nullptr, *in_b = cr ? at_layer(cr->in_b, li) : nullptr;
+            const uint64_t *out_a = cr ? at_layer(cr->out_a, li) : nullptr;
+            const uint64_t *out_b = cr ? at_layer(cr->out_b, li) : nullptr;
             ev = prof_begin();
             launch_rmsnorm(A, x, c.hidden, L.in_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream);
             prof_end(ev, 4, 0);
@@ -727,6 +803,10 @@ struct Model {
                 d.v = dvv;
                 d.g = dg;
                 d.beta = db;
+                d.tok_row = tok_row;
+                d.hist_in = in_b;
+                if (out_b)
+                    launch_conv_history(proj, ldp, c.conv_dim(), c.taps, cu_seqlens, n_rows, in_b, out_b, stream);
                 if (dtype != HK_DTYPE_FP32 && c.dk == 128 && c.dv == 128 && c.taps == 4 && c.nv <= 32) {
                     // Input stage, then the chunked recurrence with the gated norm fused.
                     ev = prof_begin();
@@ -747,6 +827,8 @@ struct Model {
                     r.dv = c.dv;
                     r.out = dout;
                     r.exact = 0;
+                    r.state_in = in_a;
+                    r.state_out = out_a;
                     ev = prof_begin();
                     r.err = err;
                     launch_delta_chunk_gated(r, proj, ldp, c.conv_dim(), L.gnorm_w, c.eps, static_cast<__half *>(mix),
@@ -771,6 +853,8 @@ struct Model {
                     r.dv = c.dv;
                     r.out = dout;
                     r.exact = dtype == HK_DTYPE_FP32;
+                    r.state_in = in_a;
+                    r.state_out = out_a;
                     ev = prof_begin();
                     launch_delta_recurrent(r, stream);
                     prof_end(ev, 1, 4.0 * n_tok * c.nv * c.dk * c.dv);
@@ -798,6 +882,7 @@ struct Model {
                 p.q = aq;
                 p.k = ak;
                 p.v = av;
+                p.pre_len = cr ? cr->pre_len : nullptr;
                 ev = prof_begin();
                 launch_attn_prep(A, p, stream);
                 prof_end(ev, 4, 0);
@@ -818,6 +903,9 @@ struct Model {
                 at.out = mix;
                 at.ldo = ldmix;
                 at.pages = pages;
+                at.pre_len = cr ? cr->pre_len : nullptr;
+                at.kv_in = in_a;
+                if (out_a) launch_kv_store(A, at, out_a, stream);
                 ev = prof_begin();
                 launch_attention(A, at, stream);
                 prof_end(ev, 2, 0);
@@ -1055,7 +1143,7 @@ int hk_capabilities_get(const hk_model *h, hk_capabilities *out) {
 }
 
 static int score_device_impl(hk::Model &m, int n_rows, const int32_t *cu_h, const int32_t *cup_h,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, const hk::Model::CacheRefs *cr = nullptr) {
     (void)stream;
     const int n = cu_h[n_rows], p = cup_h[n_rows];
     int max_len = 0;
@@ -1101,73 +1189,208 @@ static int score_device_impl(hk::Model &m, int n_rows, const int32_t *cu_h, cons
     HK_LAUNCH_CHECK();
     m.forward(n_rows, n, max_len, p, reinterpret_cast<const uint32_t *>(m.meta + L.ids), m.meta + L.cu,
               m.meta + L.pos, m.meta + L.tok_row, m.meta + L.ridx, m.meta + L.opt_dec, m.logits, pages,
-              m.meta + L.row_order);
+              m.meta + L.row_order, cr);
 
     m.launches += hk::tl_launches - before;
     return HK_OK;
 }
+
+}  // extern "C"
+
+// The host-buffer scoring path shared by hk_score and hk_score_cached. pre[r]
+// is row r's cached prefix length (0 without a cache); cr the device table.
+static void score_host(hk::Model &m, int n_rows, const uint32_t *tokens, const int32_t *cu_seqlens,
+                       const int32_t *positions, const int32_t *cu_positions, float *out_logits,
+                       const std::vector<int> *pre, const hk::Model::CacheRefs *cr) {
+    // Validation mirrors forward_independent_batch (qwen3_5.rs:3143-3171)
+    // and Backend::forward (qwen3_5.rs:2669-2705).
+    if (n_rows < 1 || n_rows > HK_MAX_ROWS)
+        throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 batch must contain 1..=64 independent rows");
+    if (cu_seqlens[0] != 0 || cu_positions[0] != 0)
+        throw hk::ApiError(HK_ERR_ARGUMENT, "cu_seqlens[0] and cu_positions[0] must be 0");
+    for (int r = 0; r < n_rows; ++r) {
+        const int len = cu_seqlens[r + 1] - cu_seqlens[r];
+        const int np = cu_positions[r + 1] - cu_positions[r];
+        const int P = pre ? (*pre)[r] : 0;
+        if (len <= 0)
+            throw hk::ApiError(HK_ERR_BACKEND, P ? "cached continuation requires nonempty suffix tokens"
+                                                 : "Qwen3.5 batches require valid independent rows without cache handles");
+        if (np < 0) throw hk::ApiError(HK_ERR_ARGUMENT, "cu_positions must be non-decreasing");
+        if (P + len > m.max_context)
+            throw hk::ApiError(HK_ERR_BACKEND, "sequence length " + std::to_string(P + len) +
+                                                   " exceeds max_context " + std::to_string(m.max_context));
+        for (int i = cu_seqlens[r]; i < cu_seqlens[r + 1]; ++i)
+            if (tokens[i] >= static_cast<uint32_t>(m.cfg.vocab))
+                throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 token ID is outside the vocabulary");
+        for (int j = cu_positions[r]; j < cu_positions[r + 1]; ++j)
+            if (positions[j] < 0 || positions[j] >= len)
+                throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 readout position is outside the token sequence");
+    }
+    const int n = cu_seqlens[n_rows], p = cu_positions[n_rows];
+    HK_CUDA(cudaSetDevice(m.device));
+    m.ensure_workspace(n, n_rows, p);
+    hk::MetaLayout L(n_rows, n, p);
+    const size_t in_words = L.pos;  // ids | cu | positions | cu_pos
+    const size_t bytes = in_words * 4 + static_cast<size_t>(p) * 4 + 64;
+    if (bytes > m.pinned_cap) {
+        if (m.pinned) cudaFreeHost(m.pinned);
+        m.pinned = nullptr;
+        m.pinned_cap = 0;
+        HK_CUDA(cudaHostAlloc(&m.pinned, bytes * 2, cudaHostAllocDefault));
+        m.pinned_cap = bytes * 2;
+    }
+    int32_t *st = static_cast<int32_t *>(m.pinned);
+    std::memcpy(st + L.ids, tokens, static_cast<size_t>(n) * 4);
+    std::memcpy(st + L.cu, cu_seqlens, static_cast<size_t>(n_rows + 1) * 4);
+    if (p) std::memcpy(st + L.positions, positions, static_cast<size_t>(p) * 4);
+    std::memcpy(st + L.cu_pos, cu_positions, static_cast<size_t>(n_rows + 1) * 4);
+    HK_CUDA(cudaMemcpyAsync(m.meta, st, in_words * 4, cudaMemcpyHostToDevice, m.stream));
+    score_device_impl(m, n_rows, cu_seqlens, cu_positions, m.stream, cr);
+    float *res = reinterpret_cast<float *>(st + in_words);
+    uint32_t *errw = reinterpret_cast<uint32_t *>(res + p);
+    if (p) HK_CUDA(cudaMemcpyAsync(res, m.logits, static_cast<size_t>(p) * 4, cudaMemcpyDeviceToHost, m.stream));
+    HK_CUDA(cudaMemcpyAsync(errw, m.err, 4, cudaMemcpyDeviceToHost, m.stream));
+    HK_CUDA(cudaStreamSynchronize(m.stream));
+    if (*errw) {
+        HK_CUDA(cudaMemsetAsync(m.err, 0, 4, m.stream));
+        HK_CUDA(cudaStreamSynchronize(m.stream));
+        throw hk::ApiError(HK_ERR_CUDA, "device error flag " + std::to_string(*errw) + " set during the forward");
+    }
+    if (p) std::memcpy(out_logits, res, static_cast<size_t>(p) * 4);
+}
+
+extern "C" {
 
 int hk_score(hk_model *h, int n_rows, const uint32_t *tokens, const int32_t *cu_seqlens,
              const int32_t *positions, const int32_t *cu_positions, float *out_logits) {
     if (!h || !h->m || !cu_seqlens || !cu_positions) return HK_ERR_ARGUMENT;
     hk::Model &m = *h->m;
     return guarded(h, [&]() -> int {
-        // Validation mirrors forward_independent_batch (qwen3_5.rs:3143-3171)
-        // and Backend::forward (qwen3_5.rs:2669-2705).
-        if (n_rows < 1 || n_rows > HK_MAX_ROWS)
-            throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 batch must contain 1..=64 independent rows");
-        if (cu_seqlens[0] != 0 || cu_positions[0] != 0)
-            throw hk::ApiError(HK_ERR_ARGUMENT, "cu_seqlens[0] and cu_positions[0] must be 0");
-        for (int r = 0; r < n_rows; ++r) {
-            const int len = cu_seqlens[r + 1] - cu_seqlens[r];
-            const int np = cu_positions[r + 1] - cu_positions[r];
-            if (len <= 0)
-                throw hk::ApiError(HK_ERR_BACKEND,
-                                   "Qwen3.5 batches require valid independent rows without cache handles");
-            if (np < 0) throw hk::ApiError(HK_ERR_ARGUMENT, "cu_positions must be non-decreasing");
-            if (len > m.max_context)
-                throw hk::ApiError(HK_ERR_BACKEND, "sequence length " + std::to_string(len) +
-                                                       " exceeds max_context " + std::to_string(m.max_context));
-            for (int i = cu_seqlens[r]; i < cu_seqlens[r + 1]; ++i)
-                if (tokens[i] >= static_cast<uint32_t>(m.cfg.vocab))
-                    throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 token ID is outside the vocabulary");
-            for (int j = cu_positions[r]; j < cu_positions[r + 1]; ++j)
-                if (positions[j] < 0 || positions[j] >= len)
-                    throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 readout position is outside the token sequence");
-        }
-        const int n = cu_seqlens[n_rows], p = cu_positions[n_rows];
-        HK_CUDA(cudaSetDevice(m.device));
-        m.ensure_workspace(n, n_rows, p);
-        hk::MetaLayout L(n_rows, n, p);
-        const size_t in_words = L.pos;  // ids | cu | positions | cu_pos
-        const size_t bytes = in_words * 4 + static_cast<size_t>(p) * 4 + 64;
-        if (bytes > m.pinned_cap) {
-            if (m.pinned) cudaFreeHost(m.pinned);
-            m.pinned = nullptr;
-            m.pinned_cap = 0;
-            HK_CUDA(cudaHostAlloc(&m.pinned, bytes * 2, cudaHostAllocDefault));
-            m.pinned_cap = bytes * 2;
-        }
-        int32_t *st = static_cast<int32_t *>(m.pinned);
-        std::memcpy(st + L.ids, tokens, static_cast<size_t>(n) * 4);
-        std::memcpy(st + L.cu, cu_seqlens, static_cast<size_t>(n_rows + 1) * 4);
-        if (p) std::memcpy(st + L.positions, positions, static_cast<size_t>(p) * 4);
-        std::memcpy(st + L.cu_pos, cu_positions, static_cast<size_t>(n_rows + 1) * 4);
-        HK_CUDA(cudaMemcpyAsync(m.meta, st, in_words * 4, cudaMemcpyHostToDevice, m.stream));
-        score_device_impl(m, n_rows, cu_seqlens, cu_positions, m.stream);
-        float *res = reinterpret_cast<float *>(st + in_words);
-        uint32_t *errw = reinterpret_cast<uint32_t *>(res + p);
-        if (p) HK_CUDA(cudaMemcpyAsync(res, m.logits, static_cast<size_t>(p) * 4, cudaMemcpyDeviceToHost, m.stream));
-        HK_CUDA(cudaMemcpyAsync(errw, m.err, 4, cudaMemcpyDeviceToHost, m.stream));
-        HK_CUDA(cudaStreamSynchronize(m.stream));
-        if (*errw) {
-            HK_CUDA(cudaMemsetAsync(m.err, 0, 4, m.stream));
-            HK_CUDA(cudaStreamSynchronize(m.stream));
-            throw hk::ApiError(HK_ERR_CUDA, "device error flag " + std::to_string(*errw) + " set during the forward");
-        }
-        if (p) std::memcpy(out_logits, res, static_cast<size_t>(p) * 4);
+        score_host(m, n_rows, tokens, cu_seqlens, positions, cu_positions, out_logits, nullptr, nullptr);
         return HK_OK;
     });
+}
+
+int hk_score_cached(hk_model *h, int n_rows, const uint64_t *parents, int mode, const uint32_t *tokens,
+                    const int32_t *cu_seqlens, const int32_t *positions, const int32_t *cu_positions,
+                    float *out_logits, uint64_t *handles_out) {
+    if (!h || !h->m || !cu_seqlens || !cu_positions) return HK_ERR_ARGUMENT;
+    if (mode != HK_CACHE_BRANCH && mode != HK_CACHE_CONTINUE && mode != HK_CACHE_PREFILL) return HK_ERR_ARGUMENT;
+    if (mode == HK_CACHE_PREFILL && !handles_out) return HK_ERR_ARGUMENT;
+    hk::Model &m = *h->m;
+    return guarded(h, [&]() -> int {
+        using Snap = hk::Model::Snapshot;
+        if (n_rows < 1 || n_rows > HK_MAX_ROWS)
+            throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 batch must contain 1..=64 independent rows");
+        HK_CUDA(cudaSetDevice(m.device));
+        std::vector<std::shared_ptr<Snap>> in(n_rows), out(n_rows);
+        std::vector<int> pre(n_rows, 0);
+        for (int r = 0; r < n_rows; ++r) {
+            const uint64_t id = parents ? parents[r] : 0;
+            if (id) {
+                auto it = m.caches.find(id);
+                if (it == m.caches.end()) throw hk::ApiError(HK_ERR_BACKEND, "unknown Qwen3.5 cache handle");
+                in[r] = it->second;
+                pre[r] = in[r]->tokens;
+            } else if (mode == HK_CACHE_CONTINUE) {
+                throw hk::ApiError(HK_ERR_ARGUMENT, "every continued row needs a cache handle");
+            }
+            if (mode == HK_CACHE_CONTINUE)
+                for (int q = 0; q < r; ++q)
+                    if (parents[q] == id)
+                        throw hk::ApiError(HK_ERR_ARGUMENT, "a cache handle can be continued by one row per call");
+        }
+        const int NL = static_cast<int>(m.layers.size());
+        for (int r = 0; r < n_rows; ++r) {
+            const int len = cu_seqlens[r + 1] - cu_seqlens[r];
+            if (mode != HK_CACHE_BRANCH && len > 0 && pre[r] + len <= m.max_context) out[r] = m.new_snapshot(pre[r] + len);
+        }
+        bool any_in = false, any_out = mode != HK_CACHE_BRANCH;
+        for (auto &sp : in) any_in = any_in || sp;
+        // Per-layer, per-row snapshot addresses and the prefix lengths.
+        const size_t LR = static_cast<size_t>(NL) * n_rows;
+        std::vector<uint64_t> tab(4 * LR + (n_rows + 1) / 2, 0);
+        for (int li = 0; li < NL; ++li)
+            for (int r = 0; r < n_rows; ++r) {
+                const size_t k = static_cast<size_t>(li) * n_rows + r;
+                const bool delta = !m.layers[li].full;
+                if (in[r]) {
+                    tab[k] = m.piece(*in[r], li);
+                    if (delta) tab[LR + k] = tab[k] + m.delta_state_bytes();
+                }
+                if (out[r]) {
+                    tab[2 * LR + k] = m.piece(*out[r], li);
+                    if (delta) tab[3 * LR + k] = tab[2 * LR + k] + m.delta_state_bytes();
+                }
+            }
+        std::memcpy(reinterpret_cast<int32_t *>(tab.data() + 4 * LR), pre.data(), static_cast<size_t>(n_rows) * 4);
+        {
+            hk::Model::HostStage &stg = m.stage_acquire(tab.size() * 8);
+            std::memcpy(stg.p, tab.data(), tab.size() * 8);
+            HK_CUDA(cudaMemcpyAsync(m.cache_meta, stg.p, tab.size() * 8, cudaMemcpyHostToDevice, m.stream));
+            HK_CUDA(cudaEventRecord(stg.done, m.stream));
+        }
+        hk::Model::CacheRefs cr;
+        cr.pre_len = reinterpret_cast<const int32_t *>(m.cache_meta + 4 * LR);
+        if (any_in) {
+            cr.in_a = m.cache_meta;
+            cr.in_b = m.cache_meta + LR;
+        }
+        if (any_out) {
+            cr.out_a = m.cache_meta + 2 * LR;
+            cr.out_b = m.cache_meta + 3 * LR;
+        }
+        score_host(m, n_rows, tokens, cu_seqlens, positions, cu_positions, out_logits, &pre, &cr);
+        // Commit only after the whole forward succeeded (qwen3_5.rs:2745-2751).
+        for (int r = 0; r < n_rows; ++r) {
+            if (mode == HK_CACHE_CONTINUE) {
+                m.caches[parents[r]] = out[r];
+            } else if (mode == HK_CACHE_PREFILL) {
+                const uint64_t id = hk::Model::next_cache_id();
+                m.caches[id] = out[r];
+                handles_out[r] = id;
+            }
+        }
+        return HK_OK;
+    });
+}
+
+int hk_prefill(hk_model *h, int n_rows, const uint32_t *tokens, const int32_t *cu_seqlens, uint64_t *handles_out) {
+    if (!h || !h->m || !cu_seqlens || !handles_out || n_rows < 1 || n_rows > HK_MAX_ROWS) return HK_ERR_ARGUMENT;
+    std::vector<int32_t> cup(static_cast<size_t>(n_rows) + 1, 0);
+    return hk_score_cached(h, n_rows, nullptr, HK_CACHE_PREFILL, tokens, cu_seqlens, nullptr, cup.data(), nullptr,
+                           handles_out);
+}
+
+int hk_fork(hk_model *h, uint64_t handle, uint64_t *out) {
+    if (!h || !h->m || !out) return HK_ERR_ARGUMENT;
+    hk::Model &m = *h->m;
+    auto it = m.caches.find(handle);
+    if (it == m.caches.end()) return fail(h, HK_ERR_BACKEND, "unknown Qwen3.5 cache handle");
+    const uint64_t id = hk::Model::next_cache_id();
+    m.caches[id] = it->second;
+    *out = id;
+    return HK_OK;
+}
+
+int hk_release_cache(hk_model *h, uint64_t handle) {
+    if (!h || !h->m) return HK_ERR_ARGUMENT;
+    hk::Model &m = *h->m;
+    return guarded(h, [&]() -> int {
+        HK_CUDA(cudaSetDevice(m.device));
+        if (!m.caches.erase(handle)) throw hk::ApiError(HK_ERR_BACKEND, "unknown Qwen3.5 cache handle");
+        return HK_OK;
+    });
+}
+
+int hk_cache_info(const hk_model *h, uint64_t handle, int *tokens, int64_t *bytes) {
+    if (!h || !h->m || !tokens || !bytes) return HK_ERR_ARGUMENT;
+    const hk::Model &m = *h->m;
+    auto it = m.caches.find(handle);
+    if (it == m.caches.end()) return HK_ERR_BACKEND;
+    *tokens = it->second->tokens;
+    *bytes = static_cast<int64_t>(m.snapshot_bytes(it->second->tokens));
+    return HK_OK;
 }
 
 int hk_score_device(hk_model *h, int n_rows, const int32_t *cu_seqlens_host, const int32_t *cu_positions_host,

@@ -61,12 +61,21 @@ __global__ void delta_prep_kernel(DeltaPrepArgs a) {
     const int conv_dim = 2 * key_dim + value_dim;
     const int pos = a.pos[t];
     const float *proj = a.proj;
+    // Taps before the row start read the cached prefix's conv inputs (hist
+    // row taps-1+q for relative index q < 0), or nothing without a cache.
+    const uint64_t haddr = (a.hist_in && a.tok_row) ? a.hist_in[a.tok_row[t]] : 0;
+    const float *hist = reinterpret_cast<const float *>(haddr);
     for (int c = threadIdx.x; c < conv_dim; c += blockDim.x) {
         float acc = 0.f;
         for (int tap = 0; tap < a.taps; ++tap) {
             const int shift = a.taps - 1 - tap;
-            if (shift > pos) continue;
-            const float xv = proj[static_cast<size_t>(t - shift) * a.ldp + c];
+            float xv;
+            if (shift > pos) {
+                if (!hist) continue;
+                xv = hist[static_cast<size_t>(a.taps - 1 + pos - shift) * conv_dim + c];
+            } else {
+                xv = proj[static_cast<size_t>(t - shift) * a.ldp + c];
+            }
             acc = __fadd_rn(acc, __fmul_rn(a.conv_w[c * a.taps + tap], xv));
         }
         conv_s[c] = silu_f(acc);
@@ -133,17 +142,32 @@ __global__ void delta_prep_vec_kernel(DeltaPrepArgs a) {
     for (int c = 0; c < 4; ++c)
 #pragma unroll
         for (int k = 0; k < 4; ++k) w[c][k] = a.conv_w[(c0 + c) * 4 + k];
-    // History x[t-3], x[t-2], x[t-1] for the 4 channels (zero outside the row).
-    float4 h3 = make_float4(0.f, 0.f, 0.f, 0.f), h2 = h3, h1 = h3;
+    // History x[t-3], x[t-2], x[t-1] for the 4 channels: inside the row from
+    // proj, before its start from the row's cached conv inputs (hist row 3+q
+    // for relative index q), else zero.
+    auto before_row = [&](int t, int q) {
+        const uint64_t addr = (a.hist_in && a.tok_row) ? a.hist_in[a.tok_row[t]] : 0;
+        if (!addr) return make_float4(0.f, 0.f, 0.f, 0.f);
+        return *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(addr) +
+                                                 static_cast<size_t>(3 + q) * conv_dim + c0);
+    };
+    float4 h3, h2, h1;
     {
         const int p0 = a.pos[t0];
-        if (p0 >= 3) h3 = *reinterpret_cast<const float4 *>(a.proj + static_cast<size_t>(t0 - 3) * a.ldp + c0);
-        if (p0 >= 2) h2 = *reinterpret_cast<const float4 *>(a.proj + static_cast<size_t>(t0 - 2) * a.ldp + c0);
-        if (p0 >= 1) h1 = *reinterpret_cast<const float4 *>(a.proj + static_cast<size_t>(t0 - 1) * a.ldp + c0);
+        h3 = p0 >= 3 ? *reinterpret_cast<const float4 *>(a.proj + static_cast<size_t>(t0 - 3) * a.ldp + c0)
+                     : before_row(t0, p0 - 3);
+        h2 = p0 >= 2 ? *reinterpret_cast<const float4 *>(a.proj + static_cast<size_t>(t0 - 2) * a.ldp + c0)
+                     : before_row(t0, p0 - 2);
+        h1 = p0 >= 1 ? *reinterpret_cast<const float4 *>(a.proj + static_cast<size_t>(t0 - 1) * a.ldp + c0)
+                     : before_row(t0, p0 - 1);
     }
     const float qscale = 1.0f / sqrtf(128.0f);
     for (int t = t0; t < t1; ++t) {
-        if (a.pos[t] == 0) h3 = h2 = h1 = make_float4(0.f, 0.f, 0.f, 0.f);  // a new row starts
+        if (a.pos[t] == 0 && t > t0) {  // a new row starts
+            h3 = before_row(t, -3);
+            h2 = before_row(t, -2);
+            h1 = before_row(t, -1);
+        }
         const float4 x = *reinterpret_cast<const float4 *>(a.proj + static_cast<size_t>(t) * a.ldp + c0);
         const float xs[4][4] = {{h3.x, h2.x, h1.x, x.x}, {h3.y, h2.y, h1.y, x.y},
                                 {h3.z, h2.z, h1.z, x.z}, {h3.w, h2.w, h1.w, x.w}};
@@ -185,9 +209,14 @@ __global__ void __launch_bounds__(128) delta_recurrent_kernel(DeltaRecArgs a) {
     const int j = threadIdx.x;
     const int kh = h / (a.nv / a.nk);  // repeat_interleave of key heads (qwen3_5.rs:901-915)
     const int start = a.cu_seqlens[row], end = a.cu_seqlens[row + 1];
+    const uint64_t sin = a.state_in ? a.state_in[row] : 0, sout = a.state_out ? a.state_out[row] : 0;
     float S[DK];
+    {
+        const float *st = reinterpret_cast<const float *>(sin);
 #pragma unroll
-    for (int i = 0; i < DK; ++i) S[i] = 0.f;
+        for (int i = 0; i < DK; ++i)
+            S[i] = (st && j < a.dv) ? st[(static_cast<size_t>(h) * DK + i) * a.dv + j] : 0.f;
+    }
     int buf = 0;
     for (int t = start; t < end; ++t) {
         for (int i = threadIdx.x; i < DK; i += blockDim.x) {
@@ -235,6 +264,11 @@ __global__ void __launch_bounds__(128) delta_recurrent_kernel(DeltaRecArgs a) {
             a.out[(static_cast<size_t>(t) * a.nv + h) * a.dv + j] = o;
         }
         buf ^= 1;
+    }
+    if (sout && j < a.dv) {
+        float *st = reinterpret_cast<float *>(sout);
+#pragma unroll
+        for (int i = 0; i < DK; ++i) st[(static_cast<size_t>(h) * DK + i) * a.dv + j] = S[i];
     }
 }
 
@@ -361,7 +395,7 @@ __global__ void attn_prep_kernel(AttnPrepArgs a) {
     const float denom = sqrtf(ss / static_cast<float>(a.hd) + a.eps);
     for (int i = lane; i < a.hd; i += 32) buf[i] = (src[i] / denom) * w[i];
     __syncwarp();
-    const float p = static_cast<float>(a.pos[t]);
+    const float p = static_cast<float>(a.pos[t] + (a.pre_len ? a.pre_len[a.tok_row[t]] : 0));
     const int half = a.rd / 2;
     const int kvs = is_q ? t : kv_slot(a.pages, a.tok_row[t], t - a.pos[t], a.pos[t]);
     T *dst = (is_q ? static_cast<T *>(a.q) + (static_cast<size_t>(t) * a.nh + h) * a.hd
@@ -404,9 +438,14 @@ __global__ void attn_simt_kernel(AttnArgs a) {
     }
     const float scale = 1.0f / sqrtf(static_cast<float>(a.hd));
     float m = -INFINITY, l = 0.f;
-    for (int s = start; s <= t; ++s) {
-        const int kvs = kv_slot(a.pages, row, start, s - start);
-        const T *k = static_cast<const T *>(a.k) + (static_cast<size_t>(kvs) * a.nkv + kh) * a.hd;
+    // Keys: the row's cached prefix (P tokens) then its own tokens up to t.
+    const int P = a.pre_len ? a.pre_len[row] : 0;
+    const T *ck = P ? reinterpret_cast<const T *>(a.kv_in[row]) : nullptr;
+    const T *cv = P ? ck + static_cast<size_t>(P) * a.nkv * a.hd : nullptr;
+    for (int s = start - P; s <= t; ++s) {
+        const int kvs = s >= start ? kv_slot(a.pages, row, start, s - start) : 0;
+        const T *k = s >= start ? static_cast<const T *>(a.k) + (static_cast<size_t>(kvs) * a.nkv + kh) * a.hd
+                                : ck + (static_cast<size_t>(s - start + P) * a.nkv + kh) * a.hd;
         float dot = 0.f;
 #pragma unroll
         for (int e = 0; e < MAXE; ++e) {
@@ -418,7 +457,8 @@ __global__ void attn_simt_kernel(AttnArgs a) {
         const float corr = expf(m - mn);
         const float pw = expf(dot - mn);
         l = l * corr + pw;
-        const T *v = static_cast<const T *>(a.v) + (static_cast<size_t>(kvs) * a.nkv + kh) * a.hd;
+        const T *v = s >= start ? static_cast<const T *>(a.v) + (static_cast<size_t>(kvs) * a.nkv + kh) * a.hd
+                                : cv + (static_cast<size_t>(s - start + P) * a.nkv + kh) * a.hd;
 #pragma unroll
         for (int e = 0; e < MAXE; ++e) {
             const int i = lane + 32 * e;
@@ -518,6 +558,72 @@ void launch_rmsnorm(int act, const float *x, int ldx, const float *w_eff, float 
     HK_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------------------------ snapshots
+// Conv history for a row's output snapshot: the last H = taps-1 entries of
+// [hist_in (H rows) ; own qkv rows (L)], i.e. concat index L + hrow.
+__global__ void conv_history_kernel(const float *proj, int ldp, int conv_dim, int taps, const int32_t *cu,
+                                    const uint64_t *hist_in, const uint64_t *hist_out) {
+    const int r = blockIdx.x;
+    const uint64_t oaddr = hist_out[r];
+    if (!oaddr) return;
+    const int start = cu[r], L = cu[r + 1] - start, H = taps - 1;
+    const float *in = reinterpret_cast<const float *>(hist_in ? hist_in[r] : 0);
+    float *out = reinterpret_cast<float *>(oaddr);
+    for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < H * conv_dim; i += gridDim.y * blockDim.x) {
+        const int hrow = i / conv_dim, c = i % conv_dim, q = L + hrow;
+        out[i] = q < H ? (in ? in[static_cast<size_t>(q) * conv_dim + c] : 0.f)
+                       : proj[static_cast<size_t>(start + q - H) * ldp + c];
+    }
+}
+
+// K/V of a row's output snapshot: prefix keys from kv_in, then own keys from
+// the workspace slots; one CTA per (row, block of key positions).
+template <typename T>
+__global__ void kv_store_kernel(AttnArgs a, const uint64_t *kv_out) {
+    const int r = blockIdx.x;
+    const uint64_t oaddr = kv_out[r];
+    if (!oaddr) return;
+    const int start = a.cu_seqlens[r], L = a.cu_seqlens[r + 1] - start;
+    const int P = a.pre_len ? a.pre_len[r] : 0, total = P + L;
+    const size_t unit = static_cast<size_t>(a.nkv) * a.hd;
+    const T *ck = P ? reinterpret_cast<const T *>(a.kv_in[r]) : nullptr;
+    T *ok = reinterpret_cast<T *>(oaddr), *ov = ok + static_cast<size_t>(total) * unit;
+    for (size_t i = blockIdx.y * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total * unit;
+         i += static_cast<size_t>(gridDim.y) * blockDim.x) {
+        const int j = static_cast<int>(i / unit);
+        const size_t e = i % unit;
+        T kx, vx;
+        if (j < P) {
+            kx = ck[static_cast<size_t>(j) * unit + e];
+            vx = ck[static_cast<size_t>(P + j) * unit + e];
+        } else {
+            const size_t slot = static_cast<size_t>(kv_slot(a.pages, r, start, j - P));
+            kx = static_cast<const T *>(a.k)[slot * unit + e];
+            vx = static_cast<const T *>(a.v)[slot * unit + e];
+        }
+        ok[i] = kx;
+        ov[i] = vx;
+    }
+}
+
+void launch_conv_history(const float *proj, int ldp, int conv_dim, int taps, const int32_t *cu_seqlens, int n_rows,
+                         const uint64_t *hist_in, const uint64_t *hist_out, cudaStream_t s) {
+    if (n_rows <= 0 || !hist_out || taps <= 1) return;
+    dim3 grid(n_rows, ceil_div((taps - 1) * conv_dim, 256 * 4));
+    conv_history_kernel<<<grid, 256, 0, s>>>(proj, ldp, conv_dim, taps, cu_seqlens, hist_in, hist_out);
+    HK_LAUNCH_CHECK();
+}
+
+void launch_kv_store(int act, const AttnArgs &a, const uint64_t *kv_out, cudaStream_t s) {
+    if (a.n_rows <= 0 || !kv_out) return;
+    dim3 grid(a.n_rows, 64);
+    if (act == kActF32)
+        kv_store_kernel<float><<<grid, 256, 0, s>>>(a, kv_out);
+    else
+        kv_store_kernel<__half><<<grid, 256, 0, s>>>(a, kv_out);
+    HK_LAUNCH_CHECK();
+}
+
 void launch_delta_prep(const DeltaPrepArgs &a, cudaStream_t s) {
     if (a.n <= 0) return;
     if (a.dk == 128 && a.dv == 128 && a.taps == 4 && a.nv <= 32 && (a.ldp % 4) == 0) {
@@ -536,7 +642,7 @@ void launch_delta_prep(const DeltaPrepArgs &a, cudaStream_t s) {
 
 template <int DK>
 static void launch_rec_dk(const DeltaRecArgs &a, cudaStream_t s) {
-    if (DK == 128 && !a.exact && a.dv <= 128) {
+    if (DK == 128 && !a.exact && a.dv <= 128 && !a.state_in && !a.state_out) {
         dim3 grid(a.n_rows, a.nv);
         delta_recurrent_split_kernel<128, 4, 4><<<grid, 512, 0, s>>>(a);
         return;
@@ -551,7 +657,7 @@ static void launch_rec_dk(const DeltaRecArgs &a, cudaStream_t s) {
 
 void launch_delta_recurrent(const DeltaRecArgs &a, cudaStream_t s) {
     if (a.n_rows <= 0) return;
-    if (!a.exact && delta_tc_supported(a)) {
+    if (!a.exact && !a.state_in && !a.state_out && delta_tc_supported(a)) {
         launch_delta_tc(a, s);
         return;
     }

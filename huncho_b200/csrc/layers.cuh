@@ -38,8 +38,19 @@ struct DeltaPrepArgs {
     float *q, *k;  // [n, nk, dk] fp32
     float *v;      // [n, nv, dv] fp32
     float *g, *beta;  // [n, nv] fp32
+    // Continued rows (a fork of a cached prefix): hist_in[row] is the device
+    // address of the row's conv history [taps-1][conv_dim] fp32 (the prefix's
+    // last pre-conv inputs, oldest first), or 0 for none (zero history).
+    const int32_t *tok_row = nullptr;
+    const uint64_t *hist_in = nullptr;
 };
 void launch_delta_prep(const DeltaPrepArgs &a, cudaStream_t s);
+
+// Conv history of each row for its output snapshot: the last taps-1 pre-conv
+// inputs of [hist_in rows ; the row's own qkv projection rows] written to
+// hist_out[row] (rows with hist_out 0 are skipped).
+void launch_conv_history(const float *proj, int ldp, int conv_dim, int taps, const int32_t *cu_seqlens, int n_rows,
+                         const uint64_t *hist_in, const uint64_t *hist_out, cudaStream_t s);
 
 // Per-token gated delta rule with an fp32 state per (row, value head)
 // (qwen3_5.rs:950-987). `exact` keeps the reference's ascending-key fp32
@@ -52,6 +63,10 @@ struct DeltaRecArgs {
     float *out;  // [n, nv, dv]
     int exact;
     uint32_t *err = nullptr;  // device error word (bounded waits)
+    // Per-row device addresses of the initial state and of where to write the
+    // final state, both [nv][dk][dv] fp32 (S[h][i][j], i the key index); 0 (or
+    // a null array) means a zero initial state / no write.
+    const uint64_t *state_in = nullptr, *state_out = nullptr;
 };
 void launch_delta_recurrent(const DeltaRecArgs &a, cudaStream_t s);
 // The chunked tcgen05 form behind launch_delta_recurrent (non-exact mode,
@@ -105,6 +120,7 @@ struct AttnPrepArgs {
     float eps;
     void *q, *k, *v;  // q [n, nh, hd]; k, v [slots, nkv, hd] at kv_slot()
     KvPages pages;
+    const int32_t *pre_len = nullptr;  // per row: cached prefix tokens (RoPE offset), or null
 };
 void launch_attn_prep(int act, const AttnPrepArgs &a, cudaStream_t s);
 
@@ -120,8 +136,17 @@ struct AttnArgs {
     void *out;
     int ldo;
     KvPages pages;
+    // Continued rows: the row's first pre_len[row] keys come from its cached
+    // prefix at kv_in[row] (K [P][nkv][hd] then V [P][nkv][hd], activation
+    // type); its own tokens follow at absolute positions P, P+1, ...
+    const int32_t *pre_len = nullptr;
+    const uint64_t *kv_in = nullptr;
 };
 void launch_attention(int act, const AttnArgs &a, cudaStream_t s);
+// Output snapshot K/V of each row with kv_out[row] != 0: the cached prefix
+// keys (from kv_in) then the row's own keys (from the workspace slots), as
+// K [P+L][nkv][hd] then V [P+L][nkv][hd].
+void launch_kv_store(int act, const AttnArgs &a, const uint64_t *kv_out, cudaStream_t s);
 // The tensor-core (fp16) kernel behind launch_attention for head_dim 64/128/256.
 bool attention_tc_supported(int hd);
 void launch_attention_tc(const AttnArgs &a, cudaStream_t s);

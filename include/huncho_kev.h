@@ -106,6 +106,53 @@ int hk_score(hk_model *m, int n_rows, const uint32_t *tokens, const int32_t *cu_
              const int32_t *positions, const int32_t *cu_positions, float *out_logits);
 
 /*
+ * Cached prefixes (prefill / fork). A cache handle names the model state after
+ * a token sequence: every delta layer's recurrent state and conv tail, every
+ * attention layer's K/V (the reference's LayerCache, qwen3_5.rs:1111-1125),
+ * held in device memory. Handles are 64-bit ids; 0 is never a handle.
+ *
+ * hk_score_cached scores rows that may each continue a cached prefix:
+ *   parents      [n_rows] handle per row, 0 for an independent row (or NULL
+ *                for none); a row's tokens are the suffix after its prefix,
+ *                its positions are relative to the suffix, and its attention
+ *                and RoPE positions continue at the prefix length.
+ *   mode         HK_CACHE_BRANCH: rows read their parents and leave them
+ *                unchanged (Backend::forward_fork_batch and
+ *                forward_padded_fork_batch, qwen3_5.rs:2780-2804, across any
+ *                number of parents in one call);
+ *                HK_CACHE_CONTINUE: each row's handle advances to the state
+ *                after its suffix (Backend::forward with fork_from,
+ *                qwen3_5.rs:2676-2751); every row needs a distinct handle;
+ *                HK_CACHE_PREFILL: each row's final state becomes a new handle
+ *                in handles_out[r] (a row with a parent extends it).
+ *   out_logits   as hk_score. State commits only after the whole call
+ *                succeeds. Errors: unknown handle or empty suffix ->
+ *                HK_ERR_BACKEND; prefix + suffix beyond max_context ->
+ *                HK_ERR_BACKEND.
+ */
+#define HK_CACHE_BRANCH 0
+#define HK_CACHE_CONTINUE 1
+#define HK_CACHE_PREFILL 2
+int hk_score_cached(hk_model *m, int n_rows, const uint64_t *parents, int mode, const uint32_t *tokens,
+                    const int32_t *cu_seqlens, const int32_t *positions, const int32_t *cu_positions,
+                    float *out_logits, uint64_t *handles_out);
+
+/* Backend::prefill (qwen3_5.rs:2833-2835) for n_rows prefixes at once: one
+ * new handle per row in handles_out, no readout. */
+int hk_prefill(hk_model *m, int n_rows, const uint32_t *tokens, const int32_t *cu_seqlens, uint64_t *handles_out);
+
+/* Backend::fork (qwen3_5.rs:2818-2831): a new handle for the same state. The
+ * state is shared, not copied; continuing either handle leaves the other. */
+int hk_fork(hk_model *m, uint64_t handle, uint64_t *out);
+
+/* Backend::release_cache (qwen3_5.rs:2837-2846). Releasing a parent leaves its
+ * forks valid. Unknown handle -> HK_ERR_BACKEND. */
+int hk_release_cache(hk_model *m, uint64_t handle);
+
+/* Tokens a handle covers and the device bytes its state occupies. */
+int hk_cache_info(const hk_model *m, uint64_t handle, int *tokens, int64_t *bytes);
+
+/*
  * The same forward with device-resident inputs and output, enqueued on
  * `stream` (a cudaStream_t; NULL = the handle's own stream) without a host
  * synchronisation. Host copies of the two offset arrays are still needed to
