@@ -188,6 +188,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=None,
                     help="requests per GPU (default: the config's); smaller cases are for profiling")
+    ap.add_argument("--prefix-cache", action="store_true",
+                    help="score each request's questions as branches of its cached shared prefix (the reference "
+                         "engine's prefix_cache option: prefill + fork); default: independent rows")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -251,6 +254,55 @@ def main():
             backend.score_device(cu, cup, dev["tok"].data_ptr(), dev["cu"].data_ptr(), dev["pos"].data_ptr(),
                                  dev["out"].data_ptr(), stream.cuda_stream)
 
+    # Prefix-cache mode: per request, the longest common prefix of its rows
+    # that leaves every readout in the suffix is prefilled once; each question
+    # is then scored as a branch of it (eng:878-960 with prefix_cache).
+    fork_plan = None
+    if args.prefix_cache:
+        from huncho_b200 import _native
+        by_req = {}
+        for i, r in enumerate(wl.request_of):
+            by_req.setdefault(r, []).append(i)
+        reqs_rows = [by_req[k] for k in sorted(by_req)]
+        prefixes, suffixes = [], []
+        for q in reqs_rows:
+            rows_q = [wl.rows[i] for i in q]
+            p = min(len(r) for r in rows_q)
+            for r in rows_q[1:]:
+                p = min(p, next((j for j, (x, y) in enumerate(zip(rows_q[0], r)) if x != y), p))
+            p = min([p] + [min(wl.positions[i]) for i in q])
+            prefixes.append(list(rows_q[0][:p]))
+            for i in q:
+                suffixes.append((len(prefixes) - 1, i, list(wl.rows[i][p:]), [x - p for x in wl.positions[i]]))
+        lim = _native.HK_MAX_CACHED_ROWS
+        pre_groups = [list(range(a, min(len(prefixes), a + lim))) for a in range(0, len(prefixes), lim)]
+        row_groups = [suffixes[a:a + lim] for a in range(0, len(suffixes), lim)]
+        packed_rows = [(grp, pack_rows([x[2] for x in grp], [x[3] for x in grp])) for grp in row_groups]
+        fork_plan = (prefixes, pre_groups, packed_rows)
+
+    def fork_step(answers: bool):
+        prefixes, pre_groups, packed_rows = fork_plan
+        handles = []
+        for g in pre_groups:
+            handles += backend.prefill_batch([prefixes[j] for j in g])
+        for grp, args_ in packed_rows:
+            logits, _ = backend.score_cached(*args_, parents=[handles[x[0]] for x in grp],
+                                             mode=_native.HK_CACHE_BRANCH)
+            if answers:
+                cup = args_[3]
+                for j, x in enumerate(grp):
+                    lo, hi = int(cup[j]), int(cup[j + 1])
+                    probs = calibration.calibrate(logits[lo:hi], backend.temperature)
+                    q = engine.Question(wl.qtypes[x[1]], labels=[str(v) for v in range(hi - lo)],
+                                        descriptions=["" for _ in range(hi - lo)])
+                    engine.build_answer(q, engine.candidates_for(q, wl.positions[x[1]]), probs)
+        for h in handles:
+            backend.release_cache(h)
+
+    if fork_plan is not None:
+        def device_step():  # noqa: F811 -- the native calls synchronise; timed on the host clock
+            fork_step(False)
+
     # warm-up (also sizes the workspace)
     for _ in range(args.warmup):
         flush.zero_()
@@ -261,12 +313,19 @@ def main():
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     launches0 = backend.kernel_launches
-    backend.profile(True)
+    backend.profile(fork_plan is None)
     barrier()
     torch.cuda.synchronize()
+    host_ms = []
     with ClockSampler(local) as clk:
         for k in range(args.steps):
             flush.zero_()
+            if fork_plan is not None:
+                torch.cuda.synchronize()
+                ts = time.perf_counter()
+                device_step()
+                host_ms.append(1000.0 * (time.perf_counter() - ts))
+                continue
             starts[k].record(stream)
             device_step()
             ends[k].record(stream)
@@ -275,14 +334,22 @@ def main():
     backend.profile(False)
     prof = backend.profile_read()
     launches = backend.kernel_launches - launches0
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    step_ms = host_ms if fork_plan is not None else [s.elapsed_time(e) for s, e in zip(starts, ends)]
     dev_total_s = max_over_ranks(sum(step_ms) / 1000.0)
 
     # ---- e2e: the public host API, host calibration and answers included
     h2d = sum(tok.nbytes + cu.nbytes + pos.nbytes + cup.nbytes for _, tok, cu, pos, cup, _ in packed)
     d2h = sum(4 * int(cup[-1]) + 4 for _, _, _, _, cup, _ in packed)
 
+    if fork_plan is not None:
+        h2d = sum(4 * len(p) + 8 for p in fork_plan[0]) + sum(
+            a[0].nbytes + a[1].nbytes + a[2].nbytes + a[3].nbytes + 8 * len(g) for g, a in fork_plan[2])
+        d2h = sum(4 * int(a[3][-1]) + 4 for _, a in fork_plan[2]) + 8 * len(fork_plan[0])
+
     def e2e_step():
+        if fork_plan is not None:
+            fork_step(True)
+            return
         for g, tok, cu, pos, cup, _ in packed:
             logits = backend.score_packed(tok, cu, pos, cup)
             for j, i in enumerate(g):
@@ -332,16 +399,23 @@ def main():
         "p50_request_latency_ms": statistics.median(step_ms),
         "p50_single_request_latency_ms": 1000.0 * statistics.median(lat),
         "step_ms": [round(x, 3) for x in step_ms],
-        "config": {"workload": WORKLOADS[args.config].format(n=wl.n_requests, dtype=dtype), "model": name,
+        "config": {"workload": WORKLOADS[args.config].format(n=wl.n_requests, dtype=dtype)
+                   + ("; prefix cache: each request's shared prefix prefilled once, questions scored as its "
+                      "branches" if fork_plan is not None else ""), "model": name,
                    "rows_per_step": len(wl.rows) * world,
                    "tokens_per_step": toks_all, "native_batches_per_step": len(groups),
                    "l2": "flushed between steps (256 MiB write, outside the timed events); weights 1 GB > L2",
-                   "parallelism": f"replicas x{world}"},
+                   "parallelism": f"replicas x{world}",
+                   **({"timing": "host clock around the synchronous native calls (prefill, branch scoring, "
+                                 "release); inputs uploaded inside them", "prefill_tokens_per_step":
+                       sum(len(p) for p in fork_plan[0]) * world,
+                       "suffix_tokens_per_step": sum(int(a[1][-1]) for _, a in fork_plan[2]) * world}
+                      if fork_plan is not None else {})},
         "e2e": {"value": reqs * args.steps / e2e_total_s, "unit": "requests/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "includes": "hk_score (H2D inputs, forward, D2H logits) + host "
                                                       "calibration and answers"},
         "gpu_launches": int(launches),
-        "roofline": {"kernel": "gemm_bf16_tc (tcgen05 projections)", "bound": "tensor", "achieved": achieved,
+        "roofline": {"kernel": "gemm_f16_tc (tcgen05 projections)", "bound": "tensor", "achieved": achieved,
                      "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                      "frac": (achieved / pk["bf16_tflops_sustained"]) if achieved else None,
                      "traffic": traffic, "peak_source": pk["source"] + " (sustained: kernels timed inside a step)",

@@ -201,10 +201,10 @@ class KevBackend:
         return self.prefill_batch([tokens])[0]
 
     def prefill_batch(self, rows) -> list:
-        """Prefill up to 64 prefixes in one native call; one handle per row."""
+        """Prefill up to 256 prefixes in one native call; one handle per row."""
         rows = [list(r) for r in rows]
-        if not rows or len(rows) > _native.HK_MAX_ROWS:
-            raise BackendError("Qwen3.5 batch must contain 1..=64 independent rows")
+        if not rows or len(rows) > _native.HK_MAX_CACHED_ROWS:
+            raise BackendError("cached batches take 1..=256 rows")
         tokens, cu, _, _ = pack_rows(rows, [[] for _ in rows])
         handles = np.zeros(len(rows), np.uint64)
         self._check(self._lib.hk_prefill(

@@ -213,10 +213,14 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
 #pragma unroll
             for (int e = 0; e < 4; ++e)
                 S[nt][e] = sh[(warp * 16 + g4 + (e >> 1) * 8) * D + nt * 8 + 2 * t4 + (e & 1)];
-        for (int i = tid; i < D * LDH; i += THREADS) {
-            const int r = i / LDH, c = i % LDH;
-            (&sm.S[0][0])[i] = __float2half_rn(c < D ? sh[r * D + c] : 0.f);
-        }
+        // The fp16 copy from the fragments just loaded (as at the end of a chunk).
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int r = warp * 16 + g4 + hf * 8, c = nt * 8 + 2 * t4;
+                *reinterpret_cast<__half2 *>(&sm.S[r][c]) = __floats2half2_rn(S[nt][2 * hf], S[nt][2 * hf + 1]);
+            }
     } else {
 #pragma unroll
         for (int nt = 0; nt < 16; ++nt) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0.f;

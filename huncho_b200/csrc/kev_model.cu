@@ -397,7 +397,7 @@ struct Model {
     }
     std::vector<int> layer_slot;  // index among the delta layers, or among the attention layers
     int n_delta = 0, n_attn = 0;
-    // Device table of a cached batch: 4 x [layers][HK_MAX_ROWS] addresses (in
+    // Device table of a cached batch: 4 x [layers][rows] addresses (in
     // state|K, in conv history, out state|K, out conv history), then the
     // per-row prefix lengths.
     uint64_t *cache_meta = nullptr;
@@ -416,12 +416,24 @@ struct Model {
         if (!layers[li].full) return b + layer_slot[li] * delta_block();
         return b + n_delta * delta_block() + layer_slot[li] * kv_block(sn.tokens);
     }
+    // Snapshots come from the model's own stream-ordered pool, which keeps
+    // freed memory for reuse instead of returning it at every synchronisation.
+    cudaMemPool_t pool = nullptr;
     std::shared_ptr<Snapshot> new_snapshot(int tokens) {
+        if (!pool) {
+            cudaMemPoolProps props = {};
+            props.allocType = cudaMemAllocationTypePinned;
+            props.location.type = cudaMemLocationTypeDevice;
+            props.location.id = device;
+            HK_CUDA(cudaMemPoolCreate(&pool, &props));
+            uint64_t keep = UINT64_MAX;
+            HK_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+        }
         auto sn = std::make_shared<Snapshot>();
         sn->tokens = tokens;
         sn->device = device;
         sn->stream = stream;
-        HK_CUDA(cudaMallocAsync(&sn->buf, std::max<size_t>(snapshot_bytes(tokens), 256), stream));
+        HK_CUDA(cudaMallocFromPoolAsync(&sn->buf, std::max<size_t>(snapshot_bytes(tokens), 256), pool, stream));
         return sn;
     }
 
@@ -474,6 +486,7 @@ struct Model {
         if (device >= 0) cudaSetDevice(device);
         caches.clear();
         if (stream) cudaStreamSynchronize(stream);
+        if (pool) cudaMemPoolDestroy(pool);
         for (auto &r : prof_recs) {
             cudaEventDestroy(r.a);
             cudaEventDestroy(r.b);
@@ -686,7 +699,7 @@ struct Model {
         err = dev_alloc<uint32_t>(1, allocs);
         HK_CUDA(cudaMemset(err, 0, 4));
         for (const Layer &L : layers) layer_slot.push_back(L.full ? n_attn++ : n_delta++);
-        cache_meta = dev_alloc<uint64_t>(4 * layers.size() * HK_MAX_ROWS + HK_MAX_ROWS, allocs);
+        cache_meta = dev_alloc<uint64_t>(4 * layers.size() * HK_MAX_CACHED_ROWS + HK_MAX_CACHED_ROWS, allocs);
     }
 
     void ensure_workspace(int tokens, int rows, int readouts) {
@@ -1204,8 +1217,9 @@ static void score_host(hk::Model &m, int n_rows, const uint32_t *tokens, const i
                        const std::vector<int> *pre, const hk::Model::CacheRefs *cr) {
     // Validation mirrors forward_independent_batch (qwen3_5.rs:3143-3171)
     // and Backend::forward (qwen3_5.rs:2669-2705).
-    if (n_rows < 1 || n_rows > HK_MAX_ROWS)
-        throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 batch must contain 1..=64 independent rows");
+    if (n_rows < 1 || n_rows > (pre ? HK_MAX_CACHED_ROWS : HK_MAX_ROWS))
+        throw hk::ApiError(HK_ERR_BACKEND, pre ? "cached batches take 1..=256 rows"
+                                               : "Qwen3.5 batch must contain 1..=64 independent rows");
     if (cu_seqlens[0] != 0 || cu_positions[0] != 0)
         throw hk::ApiError(HK_ERR_ARGUMENT, "cu_seqlens[0] and cu_positions[0] must be 0");
     for (int r = 0; r < n_rows; ++r) {
@@ -1280,8 +1294,8 @@ int hk_score_cached(hk_model *h, int n_rows, const uint64_t *parents, int mode, 
     hk::Model &m = *h->m;
     return guarded(h, [&]() -> int {
         using Snap = hk::Model::Snapshot;
-        if (n_rows < 1 || n_rows > HK_MAX_ROWS)
-            throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 batch must contain 1..=64 independent rows");
+        if (n_rows < 1 || n_rows > HK_MAX_CACHED_ROWS)
+            throw hk::ApiError(HK_ERR_BACKEND, "cached batches take 1..=256 rows");
         HK_CUDA(cudaSetDevice(m.device));
         std::vector<std::shared_ptr<Snap>> in(n_rows), out(n_rows);
         std::vector<int> pre(n_rows, 0);
@@ -1356,7 +1370,7 @@ int hk_score_cached(hk_model *h, int n_rows, const uint64_t *parents, int mode, 
 }
 
 int hk_prefill(hk_model *h, int n_rows, const uint32_t *tokens, const int32_t *cu_seqlens, uint64_t *handles_out) {
-    if (!h || !h->m || !cu_seqlens || !handles_out || n_rows < 1 || n_rows > HK_MAX_ROWS) return HK_ERR_ARGUMENT;
+    if (!h || !h->m || !cu_seqlens || !handles_out || n_rows < 1 || n_rows > HK_MAX_CACHED_ROWS) return HK_ERR_ARGUMENT;
     std::vector<int32_t> cup(static_cast<size_t>(n_rows) + 1, 0);
     return hk_score_cached(h, n_rows, nullptr, HK_CACHE_PREFILL, tokens, cu_seqlens, nullptr, cup.data(), nullptr,
                            handles_out);

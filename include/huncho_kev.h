@@ -119,7 +119,7 @@ int hk_score(hk_model *m, int n_rows, const uint32_t *tokens, const int32_t *cu_
  *   mode         HK_CACHE_BRANCH: rows read their parents and leave them
  *                unchanged (Backend::forward_fork_batch and
  *                forward_padded_fork_batch, qwen3_5.rs:2780-2804, across any
- *                number of parents in one call);
+ *                number of parents in one call, up to HK_MAX_CACHED_ROWS rows);
  *                HK_CACHE_CONTINUE: each row's handle advances to the state
  *                after its suffix (Backend::forward with fork_from,
  *                qwen3_5.rs:2676-2751); every row needs a distinct handle;
@@ -130,6 +130,7 @@ int hk_score(hk_model *m, int n_rows, const uint32_t *tokens, const int32_t *cu_
  *                HK_ERR_BACKEND; prefix + suffix beyond max_context ->
  *                HK_ERR_BACKEND.
  */
+#define HK_MAX_CACHED_ROWS 256 /* rows per hk_score_cached / hk_prefill call */
 #define HK_CACHE_BRANCH 0
 #define HK_CACHE_CONTINUE 1
 #define HK_CACHE_PREFILL 2
