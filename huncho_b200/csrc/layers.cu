@@ -48,6 +48,40 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, int ldx, const float
     for (int i = lane; i < hidden; i += 32) o[i] = Act<T>::from_f((xr[i] / denom) * w[i]);
 }
 
+// Register-resident form for hidden = 128 * NCH: each lane holds NCH float4 of
+// its row, so the row is read once; fp16 output in 8-byte stores.
+template <typename T, int NCH>
+__global__ void rmsnorm_reg_kernel(const float *__restrict__ x, int ldx, const float *__restrict__ w,
+                                   float eps, int rows, T *__restrict__ out, int ldo) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float *xr = x + static_cast<size_t>(row) * ldx;
+    float4 v[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) v[c] = *reinterpret_cast<const float4 *>(xr + c * 128 + lane * 4);
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) ss += v[c].x * v[c].x + v[c].y * v[c].y + v[c].z * v[c].z + v[c].w * v[c].w;
+    ss = warp_sum(ss);
+    const float denom = sqrtf(ss / static_cast<float>(NCH * 128) + eps);
+    T *o = out + static_cast<size_t>(row) * ldo;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int i = c * 128 + lane * 4;
+        const float4 wv = *reinterpret_cast<const float4 *>(w + i);
+        const float y0 = (v[c].x / denom) * wv.x, y1 = (v[c].y / denom) * wv.y;
+        const float y2 = (v[c].z / denom) * wv.z, y3 = (v[c].w / denom) * wv.w;
+        if constexpr (sizeof(T) == 2) {
+            const __half2 a = __floats2half2_rn(y0, y1), b = __floats2half2_rn(y2, y3);
+            *reinterpret_cast<uint2 *>(o + i) =
+                make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+        } else {
+            *reinterpret_cast<float4 *>(o + i) = make_float4(y0, y1, y2, y3);
+        }
+    }
+}
+
 // ------------------------------------------------------------------ delta prep
 // One CTA per token. Stage 1: conv + SiLU of every q|k|v channel (fp32, taps in
 // ascending order from a zero accumulator, no fused multiply-add, matching
@@ -550,6 +584,24 @@ void launch_rmsnorm(int act, const float *x, int ldx, const float *w_eff, float 
                     int hidden, void *out, int ldo, cudaStream_t s) {
     if (rows <= 0) return;
     const int grid = ceil_div(rows, 8);
+    const bool vec = (ldx % 4) == 0 && (ldo % 4) == 0 && (hidden % 128) == 0;
+#define HK_RMS_REG(NCH)                                                                                          \
+    if (vec && hidden == 128 * (NCH)) {                                                                          \
+        if (act == kActF32)                                                                                      \
+            rmsnorm_reg_kernel<float, NCH><<<grid, 256, 0, s>>>(x, ldx, w_eff, eps, rows, static_cast<float *>(out), \
+                                                                ldo);                                            \
+        else                                                                                                     \
+            rmsnorm_reg_kernel<__half, NCH><<<grid, 256, 0, s>>>(x, ldx, w_eff, eps, rows,                        \
+                                                                 static_cast<__half *>(out), ldo);               \
+        HK_LAUNCH_CHECK();                                                                                       \
+        return;                                                                                                  \
+    }
+    HK_RMS_REG(8)
+    HK_RMS_REG(16)
+    HK_RMS_REG(20)
+    HK_RMS_REG(24)
+    HK_RMS_REG(32)
+#undef HK_RMS_REG
     if (act == kActF32)
         rmsnorm_kernel<float><<<grid, 256, 0, s>>>(x, ldx, w_eff, eps, rows, hidden, static_cast<float *>(out), ldo);
     else
