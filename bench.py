@@ -115,15 +115,52 @@ def groups_of(rows, limit=64):
     return [list(range(i, min(n, i + size))) for i in range(0, n, size)]
 
 
+def request_plan(wl):
+    """Per request: its shared prefix (the longest common prefix of its rows
+    that leaves every readout in the suffix) and, per question row, the suffix
+    and suffix-relative positions (the engine's prefix_cache fan-out,
+    eng:878-960)."""
+    by_req = {}
+    for i, r in enumerate(wl.request_of):
+        by_req.setdefault(r, []).append(i)
+    plan = []
+    for key in sorted(by_req):
+        q = by_req[key]
+        rows_q = [wl.rows[i] for i in q]
+        p = min(len(r) for r in rows_q)
+        for r in rows_q[1:]:
+            p = min(p, next((j for j, (x, y) in enumerate(zip(rows_q[0], r)) if x != y), p))
+        p = min([p] + [min(wl.positions[i]) for i in q])
+        plan.append((list(rows_q[0][:p]), [(i, list(wl.rows[i][p:]), [x - p for x in wl.positions[i]]) for i in q]))
+    return plan
+
+
 def model_dir_for(name, store, seed):
     return synth.default_dir(name, seed, store)
 
 
-def cpu_baseline(model_dir, dtype, wl, rows_idx, max_seconds=30.0):
-    """The CPU oracle on a bounded sample of the workload (whole rows)."""
+def cpu_baseline(model_dir, dtype, wl, rows_idx, max_seconds=30.0, prefix_cache=False):
+    """The CPU oracle on a bounded sample of the workload (whole rows; with
+    prefix_cache whole requests: prefix once, each question as a branch)."""
     from oracle import kev_oracle as ko
     ko.set_threads(os.cpu_count() or 1)
     m = ko.load_model(model_dir, dtype)
+    if prefix_cache:
+        t0 = time.perf_counter()
+        done, toks = 0, 0
+        for prefix, qs in request_plan(wl):
+            cache = ko.prefill(m, prefix)
+            for i, suf, sp in qs:
+                ko.calibrate(ko.score_branch(m, cache, suf, sp), m.temperature)
+                toks += len(wl.rows[i])
+            done += 1
+            if time.perf_counter() - t0 > max_seconds:
+                break
+        dt = time.perf_counter() - t0
+        return {"value": done / dt, "unit": "requests/s", "cores": os.cpu_count(), "kind": "port",
+                "tokens_per_s": toks / dt,
+                "sample": f"{done} whole requests ({toks} prompt tokens) of the workload, CPU fp32 oracle with "
+                          f"prefix caches (prefix once, each question a branch) on the same weights, {dt:.1f} s"}
     t0 = time.perf_counter()
     done, toks = 0, 0
     for i in rows_idx:
@@ -151,6 +188,35 @@ def reference_arm(args, rank, world):
     wl = synth.make_workload(args.config, m.cfg.vocab_size, seed=args.seed)
     rows_per_req = len(wl.rows) / wl.n_requests
     times, toks = [], 0
+    if args.prefix_cache:
+        plan = request_plan(wl)
+        for s in range(args.warmup + args.steps):
+            prefix, qs = plan[s % len(plan)]
+            t0 = time.perf_counter()
+            cache = ko.prefill(m, prefix)
+            for i, suf, sp in qs:
+                ko.calibrate(ko.score_branch(m, cache, suf, sp), m.temperature)
+            if s >= args.warmup:
+                times.append(time.perf_counter() - t0)
+                toks += sum(len(wl.rows[i]) for i, _, _ in qs)
+        total = sum(times)
+        value = len(times) / total
+        line = {
+            "impl": "reference", "metric": "scored requests/s", "value": value, "unit": "requests/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "prompt_tokens_per_s": toks / total,
+            "config": {"workload": f"cfg{args.config}: Kev-0.8B, 32 requests x (choice-4, noul, score-5), lengths "
+                                   "U[64,512]; prefix cache: each request's shared prefix once, questions as branches",
+                       "model": "kev-0.8b (bf16 weights, fp32 math)", "step": "one whole request per step"},
+            "cpu_baseline": {"value": value, "unit": "requests/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{len(times)} whole requests, {toks} prompt tokens; the CPU oracle restating "
+                                       "the reference CPU fp32 Kev forward with its prefix caches (the Rust reference "
+                                       "cannot be built here)"},
+            "e2e": {"value": value, "unit": "requests/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line))
+        return 0
     for s in range(args.warmup + args.steps):
         i = s % len(wl.rows)
         t0 = time.perf_counter()
@@ -260,20 +326,11 @@ def main():
     fork_plan = None
     if args.prefix_cache:
         from huncho_b200 import _native
-        by_req = {}
-        for i, r in enumerate(wl.request_of):
-            by_req.setdefault(r, []).append(i)
-        reqs_rows = [by_req[k] for k in sorted(by_req)]
         prefixes, suffixes = [], []
-        for q in reqs_rows:
-            rows_q = [wl.rows[i] for i in q]
-            p = min(len(r) for r in rows_q)
-            for r in rows_q[1:]:
-                p = min(p, next((j for j, (x, y) in enumerate(zip(rows_q[0], r)) if x != y), p))
-            p = min([p] + [min(wl.positions[i]) for i in q])
-            prefixes.append(list(rows_q[0][:p]))
-            for i in q:
-                suffixes.append((len(prefixes) - 1, i, list(wl.rows[i][p:]), [x - p for x in wl.positions[i]]))
+        for prefix, qs in request_plan(wl):
+            prefixes.append(prefix)
+            for i, suf, sp in qs:
+                suffixes.append((len(prefixes) - 1, i, suf, sp))
         lim = _native.HK_MAX_CACHED_ROWS
         pre_groups = [list(range(a, min(len(prefixes), a + lim))) for a in range(0, len(prefixes), lim)]
         row_groups = [suffixes[a:a + lim] for a in range(0, len(suffixes), lim)]
@@ -424,7 +481,7 @@ def main():
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         order = [i for r in range(wl.n_requests) for i in range(len(wl.rows)) if wl.request_of[i] == r]
-        line["cpu_baseline"] = cpu_baseline(d, dtype, wl, order)
+        line["cpu_baseline"] = cpu_baseline(d, dtype, wl, order, prefix_cache=fork_plan is not None)
     line["clocks"] = clk.summary()
     if rank == 0:
         print(json.dumps(line), flush=True)

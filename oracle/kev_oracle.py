@@ -402,8 +402,13 @@ def linear(x, w):
 # Layers (qwen3_5.rs:586-1104)
 # ---------------------------------------------------------------------------
 
-def linear_attn(m: KevModel, p: str, x):
-    """LinearAttn::forward, qwen3_5.rs:846-947, for one row x [T, H]."""
+def linear_attn(m: KevModel, p: str, x, cache=None):
+    """LinearAttn::forward, qwen3_5.rs:846-947, for one row x [T, H].
+
+    With `cache` (a dict, the layer's LayerCache): the conv runs over
+    [cache["conv"] ; this row's inputs] and keeps the suffix part, the
+    recurrence starts from cache["state"], and both are replaced by the state
+    after this row (q35:851-866, 929-944)."""
     c, w = m.cfg, m.w
     T = x.shape[0]
     nk, nv = c.linear_num_key_heads, c.linear_num_value_heads
@@ -411,7 +416,15 @@ def linear_attn(m: KevModel, p: str, x):
     key_dim, value_dim = nk * dk, nv * dv
     mixed = linear(x, w[f"{p}.in_proj_qkv.weight"])  # [T, conv_dim]
     cw = w[f"{p}.conv1d.weight"].reshape(mixed.shape[1], -1)
-    conv = causal_conv(mixed.T.copy(), cw)  # [conv_dim, T]
+    xt = mixed.T.copy()  # [conv_dim, T]
+    hist = cache.get("conv") if cache is not None else None
+    hl = 0 if hist is None else hist.shape[1]
+    if hl:
+        xt = np.ascontiguousarray(np.concatenate([hist, xt], axis=1))
+    if cache is not None:
+        keep = min(cw.shape[1] - 1, xt.shape[1])
+        cache["conv"] = xt[:, xt.shape[1] - keep:].copy()
+    conv = causal_conv(xt, cw)[:, hl:]  # [conv_dim, T]
     mixed = silu(conv).T.copy()  # [T, conv_dim]
     q = mixed[:, :key_dim].reshape(T, nk, dk)
     k = mixed[:, key_dim:2 * key_dim].reshape(T, nk, dk)
@@ -431,14 +444,21 @@ def linear_attn(m: KevModel, p: str, x):
     scale = F32(1.0 / math.sqrt(dk))
     q = (l2norm(q) * scale).astype(F32)
     k = l2norm(k)
-    out, _ = delta_recurrent(q, k, v, g.T.copy(), beta.T.copy())
+    out, state = delta_recurrent(q, k, v, g.T.copy(), beta.T.copy(),
+                                 None if cache is None else cache.get("state"))
+    if cache is not None:
+        cache["state"] = state
     out = out.transpose(1, 0, 2)  # [T, nv, dv]
     out = rms_norm_gated(out, z, w[f"{p}.norm.weight"], c.rms_norm_eps).reshape(T, value_dim)
     return linear(out, w[f"{p}.out_proj.weight"])
 
 
-def full_attn(m: KevModel, p: str, x, cos, sin):
-    """Attention::forward, qwen3_5.rs:586-726 (flat KV, dense causal mask)."""
+def full_attn(m: KevModel, p: str, x, cos, sin, cache=None):
+    """Attention::forward, qwen3_5.rs:586-726 (flat KV, dense causal mask).
+
+    With `cache`: the row continues cache["k"], cache["v"] ([nkv, P, hd], after
+    norm and RoPE); cos / sin then cover positions P.., queries see every cached
+    key plus their own causal prefix, and the cache grows by this row."""
     c, w = m.cfg, m.w
     T = x.shape[0]
     nh, nkv, hd = c.num_attention_heads, c.num_key_value_heads, c.head_dim
@@ -451,12 +471,19 @@ def full_attn(m: KevModel, p: str, x, cos, sin):
     rd = c.rotary_dim()
     q = apply_partial_rotary(q, cos, sin, rd)
     k = apply_partial_rotary(k, cos, sin, rd)
+    P = 0
+    if cache is not None:
+        if "k" in cache:
+            P = cache["k"].shape[1]
+            k = np.concatenate([cache["k"], k], axis=1)
+            v = np.concatenate([cache["v"], v], axis=1)
+        cache["k"], cache["v"] = k, v
     n_rep = nh // nkv
     k = np.repeat(k, n_rep, axis=0)
     v = np.repeat(v, n_rep, axis=0)
     scale = F32(1.0 / math.sqrt(hd))
     scores = (np.matmul(q, k.transpose(0, 2, 1)) * scale).astype(F32)
-    mask = np.triu(np.full((T, T), -np.inf, F32), 1)
+    mask = np.triu(np.full((T, P + T), -np.inf, F32), P + 1)
     scores = scores + mask[None]
     mx = np.max(scores, axis=-1, keepdims=True)
     e = np.exp(scores - mx).astype(F32)
@@ -473,8 +500,12 @@ def mlp(m: KevModel, p: str, x):
     return linear((g * u).astype(F32), m.w[f"{p}.down_proj.weight"])
 
 
-def forward_hidden(m: KevModel, ids) -> np.ndarray:
-    """Model::forward_inner (qwen3_5.rs:1533-1553) for one row: final-normed hidden [T, H]."""
+def forward_hidden(m: KevModel, ids, cache=None) -> np.ndarray:
+    """Model::forward_inner (qwen3_5.rs:1533-1553) for one row: final-normed hidden [T, H].
+
+    `cache` (from new_cache(), or a copy of a prefilled one) continues a cached
+    prefix: positions start at cache["tokens"], and the cache advances to the
+    state after this row (Model::forward_cached, qwen3_5.rs:1111-1212)."""
     c, w = m.cfg, m.w
     ids = np.asarray(ids, dtype=np.int64)
     if ids.size == 0:
@@ -482,19 +513,51 @@ def forward_hidden(m: KevModel, ids) -> np.ndarray:
     if (ids < 0).any() or (ids >= c.vocab_size).any():
         raise ValueError("token id is outside the vocabulary")
     T = ids.shape[0]
-    cos, sin = rotary_cos_sin(c, T)
+    offset = 0 if cache is None else cache["tokens"]
+    cos, sin = rotary_cos_sin(c, T, offset)
     x = w["model.language_model.embed_tokens.weight"][ids].astype(F32)
     for i in range(c.num_hidden_layers):
         p = f"model.language_model.layers.{i}"
+        lc = None if cache is None else cache["layers"][i]
         h = rms_norm_effective(x, F32(1.0) + w[f"{p}.input_layernorm.weight"], c.rms_norm_eps)
         if c.layer_types[i] == "linear":
-            h = linear_attn(m, f"{p}.linear_attn", h)
+            h = linear_attn(m, f"{p}.linear_attn", h, lc)
         else:
-            h = full_attn(m, f"{p}.self_attn", h, cos, sin)
+            h = full_attn(m, f"{p}.self_attn", h, cos, sin, lc)
         h = (h + x).astype(F32)
         n = rms_norm_effective(h, F32(1.0) + w[f"{p}.post_attention_layernorm.weight"], c.rms_norm_eps)
         x = (mlp(m, f"{p}.mlp", n) + h).astype(F32)
+    if cache is not None:
+        cache["tokens"] = offset + T
     return rms_norm_effective(x, F32(1.0) + w["model.language_model.norm.weight"], c.rms_norm_eps)
+
+
+def new_cache(m: KevModel) -> dict:
+    """An empty ModelCache (qwen3_5.rs:1120-1125): per-layer dicts, 0 tokens."""
+    return {"tokens": 0, "layers": [dict() for _ in range(m.cfg.num_hidden_layers)]}
+
+
+def copy_cache(cache: dict) -> dict:
+    """Fork: an independent branch of the same state (qwen3_5.rs:2818-2831)."""
+    return {"tokens": cache["tokens"],
+            "layers": [{k: v.copy() for k, v in lc.items()} for lc in cache["layers"]]}
+
+
+def prefill(m: KevModel, tokens) -> dict:
+    """Backend::prefill (qwen3_5.rs:2833-2835): the cache after `tokens`."""
+    cache = new_cache(m)
+    forward_hidden(m, tokens, cache)
+    return cache
+
+
+def score_branch(m: KevModel, cache: dict, tokens, positions) -> np.ndarray:
+    """forward with fork_from on a copy of `cache` (the parent is left as is):
+    raw logits of the suffix `tokens` at suffix-relative `positions`."""
+    tokens, positions = list(tokens), list(positions)
+    if any(p >= len(tokens) or p < 0 for p in positions):
+        raise ValueError("readout position is outside the token sequence")
+    hidden = forward_hidden(m, tokens, copy_cache(cache))
+    return pointer_head(m, hidden[len(tokens) - 1], hidden[positions])
 
 
 def pointer_head(m: KevModel, decide, options):

@@ -144,3 +144,30 @@ def test_int8_quantization_roundtrip():
     assert s[3] == 1.0
     deq = q.astype(np.float32) * s[:, None]
     assert np.all(np.abs(deq - w) <= s[:, None] / 2 + 1e-9)
+
+
+def test_oracle_prefix_cache_matches_full_rows(model, golden):
+    """The oracle's prefill / fork / continuation (the CPU side of the GPU fork
+    tests): prefixes of 1, 2 and the shared length, continued in chunks of 1, 3
+    and all at once, give the full row's logits (prefix_cache.rs:141-205) and
+    the upstream golden within its fp32 gate."""
+    for case in golden["cases"]:
+        rows = case["rows"]
+        first = rows[0]["tokens"]
+        for prefix_len in (1, 2, rows[0]["prefix_len"]):
+            parent = ko.prefill(model, first[:prefix_len])
+            assert parent["tokens"] == prefix_len
+            for row in rows:
+                tokens, positions = row["tokens"], row["positions"]
+                full = ko.score_row(model, tokens, positions)
+                for chunk in (1, 3, None):
+                    branch = ko.copy_cache(parent)
+                    offset = prefix_len
+                    while offset < positions[0]:
+                        end = positions[0] if chunk is None else min(offset + chunk, positions[0])
+                        ko.forward_hidden(model, tokens[offset:end], branch)
+                        offset = end
+                    got = ko.score_branch(model, branch, tokens[offset:], [p - offset for p in positions])
+                    assert np.abs(got - full).max() < 1e-5, (got, full)
+                    assert np.abs(got - np.asarray(row["raw_logits"], np.float32)).max() < 2e-4
+            assert parent["tokens"] == prefix_len  # branches never touch the parent
