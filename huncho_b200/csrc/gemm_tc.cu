@@ -248,7 +248,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
-                            __half2 h2 = __floats2half2_rn(silu_f(g[2 * i]) * u[2 * i], silu_f(g[2 * i + 1]) * u[2 * i + 1]);
+                            __half2 h2 = __floats2half2_rn(silu_fast(g[2 * i]) * u[2 * i],
+                                                           silu_fast(g[2 * i + 1]) * u[2 * i + 1]);
                             packed[16 * hh + i] = *reinterpret_cast<uint32_t *>(&h2);
                         }
                     }
