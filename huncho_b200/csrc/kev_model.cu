@@ -818,6 +818,7 @@ struct Model {
                 d.beta = db;
                 d.tok_row = tok_row;
                 d.hist_in = in_b;
+                d.fast = dtype != HK_DTYPE_FP32;
                 if (out_b)
                     launch_conv_history(proj, ldp, c.conv_dim(), c.taps, cu_seqlens, n_rows, in_b, out_b, stream);
                 if (dtype != HK_DTYPE_FP32 && c.dk == 128 && c.dv == 128 && c.taps == 4 && c.nv <= 32) {

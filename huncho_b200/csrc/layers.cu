@@ -146,7 +146,7 @@ __global__ void delta_prep_kernel(DeltaPrepArgs a) {
 // projection element is read once (float4) and every output written once.
 // The conv sum keeps the taps' ascending order with separately rounded
 // products (conv_cpu.rs:38-49).
-template <int TB>
+template <int TB, bool FAST>
 __global__ void delta_prep_vec_kernel(DeltaPrepArgs a) {
     const int warps = blockDim.x / 32;
     const int wid = blockIdx.x * warps + threadIdx.x / 32;
@@ -210,13 +210,14 @@ __global__ void delta_prep_vec_kernel(DeltaPrepArgs a) {
         for (int c = 0; c < 4; ++c) {
             float acc = 0.f;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) acc = __fadd_rn(acc, __fmul_rn(w[c][k], xs[c][k]));
-            y[c] = silu_f(acc);
+            for (int k = 0; k < 4; ++k)
+                acc = FAST ? fmaf(w[c][k], xs[c][k], acc) : __fadd_rn(acc, __fmul_rn(w[c][k], xs[c][k]));
+            y[c] = FAST ? silu_fast(acc) : silu_f(acc);
         }
         float4 out;
         if (is_q || is_k) {
             float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
-            const float inv = 1.0f / sqrtf(ss + 1e-6f);
+            const float inv = FAST ? rsqrtf(ss + 1e-6f) : 1.0f / sqrtf(ss + 1e-6f);
             const float sc = is_q ? qscale : 1.0f;
             out = make_float4((y[0] * inv) * sc, (y[1] * inv) * sc, (y[2] * inv) * sc, (y[3] * inv) * sc);
             float *dst = (is_q ? a.q : a.k) + static_cast<size_t>(t) * key_dim + (c0 - (is_q ? 0 : key_dim));
@@ -681,7 +682,10 @@ void launch_delta_prep(const DeltaPrepArgs &a, cudaStream_t s) {
     if (a.dk == 128 && a.dv == 128 && a.taps == 4 && a.nv <= 32 && (a.ldp % 4) == 0) {
         constexpr int TB = 16;
         const long warps = static_cast<long>((a.n + TB - 1) / TB) * (2 * a.nk + a.nv + 1);
-        delta_prep_vec_kernel<TB><<<ceil_div(warps, 8), 256, 0, s>>>(a);
+        if (a.fast)
+            delta_prep_vec_kernel<TB, true><<<ceil_div(warps, 8), 256, 0, s>>>(a);
+        else
+            delta_prep_vec_kernel<TB, false><<<ceil_div(warps, 8), 256, 0, s>>>(a);
         HK_LAUNCH_CHECK();
         return;
     }

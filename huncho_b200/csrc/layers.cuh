@@ -43,6 +43,10 @@ struct DeltaPrepArgs {
     // last pre-conv inputs, oldest first), or 0 for none (zero history).
     const int32_t *tok_row = nullptr;
     const uint64_t *hist_in = nullptr;
+    // Half-precision models: fused multiply-adds in the conv, intrinsic SiLU
+    // and rsqrt (their q, k, v are split into fp16 operands right after); the
+    // fp32 model keeps the reference's exact operation order.
+    int fast = 0;
 };
 void launch_delta_prep(const DeltaPrepArgs &a, cudaStream_t s);
 
