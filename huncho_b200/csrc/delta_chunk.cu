@@ -59,6 +59,12 @@ struct Smem {
     float sq[C][D], sk[C][D], sv[C][D];
     float sz[C][D];  // z rows of the chunk whose gated output is pending
     float sg[C], sb[C];
+    // RAW input: the staging above holds pre-conv projection rows [C][q|k|v]
+    // of this head; the conv history (last 3 rows, double-buffered by chunk
+    // parity), the head's conv weights and the raw b / a projections.
+    float hist[2][3][3 * D];
+    float cw[3 * D][4];
+    float sbr[C], sar[C];
 };
 
 __device__ __forceinline__ uint32_t sa(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -152,10 +158,14 @@ struct ChunkArgs {
     int ldmix;
     // Per-row addresses of the initial / final state [nv][128][128] fp32, or 0.
     const uint64_t *state_in, *state_out;
+    // RAW: the input stage fused in (conv + SiLU, l2norm, gates from proj).
+    const float *conv_w, *base_g, *dt_bias;  // [conv_dim][4], [nv], [nv]
+    const uint64_t *hist_in;                 // per row: prefix conv history [3][conv_dim] fp32, or 0
+    int key_dim, value_dim, conv_dim;
 };
 
 
-template <bool GATED_OUT>
+template <bool GATED_OUT, bool RAW>
 __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
@@ -192,6 +202,29 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
                 cp4(&sm.sb[r], a.beta + t * a.nv + h, ok);
         }
     };
+    // RAW: this head's pre-conv q | k | v projection columns.
+    const int ch_q = kh * D, ch_k = a.key_dim + kh * D, ch_v = 2 * a.key_dim + h * D;
+    auto prefetch_raw = [&](int c0) {
+        const int nn = min(C, end - c0);
+        float *sraw = &sm.sq[0][0];  // [C][3D] over the q|k|v staging
+        for (int i = tid; i < C * (3 * D / 4); i += THREADS) {
+            const int r = i / (3 * D / 4), w = i % (3 * D / 4), which = w / (D / 4), c = (w % (D / 4)) * 4;
+            const bool ok = r < nn;
+            const size_t t = static_cast<size_t>(c0 + (ok ? r : 0));
+            const int ch = which == 0 ? ch_q : which == 1 ? ch_k : ch_v;
+            cp16(sraw + r * 3 * D + which * D + c, a.proj + t * a.ldp + ch + c, ok);
+        }
+        if (tid < 2 * C) {
+            const int r = tid % C;
+            const bool ok = r < nn;
+            const size_t t = static_cast<size_t>(c0 + (ok ? r : 0));
+            const float *pb = a.proj + t * a.ldp + a.conv_dim + a.value_dim;
+            if (tid < C)
+                cp4(&sm.sbr[r], pb + h, ok);
+            else
+                cp4(&sm.sar[r], pb + a.nv + h, ok);
+        }
+    };
     auto prefetch_z = [&](int c0) {
         if (!GATED_OUT) return;
         const int nn = min(C, end - c0);
@@ -226,7 +259,24 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
         for (int nt = 0; nt < 16; ++nt) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0.f;
         for (int i = tid; i < D * LDH; i += THREADS) (&sm.S[0][0])[i] = __float2half_rn(0.f);
     }
-    prefetch_qkv(start);
+    if (RAW) {
+        for (int i = tid; i < 3 * D; i += THREADS) {
+            const int which = i / D, c = i % D;
+            const float4 w4 = *reinterpret_cast<const float4 *>(
+                a.conv_w + static_cast<size_t>((which == 0 ? ch_q : which == 1 ? ch_k : ch_v) + c) * 4);
+            *reinterpret_cast<float4 *>(&sm.cw[i][0]) = w4;
+        }
+        // The conv history entering the row: its cached prefix's last inputs, or zero.
+        const float *hist = reinterpret_cast<const float *>(a.hist_in ? a.hist_in[row] : 0);
+        for (int i = tid; i < 3 * 3 * D; i += THREADS) {
+            const int j = i / (3 * D), rem = i % (3 * D), which = rem / D, c = rem % D;
+            const int ch = (which == 0 ? ch_q : which == 1 ? ch_k : ch_v) + c;
+            sm.hist[0][j][rem] = hist ? hist[static_cast<size_t>(j) * a.conv_dim + ch] : 0.f;
+        }
+        prefetch_raw(start);
+    } else {
+        prefetch_qkv(start);
+    }
     prefetch_z(start);
     cp_commit();
 
@@ -236,8 +286,15 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
         __syncthreads();  // this chunk's inputs are in the staging buffers
         // ---- P0: gates. Warp 0 scans g (padding rows carry g = 0, beta = 0).
         if (warp == 0) {
-            float gv = sm.sg[lane];
-            const float bv = sm.sb[lane];
+            float gv, bv;
+            if (RAW) {  // beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias); padding rows 0
+                const bool ok = lane < n;
+                bv = ok ? sigmoid_f(sm.sbr[lane]) : 0.f;
+                gv = ok ? a.base_g[h] * logf(expf(sm.sar[lane] + a.dt_bias[h]) + 1.0f) : 0.f;
+            } else {
+                gv = sm.sg[lane];
+                bv = sm.sb[lane];
+            }
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const float up = __shfl_up_sync(0xffffffffu, gv, o);
@@ -249,11 +306,48 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
         }
         __syncthreads();
         // ---- P0b: operands from the staging buffers. Warp w fills rows w, w+8, ...
+        const int hcur = ((c0 - start) / C) & 1;
 #pragma unroll
         for (int r = warp; r < C; r += WARPS) {
-            const float4 q4 = *reinterpret_cast<const float4 *>(&sm.sq[r][4 * lane]);
-            const float4 k4 = *reinterpret_cast<const float4 *>(&sm.sk[r][4 * lane]);
-            const float4 v4 = *reinterpret_cast<const float4 *>(&sm.sv[r][4 * lane]);
+            float4 q4, k4, v4;
+            if (RAW) {
+                // Causal conv over [history ; chunk] (taps in ascending order), SiLU,
+                // then the l2norm of q (scaled by 1/sqrt(128)) and k across the warp.
+                const float *sraw = &sm.sq[0][0];
+                float y[3][4];
+#pragma unroll
+                for (int which = 0; which < 3; ++which) {
+                    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int idx = r - 3 + j;
+                        const float4 x = idx >= 0
+                            ? *reinterpret_cast<const float4 *>(sraw + idx * 3 * D + which * D + 4 * lane)
+                            : *reinterpret_cast<const float4 *>(&sm.hist[hcur][3 + idx][which * D + 4 * lane]);
+                        const float xe[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) acc[c] = fmaf(sm.cw[which * D + 4 * lane + c][j], xe[c], acc[c]);
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) y[which][c] = silu_fast(acc[c]);
+                }
+                const float sq2 = warp_sum(y[0][0] * y[0][0] + y[0][1] * y[0][1] + y[0][2] * y[0][2] + y[0][3] * y[0][3]);
+                const float sk2 = warp_sum(y[1][0] * y[1][0] + y[1][1] * y[1][1] + y[1][2] * y[1][2] + y[1][3] * y[1][3]);
+                const float iq = rsqrtf(sq2 + 1e-6f) * rsqrtf(static_cast<float>(D)), ik = rsqrtf(sk2 + 1e-6f);
+                q4 = make_float4(y[0][0] * iq, y[0][1] * iq, y[0][2] * iq, y[0][3] * iq);
+                k4 = make_float4(y[1][0] * ik, y[1][1] * ik, y[1][2] * ik, y[1][3] * ik);
+                v4 = make_float4(y[2][0], y[2][1], y[2][2], y[2][3]);
+                if (r >= C - 3) {  // the next chunk's history
+#pragma unroll
+                    for (int which = 0; which < 3; ++which)
+                        *reinterpret_cast<float4 *>(&sm.hist[hcur ^ 1][r - (C - 3)][which * D + 4 * lane]) =
+                            *reinterpret_cast<const float4 *>(sraw + r * 3 * D + which * D + 4 * lane);
+                }
+            } else {
+                q4 = *reinterpret_cast<const float4 *>(&sm.sq[r][4 * lane]);
+                k4 = *reinterpret_cast<const float4 *>(&sm.sk[r][4 * lane]);
+                v4 = *reinterpret_cast<const float4 *>(&sm.sv[r][4 * lane]);
+            }
             const float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
             const float b = sm.beta[r], bg = sm.beta[r] * sm.gam[r];
             const float bvv[4] = {b * v4.x, b * v4.y, b * v4.z, b * v4.w};
@@ -264,8 +358,13 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
             store4(&sm.BK[r][4 * lane], bkk);
         }
         __syncthreads();
-        // The staging buffers are free again: fetch the next chunk's q, k, v, g, beta.
-        if (c0 + C < end) prefetch_qkv(c0 + C);
+        // The staging buffers are free again: fetch the next chunk's inputs.
+        if (c0 + C < end) {
+            if (RAW)
+                prefetch_raw(c0 + C);
+            else
+                prefetch_qkv(c0 + C);
+        }
         cp_commit();
         // ---- P1: K K^T (warps 0-3) and Q K^T (warps 4-7); 16 rows x 16 cols per warp.
         {
@@ -538,19 +637,19 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
     }
 }
 
-template <bool GO>
+template <bool GO, bool RAW>
 void launch_kernel(const ChunkArgs &a, cudaStream_t s) {
     const size_t smem = sizeof(Smem);
     static bool set[64] = {};
     int dev = 0;
     HK_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64 || !set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(delta_chunk_kernel<GO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        HK_CUDA(cudaFuncSetAttribute(delta_chunk_kernel<GO, RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
         if (dev >= 0 && dev < 64) set[dev] = true;
     }
     dim3 grid(a.n_rows, a.nv);
-    delta_chunk_kernel<GO><<<grid, THREADS, smem, s>>>(a);
+    delta_chunk_kernel<GO, RAW><<<grid, THREADS, smem, s>>>(a);
     HK_LAUNCH_CHECK();
 }
 
@@ -574,7 +673,7 @@ void launch_delta_chunk(const DeltaRecArgs &r, cudaStream_t s) {
     a.out = r.out;
     a.state_in = r.state_in;
     a.state_out = r.state_out;
-    launch_kernel<false>(a, s);
+    launch_kernel<false, false>(a, s);
 }
 
 void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp, int zoff, const float *norm_w,
@@ -600,7 +699,35 @@ void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp,
     a.ldmix = ldmix;
     a.state_in = r.state_in;
     a.state_out = r.state_out;
-    launch_kernel<true>(a, s);
+    launch_kernel<true, false>(a, s);
+}
+
+void launch_delta_chunk_fused(const DeltaRecArgs &r, const DeltaFusedInput &in, const float *norm_w, float eps,
+                              __half *mix, int ldmix, cudaStream_t s) {
+    if (r.n_rows <= 0) return;
+    ChunkArgs a{};
+    a.cu_seqlens = r.cu_seqlens;
+    a.row_order = r.row_order;
+    a.n_rows = r.n_rows;
+    a.nk = r.nk;
+    a.nv = r.nv;
+    a.proj = in.proj;
+    a.ldp = in.ldp;
+    a.zoff = in.conv_dim;
+    a.conv_w = in.conv_w;
+    a.base_g = in.base_g;
+    a.dt_bias = in.dt_bias;
+    a.hist_in = in.hist_in;
+    a.key_dim = r.nk * D;
+    a.value_dim = r.nv * D;
+    a.conv_dim = in.conv_dim;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    a.mix = mix;
+    a.ldmix = ldmix;
+    a.state_in = r.state_in;
+    a.state_out = r.state_out;
+    launch_kernel<true, true>(a, s);
 }
 
 }  // namespace hk

@@ -821,11 +821,9 @@ struct Model {
                 d.fast = dtype != HK_DTYPE_FP32;
                 if (out_b)
                     launch_conv_history(proj, ldp, c.conv_dim(), c.taps, cu_seqlens, n_rows, in_b, out_b, stream);
-                if (dtype != HK_DTYPE_FP32 && c.dk == 128 && c.dv == 128 && c.taps == 4 && c.nv <= 32) {
-                    // Input stage, then the chunked recurrence with the gated norm fused.
-                    ev = prof_begin();
-                    launch_delta_prep(d, stream);
-                    prof_end(ev, 3, 0);
+                if (dtype != HK_DTYPE_FP32 && c.dk == 128 && c.dv == 128 && c.taps == 4 && c.nv <= 32 &&
+                    (ldp % 4) == 0) {
+                    // The chunked recurrence with the input stage and the gated norm fused.
                     DeltaRecArgs r;
                     r.q = dq;
                     r.k = dkk;
@@ -843,10 +841,17 @@ struct Model {
                     r.exact = 0;
                     r.state_in = in_a;
                     r.state_out = out_a;
-                    ev = prof_begin();
                     r.err = err;
-                    launch_delta_chunk_gated(r, proj, ldp, c.conv_dim(), L.gnorm_w, c.eps, static_cast<__half *>(mix),
-                                             ldmix, stream);
+                    DeltaFusedInput in;
+                    in.proj = proj;
+                    in.ldp = ldp;
+                    in.conv_dim = c.conv_dim();
+                    in.conv_w = L.conv_w;
+                    in.base_g = L.base_g;
+                    in.dt_bias = L.dt_bias;
+                    in.hist_in = in_b;
+                    ev = prof_begin();
+                    launch_delta_chunk_fused(r, in, L.gnorm_w, c.eps, static_cast<__half *>(mix), ldmix, stream);
                     prof_end(ev, 1, delta_chunk_flops(n_tok, c));
                 } else {
                     ev = prof_begin();

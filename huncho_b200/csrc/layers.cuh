@@ -88,6 +88,18 @@ void launch_delta_chunk(const DeltaRecArgs &a, cudaStream_t s);
 // beta pre-computed.
 void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp, int zoff, const float *norm_w,
                               float eps, __half *mix, int ldmix, cudaStream_t s);
+// The same with the input stage fused in (half-precision models, 128-wide
+// heads, 4 taps): the kernel reads this head's pre-conv q | k | v columns and
+// the b / a projections from proj and does the conv + SiLU, the l2norm and the
+// gates itself; r.q/k/v/g/beta are unused. hist_in as in DeltaPrepArgs.
+struct DeltaFusedInput {
+    const float *proj;
+    int ldp, conv_dim;
+    const float *conv_w, *base_g, *dt_bias;
+    const uint64_t *hist_in = nullptr;
+};
+void launch_delta_chunk_fused(const DeltaRecArgs &r, const DeltaFusedInput &in, const float *norm_w, float eps,
+                              __half *mix, int ldmix, cudaStream_t s);
 
 // out[t, h*dv + j] = rms(o)[j] * w[j] * silu(z[t, h, j]) (qwen3_5.rs:193-201,
 // 934-938); o and z fp32, out in the activation type (the out_proj input).
