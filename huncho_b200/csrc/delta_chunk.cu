@@ -280,6 +280,16 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
     prefetch_z(start);
     cp_commit();
 
+    // This thread's gated-norm weights (columns nb + 8 nt + 2 t4 + {0, 1}).
+    const int nb = warp * 16;
+    float nwr[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    if (GATED_OUT) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            nwr[nt][0] = a.norm_w[nb + nt * 8 + 2 * t4];
+            nwr[nt][1] = a.norm_w[nb + nt * 8 + 2 * t4 + 1];
+        }
+    }
     for (int c0 = start; c0 < end; c0 += C) {
         const int n = min(C, end - c0);
         cp_wait_all();
@@ -420,8 +430,7 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
             }
         }
         __syncthreads();
-        // ---- P3: U = T (b v) (hi+lo), W = T (b gam k); warp w owns cols 16w..16w+15.
-        const int nb = warp * 16;
+        // ---- P3: U = T (b v) (hi+lo), W = T (b gam k); warp w owns cols nb = 16w..16w+15.
         float u[2][2][4];
         {
             float w[2][2][4];
@@ -581,12 +590,13 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
                     for (int w8 = 0; w8 < WARPS; ++w8) ss += sm.red[w8][t];
                     const float denom = sqrtf(ss / static_cast<float>(D) + a.eps);
                     const size_t tok = static_cast<size_t>(c0 + t);
+                    // fp16 output: the fast division and SiLU intrinsics are exact enough.
 #pragma unroll
                     for (int nt = 0; nt < 2; ++nt) {
                         const int c = nb + nt * 8 + 2 * t4;
                         const float2 zz = *reinterpret_cast<const float2 *>(&sm.sz[t][c]);
-                        const float y0 = ((o[mt][nt][2 * hf] / denom) * a.norm_w[c]) * silu_f(zz.x);
-                        const float y1 = ((o[mt][nt][2 * hf + 1] / denom) * a.norm_w[c + 1]) * silu_f(zz.y);
+                        const float y0 = (__fdividef(o[mt][nt][2 * hf], denom) * nwr[nt][0]) * silu_fast(zz.x);
+                        const float y1 = (__fdividef(o[mt][nt][2 * hf + 1], denom) * nwr[nt][1]) * silu_fast(zz.y);
                         *reinterpret_cast<__half2 *>(a.mix + tok * a.ldmix + h * D + c) = __floats2half2_rn(y0, y1);
                     }
                 }

@@ -87,6 +87,44 @@ int hk_op_delta_recurrent(const float *q, const float *k, const float *v, const 
     });
 }
 
+int hk_op_delta_chunked(int kernel, const float *q, const float *k, const float *v, const float *g, const float *beta,
+                        const int32_t *cu_seqlens, int n_rows, int nk, int nv, const float *z, int ldz,
+                        const float *norm_w, float eps, void *out, int ldo, void *stream) {
+    return op_guard([&] {
+        if (kernel != 0 && kernel != 1) throw std::invalid_argument("kernel must be 0 (mma.sync) or 1 (tcgen05)");
+        if (nk <= 0 || nv <= 0 || nv % nk != 0) throw std::invalid_argument("value heads must be a multiple of key heads");
+        if (z && (!norm_w || ldo < nv * 128 || ldz < nv * 128)) throw std::invalid_argument("bad gated-output layout");
+        hk::DeltaRecArgs a;
+        a.q = q;
+        a.k = k;
+        a.v = v;
+        a.g = g;
+        a.beta = beta;
+        a.cu_seqlens = cu_seqlens;
+        a.n_rows = n_rows;
+        a.nk = nk;
+        a.nv = nv;
+        a.dk = 128;
+        a.dv = 128;
+        a.exact = 0;
+        auto s = static_cast<cudaStream_t>(stream);
+        if (!z) {
+            a.out = static_cast<float *>(out);
+            if (kernel == 0)
+                hk::launch_delta_chunk(a, s);
+            else
+                hk::launch_delta_tc(a, s);
+        } else {
+            a.out = nullptr;
+            __half *mix = static_cast<__half *>(out);
+            if (kernel == 0)
+                hk::launch_delta_chunk_gated(a, z, ldz, 0, norm_w, eps, mix, ldo, s);
+            else
+                hk::launch_delta_tc_gated(a, z, ldz, 0, norm_w, eps, mix, ldo, s);
+        }
+    });
+}
+
 int hk_op_attention(int act, const void *q, const void *k, const void *v, const float *proj, int ldp,
                     const int32_t *cu_seqlens, const int32_t *tok_row, int n, int n_rows, int max_len, int nh,
                     int nkv, int hd, void *out, int ldo, void *stream) {

@@ -31,6 +31,18 @@ int hk_op_delta_recurrent(const float *q, const float *k, const float *v, const 
                           const float *beta, const int32_t *cu_seqlens, int n_rows, int nk, int nv,
                           int dk, int dv, int exact, float *out, void *stream);
 
+/* The chunked forms of the same rule for 128-wide heads (the WY form of the
+ * chunk-reassociated recurrence, fp16 tensor-core operands with hi/lo splits
+ * on the sensitive ones, fp32 state): `kernel` 0 = mma.sync, 32-token chunks;
+ * 1 = tcgen05 with the state in tensor memory, 64-token chunks. With z == NULL
+ * the output is o [n, nv, 128] fp32; otherwise it is the gated RMSNorm
+ * rms(o) * norm_w * silu(z) (qwen3_5.rs:193-201) in fp16 at out[t * ldo +
+ * h*128 + j], with z[t * ldz + h*128 + j] fp32 (the delta layer's out_proj
+ * input). No reference counterpart (the reference runs the per-token rule). */
+int hk_op_delta_chunked(int kernel, const float *q, const float *k, const float *v, const float *g,
+                        const float *beta, const int32_t *cu_seqlens, int n_rows, int nk, int nv, const float *z,
+                        int ldz, const float *norm_w, float eps, void *out, int ldo, void *stream);
+
 /* Causal GQA attention with the sigmoid output gate (qwen3_5.rs:669-714).
  * act 0: fp32, 1: fp16. q [n, nh, hd]; k, v [n, nkv, hd] (act type); gate read
  * from the fp32 proj[t, h*2*hd + hd + i] (row stride ldp); out [n, ldo] (act

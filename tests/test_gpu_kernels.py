@@ -258,6 +258,59 @@ def test_readout_vs_torch(lib):
     torch.testing.assert_close(logits, ref, rtol=1e-4, atol=1e-5)
 
 
+def _run_chunked(lib, kernel, q, k, v, g, b, cu, nk, nv, z=None, norm_w=None, eps=1e-6):
+    t = [torch.from_numpy(a).cuda() for a in (q, k, v, g, b, cu)]
+    n = q.shape[0]
+    lib.hk_op_delta_chunked.argtypes = ([ctypes.c_int] + [ctypes.c_void_p] * 6 + [ctypes.c_int] * 3
+                                        + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_float,
+                                           ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p])
+    if z is None:
+        out, zt, nw, ldz, ldo = torch.zeros_like(t[2]), None, None, 0, 0
+    else:
+        zt, nw = torch.from_numpy(z).cuda(), torch.from_numpy(norm_w).cuda()
+        out = torch.zeros(n, nv * 128, dtype=torch.half, device="cuda")
+        ldz = ldo = nv * 128
+    rc = lib.hk_op_delta_chunked(kernel, *[_p(x) for x in t], len(cu) - 1, nk, nv,
+                                 None if zt is None else _p(zt), ldz, None if nw is None else _p(nw), eps,
+                                 _p(out), ldo, None)
+    assert rc == 0, lib.hk_op_last_error()
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("kernel", [0, 1])
+@pytest.mark.parametrize("nk", [16, 8])
+def test_delta_chunked_kernels_vs_oracle(lib, kernel, nk):
+    """Both chunked forms (0: mma.sync, 32-token chunks; 1: tcgen05, 64-token
+    chunks) against the per-token fp32 recurrence: ragged tails, a 1-token
+    row, rows of many chunks, and the key-head repeat (nk < nv)."""
+    rng = np.random.default_rng(11)
+    nv = 16
+    args = _delta_inputs(rng, [37, 1, 130, 64, 300], nk, nv, 128, 128)
+    got = _run_chunked(lib, kernel, *args, nk, nv)
+    ref = _delta_oracle(*args, nk, nv)
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() <= 1e-3 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("kernel", [0, 1])
+def test_delta_chunked_gated_output_vs_oracle(lib, kernel):
+    """The fused gated RMSNorm output rms(o) * w * silu(z) (qwen3_5.rs:193-201)
+    of both chunked kernels against the oracle's recurrence + rms_norm_gated,
+    in fp16 (the out_proj input)."""
+    rng = np.random.default_rng(12)
+    nk = nv = 16
+    q, k, v, g, b, cu = _delta_inputs(rng, [37, 1, 130, 64, 300], nk, nv, 128, 128)
+    n = q.shape[0]
+    z = rng.standard_normal((n, nv * 128), dtype=np.float32)
+    w = (1.0 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    got = _run_chunked(lib, kernel, q, k, v, g, b, cu, nk, nv, z=z, norm_w=w)
+    o = _delta_oracle(q, k, v, g, b, cu, nk, nv)
+    ref = ko.rms_norm_gated(o, z.reshape(n, nv, 128), w, 1e-6).reshape(n, nv * 128)
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() <= 3e-3 * np.abs(ref).max()
+
+
 def test_delta_chunked_long_context_stress(lib):
     """The long-context stress configuration at the delta-rule kernel boundary:
     8192-token rows, log-decay g uniform in [-0.1, 0] (a state that remembers
