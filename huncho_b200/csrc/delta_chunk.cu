@@ -63,7 +63,7 @@ struct Smem {
     // of this head; the conv history (last 3 rows, double-buffered by chunk
     // parity), the head's conv weights and the raw b / a projections.
     float hist[2][3][3 * D];
-    float cw[3 * D][4];
+    float cw[3][4][D];  // [tensor][tap][channel]
     float sbr[C], sar[C];
 };
 
@@ -264,7 +264,10 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
             const int which = i / D, c = i % D;
             const float4 w4 = *reinterpret_cast<const float4 *>(
                 a.conv_w + static_cast<size_t>((which == 0 ? ch_q : which == 1 ? ch_k : ch_v) + c) * 4);
-            *reinterpret_cast<float4 *>(&sm.cw[i][0]) = w4;
+            sm.cw[which][0][c] = w4.x;
+            sm.cw[which][1][c] = w4.y;
+            sm.cw[which][2][c] = w4.z;
+            sm.cw[which][3][c] = w4.w;
         }
         // The conv history entering the row: its cached prefix's last inputs, or zero.
         const float *hist = reinterpret_cast<const float *>(a.hist_in ? a.hist_in[row] : 0);
@@ -280,6 +283,7 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
     prefetch_z(start);
     cp_commit();
 
+    const float bg_h = RAW ? a.base_g[h] : 0.f, dt_h = RAW ? a.dt_bias[h] : 0.f;
     // This thread's gated-norm weights (columns nb + 8 nt + 2 t4 + {0, 1}).
     const int nb = warp * 16;
     float nwr[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
@@ -294,78 +298,113 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
         const int n = min(C, end - c0);
         cp_wait_all();
         __syncthreads();  // this chunk's inputs are in the staging buffers
-        // ---- P0: gates. Warp 0 scans g (padding rows carry g = 0, beta = 0).
-        if (warp == 0) {
-            float gv, bv;
-            if (RAW) {  // beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias); padding rows 0
-                const bool ok = lane < n;
-                bv = ok ? sigmoid_f(sm.sbr[lane]) : 0.f;
-                gv = ok ? a.base_g[h] * logf(expf(sm.sar[lane] + a.dt_bias[h]) + 1.0f) : 0.f;
-            } else {
-                gv = sm.sg[lane];
-                bv = sm.sb[lane];
-            }
+        // ---- P0: gates. Every warp scans g in registers (lane = row; padding
+        // rows carry g = 0, beta = 0); warp 0 also publishes G, gam, beta for the
+        // later phases, which read them after the next barrier.
+        float gv, bv;
+        if (RAW) {  // beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias)
+            const bool ok = lane < n;
+            bv = ok ? sigmoid_f(sm.sbr[lane]) : 0.f;
+            gv = ok ? bg_h * logf(expf(sm.sar[lane] + dt_h) + 1.0f) : 0.f;
+        } else {
+            gv = sm.sg[lane];
+            bv = sm.sb[lane];
+        }
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const float up = __shfl_up_sync(0xffffffffu, gv, o);
-                if (lane >= o) gv += up;
-            }
+        for (int o = 1; o < 32; o <<= 1) {
+            const float up = __shfl_up_sync(0xffffffffu, gv, o);
+            if (lane >= o) gv += up;
+        }
+        const float gamv = expf(gv);
+        if (warp == 0) {
             sm.G[lane] = gv;
-            sm.gam[lane] = expf(gv);
+            sm.gam[lane] = gamv;
             sm.beta[lane] = bv;
         }
-        __syncthreads();
-        // ---- P0b: operands from the staging buffers. Warp w fills rows w, w+8, ...
+        // ---- P0b: operands from the staging buffers.
         const int hcur = ((c0 - start) / C) & 1;
+        if (RAW) {
+            // Warp w takes rows 4w .. 4w+3: causal conv over [history ; chunk]
+            // (taps in ascending order) sliding over rows 4w-3 .. 4w+3, SiLU, then
+            // per row the l2norm of q (scaled by 1/sqrt(128)) and k across the warp.
+            const float *sraw = &sm.sq[0][0];  // [C][3D]
+            const int r0 = 4 * warp;
 #pragma unroll
-        for (int r = warp; r < C; r += WARPS) {
-            float4 q4, k4, v4;
-            if (RAW) {
-                // Causal conv over [history ; chunk] (taps in ascending order), SiLU,
-                // then the l2norm of q (scaled by 1/sqrt(128)) and k across the warp.
-                const float *sraw = &sm.sq[0][0];
-                float y[3][4];
+            for (int which = 0; which < 3; ++which) {
+                float4 w4[4], x4[7];
 #pragma unroll
-                for (int which = 0; which < 3; ++which) {
+                for (int j = 0; j < 4; ++j) w4[j] = *reinterpret_cast<const float4 *>(&sm.cw[which][j][4 * lane]);
+#pragma unroll
+                for (int i = 0; i < 7; ++i) {
+                    const int idx = r0 - 3 + i;
+                    x4[i] = idx >= 0 ? *reinterpret_cast<const float4 *>(sraw + idx * 3 * D + which * D + 4 * lane)
+                                     : *reinterpret_cast<const float4 *>(&sm.hist[hcur][3 + idx][which * D + 4 * lane]);
+                }
+                float y[4][4], ss[4];
+#pragma unroll
+                for (int rr = 0; rr < 4; ++rr) {
                     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        const int idx = r - 3 + j;
-                        const float4 x = idx >= 0
-                            ? *reinterpret_cast<const float4 *>(sraw + idx * 3 * D + which * D + 4 * lane)
-                            : *reinterpret_cast<const float4 *>(&sm.hist[hcur][3 + idx][which * D + 4 * lane]);
-                        const float xe[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) acc[c] = fmaf(sm.cw[which * D + 4 * lane + c][j], xe[c], acc[c]);
+                        const float4 x = x4[rr + j], w = w4[j];
+                        acc[0] = fmaf(w.x, x.x, acc[0]);
+                        acc[1] = fmaf(w.y, x.y, acc[1]);
+                        acc[2] = fmaf(w.z, x.z, acc[2]);
+                        acc[3] = fmaf(w.w, x.w, acc[3]);
                     }
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) y[which][c] = silu_fast(acc[c]);
+                    for (int c = 0; c < 4; ++c) y[rr][c] = silu_fast(acc[c]);
+                    ss[rr] = y[rr][0] * y[rr][0] + y[rr][1] * y[rr][1] + y[rr][2] * y[rr][2] + y[rr][3] * y[rr][3];
                 }
-                const float sq2 = warp_sum(y[0][0] * y[0][0] + y[0][1] * y[0][1] + y[0][2] * y[0][2] + y[0][3] * y[0][3]);
-                const float sk2 = warp_sum(y[1][0] * y[1][0] + y[1][1] * y[1][1] + y[1][2] * y[1][2] + y[1][3] * y[1][3]);
-                const float iq = rsqrtf(sq2 + 1e-6f) * rsqrtf(static_cast<float>(D)), ik = rsqrtf(sk2 + 1e-6f);
-                q4 = make_float4(y[0][0] * iq, y[0][1] * iq, y[0][2] * iq, y[0][3] * iq);
-                k4 = make_float4(y[1][0] * ik, y[1][1] * ik, y[1][2] * ik, y[1][3] * ik);
-                v4 = make_float4(y[2][0], y[2][1], y[2][2], y[2][3]);
-                if (r >= C - 3) {  // the next chunk's history
+                if (which < 2) {  // the four rows' sums of squares in one butterfly
 #pragma unroll
-                    for (int which = 0; which < 3; ++which)
-                        *reinterpret_cast<float4 *>(&sm.hist[hcur ^ 1][r - (C - 3)][which * D + 4 * lane]) =
-                            *reinterpret_cast<const float4 *>(sraw + r * 3 * D + which * D + 4 * lane);
+                    for (int o = 16; o >= 1; o >>= 1)
+#pragma unroll
+                        for (int rr = 0; rr < 4; ++rr) ss[rr] += __shfl_xor_sync(0xffffffffu, ss[rr], o);
                 }
-            } else {
-                q4 = *reinterpret_cast<const float4 *>(&sm.sq[r][4 * lane]);
-                k4 = *reinterpret_cast<const float4 *>(&sm.sk[r][4 * lane]);
-                v4 = *reinterpret_cast<const float4 *>(&sm.sv[r][4 * lane]);
+#pragma unroll
+                for (int rr = 0; rr < 4; ++rr) {
+                    const int r = r0 + rr;
+                    const float b = __shfl_sync(0xffffffffu, bv, r);
+                    if (which == 2) {
+                        const float bvv[4] = {b * y[rr][0], b * y[rr][1], b * y[rr][2], b * y[rr][3]};
+                        split_store4(&sm.Vh[r][4 * lane], &sm.Vl[r][4 * lane], bvv);
+                    } else {
+                        const float inv = which == 0 ? rsqrtf(ss[rr] + 1e-6f) * rsqrtf(static_cast<float>(D))
+                                                     : rsqrtf(ss[rr] + 1e-6f);
+                        const float nv4[4] = {y[rr][0] * inv, y[rr][1] * inv, y[rr][2] * inv, y[rr][3] * inv};
+                        if (which == 0) {
+                            split_store4(&sm.Qh[r][4 * lane], &sm.Ql[r][4 * lane], nv4);
+                        } else {
+                            split_store4(&sm.Kh[r][4 * lane], &sm.Kl[r][4 * lane], nv4);
+                            const float bg = b * __shfl_sync(0xffffffffu, gamv, r);
+                            const float bkk[4] = {bg * nv4[0], bg * nv4[1], bg * nv4[2], bg * nv4[3]};
+                            store4(&sm.BK[r][4 * lane], bkk);
+                        }
+                    }
+                }
+                if (warp == WARPS - 1) {  // rows C-3 .. C-1: the next chunk's history
+#pragma unroll
+                    for (int i = 0; i < 3; ++i)
+                        *reinterpret_cast<float4 *>(&sm.hist[hcur ^ 1][i][which * D + 4 * lane]) = x4[4 + i];
+                }
             }
-            const float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
-            const float b = sm.beta[r], bg = sm.beta[r] * sm.gam[r];
-            const float bvv[4] = {b * v4.x, b * v4.y, b * v4.z, b * v4.w};
-            const float bkk[4] = {bg * kv[0], bg * kv[1], bg * kv[2], bg * kv[3]};
-            split_store4(&sm.Qh[r][4 * lane], &sm.Ql[r][4 * lane], qv);
-            split_store4(&sm.Kh[r][4 * lane], &sm.Kl[r][4 * lane], kv);
-            split_store4(&sm.Vh[r][4 * lane], &sm.Vl[r][4 * lane], bvv);
-            store4(&sm.BK[r][4 * lane], bkk);
+        } else {
+            // Warp w fills rows w, w+8, ...
+#pragma unroll
+            for (int r = warp; r < C; r += WARPS) {
+                const float4 q4 = *reinterpret_cast<const float4 *>(&sm.sq[r][4 * lane]);
+                const float4 k4 = *reinterpret_cast<const float4 *>(&sm.sk[r][4 * lane]);
+                const float4 v4 = *reinterpret_cast<const float4 *>(&sm.sv[r][4 * lane]);
+                const float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
+                const float b = __shfl_sync(0xffffffffu, bv, r), bg = b * __shfl_sync(0xffffffffu, gamv, r);
+                const float bvv[4] = {b * v4.x, b * v4.y, b * v4.z, b * v4.w};
+                const float bkk[4] = {bg * kv[0], bg * kv[1], bg * kv[2], bg * kv[3]};
+                split_store4(&sm.Qh[r][4 * lane], &sm.Ql[r][4 * lane], qv);
+                split_store4(&sm.Kh[r][4 * lane], &sm.Kl[r][4 * lane], kv);
+                split_store4(&sm.Vh[r][4 * lane], &sm.Vl[r][4 * lane], bvv);
+                store4(&sm.BK[r][4 * lane], bkk);
+            }
         }
         __syncthreads();
         // The staging buffers are free again: fetch the next chunk's inputs.
