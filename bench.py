@@ -442,10 +442,12 @@ def main():
     pk = peaks()
     gemm_ms, gemm_flops, gemm_n = prof["gemm"]
     achieved = (gemm_flops / 1e12) / (gemm_ms / 1e3) if gemm_ms > 0 else None
-    traffic = None
-    tf = ROOT / "profiles" / "gemm_traffic.json"
-    if tf.exists():
-        traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+    traffic = None  # DRAM bytes per GEMM launch from the committed full-size ncu capture
+    tf = ROOT / "profiles" / "gemm_f16_tc_kernel_cfg2_dram.md"
+    if tf.exists() and args.config == 2:
+        for line in tf.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                traffic = int(line.split(":")[1])
     total_prof_ms = sum(v[0] for v in prof.values())
     line = {
         "metric": "scored requests/s", "value": value, "unit": "requests/s", "n_gpus": world,
