@@ -43,6 +43,7 @@ constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + EPI_BYTES 
 struct TcParams {
     int M, N, K;
     int m_tiles, n_tiles, k_blocks;
+    int n_fast;  // tile order: N fastest (narrow N: the N tiles of one M tile run together, X read once)
     void *out;
     int ldo;
     const float *scale;
@@ -116,7 +117,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t phase = 0;
             uint32_t issued_mask = 0, issued_parity = 0;
             for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-                const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
+                const int m_blk = p.n_fast ? tile / p.n_tiles : tile % p.m_tiles;
+                const int n_blk = p.n_fast ? tile % p.n_tiles : tile / p.m_tiles;
                 for (int kb = 0; kb < p.k_blocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1)) {
                         set_error(p.err, kErrWaitTimeout);
@@ -221,7 +223,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             if (*abort_flag) break;
             tc_fence_after();
-            const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
+            const int m_blk = p.n_fast ? tile / p.n_tiles : tile % p.m_tiles;
+            const int n_blk = p.n_fast ? tile % p.n_tiles : tile / p.m_tiles;
             const int row0 = m_blk * BM + quarter * 32;
             const int row = row0 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
@@ -426,6 +429,7 @@ void launch(const GemmArgs &a, cudaStream_t s, int num_sms) {
     p.K = a.K;
     p.m_tiles = ceil_div(a.M, BM);
     p.n_tiles = ceil_div(a.N, BN);
+    p.n_fast = p.n_tiles <= 8 ? 1 : 0;
     p.k_blocks = ceil_div(a.K, BK);
     p.out = a.out;
     p.ldo = a.ldo;
