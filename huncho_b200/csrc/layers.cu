@@ -440,7 +440,8 @@ __global__ void attn_prep_kernel(AttnPrepArgs a) {
         if (i < a.rd) {
             const int fi = i < half ? i : i - half;
             const float ang = p * a.inv_freq[fi];
-            const float c = cosf(ang), sn = sinf(ang);
+            float c, sn;
+            sincosf(ang, &sn, &c);
             const float rot = i < half ? -buf[i + half] : buf[i - half];
             r = r * c + rot * sn;
         }
