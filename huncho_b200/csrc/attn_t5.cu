@@ -1,0 +1,391 @@
+// Causal varlen GQA attention with the Qwen3.5 output gate (qwen3_5.rs:669-714)
+// on the 5th-generation tensor cores: tcgen05.mma with the accumulators in
+// tensor memory, for head_dim 128 and 256, fp16 operands.
+//
+// One CTA = 128 queries of one (row, query head); 4 warps, thread = query row
+// = TMEM lane. Per tile of 64 keys:
+//   S = Q K^T   (M=128, N=64, K=HD) into one of two TMEM S buffers;
+//   the row softmax in registers (tcgen05.ld), P = exp2(...) as fp16 into
+//   shared memory;
+//   O += P V    (M=128, N=HD, K=64; V read MN-major) into the TMEM O columns.
+// S of tile i+1 is issued before the softmax of tile i, so the tensor core and
+// the threads overlap. The online softmax rescales lazily: a row's reference
+// max (and with it the row of O) only moves when a tile's max exceeds it by
+// more than 8 in log2 units, so exponents stay below 2^8 (safe in fp16) and
+// O / l at the end is unchanged.
+//
+// Q, K, V and P live in shared memory as 128B-swizzled K-major tiles (V's
+// tile is the same bytes read MN-major); K and V tiles are double-buffered and
+// stream in with cp.async while earlier tiles are used. Keys are read through
+// kv_slot() (flat or paged) and, for a row that continues a cached prefix,
+// from the prefix's K/V first. Every mbarrier wait is bounded: on a timeout
+// the kernel records an error bit, lets the MMAs it issued finish, frees its
+// tensor memory and returns.
+#include <math.h>
+
+#include "common.cuh"
+#include "layers.cuh"
+#include "sm100.cuh"
+
+namespace hk {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BKV = 64, THREADS = 128;
+constexpr uint32_t TM_S = 0, TM_O = 256, TM_COLS = 512;  // S buffers at columns 0 and 64; O at 256
+
+template <int HD>
+struct Tiles {
+    static constexpr int Q_BYTES = BM * HD * 2;
+    static constexpr int KV_BYTES = BKV * HD * 2;
+    static constexpr int P_BYTES = BM * BKV * 2;
+    static constexpr int Q = 0;
+    static constexpr int K0 = Q + Q_BYTES;           // K buffers 0, 1
+    static constexpr int V0 = K0 + 2 * KV_BYTES;     // V buffers 0, 1
+    static constexpr int P0 = V0 + 2 * KV_BYTES;     // P buffers 0, 1
+    static constexpr int END = P0 + 2 * P_BYTES;
+    static constexpr int SMEM = END + 256 + 1024;    // barriers + alignment slack
+};
+static_assert(Tiles<256>::SMEM <= 232448, "attention tiles exceed shared memory");
+
+__device__ __forceinline__ void cpa16(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cpa_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// 8 consecutive fp32 values as one 16-byte fp16 store.
+__device__ __forceinline__ void st8h(uint8_t *p, const float *v) {
+    uint4 u;
+    __half2 h;
+    h = __floats2half2_rn(v[0], v[1]);
+    u.x = *reinterpret_cast<const uint32_t *>(&h);
+    h = __floats2half2_rn(v[2], v[3]);
+    u.y = *reinterpret_cast<const uint32_t *>(&h);
+    h = __floats2half2_rn(v[4], v[5]);
+    u.z = *reinterpret_cast<const uint32_t *>(&h);
+    h = __floats2half2_rn(v[6], v[7]);
+    u.w = *reinterpret_cast<const uint32_t *>(&h);
+    *reinterpret_cast<uint4 *>(p) = u;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(THREADS, 1) attn_t5_kernel(AttnArgs a) {
+    using L = Tiles<HD>;
+    constexpr int CH = HD / 8;  // 16-byte chunks per row
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L::END);
+    uint64_t *bar_s = bars, *bar_pv = bars + 2, *bar_drain = bars + 3;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 4);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int row = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * BM;
+    const int start = a.cu_seqlens[row];
+    const int len = a.cu_seqlens[row + 1] - start;
+    if (q0 >= len) return;
+    const int kh = h / (a.nh / a.nkv);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    // A continued row's first P keys are its cached prefix; key indices are
+    // absolute (prefix first), queries are the row's own tokens.
+    const int P = a.pre_len ? a.pre_len[row] : 0;
+    const __half *CK = P ? reinterpret_cast<const __half *>(a.kv_in[row]) : nullptr;
+    const __half *CV = P ? CK + static_cast<size_t>(P) * a.nkv * HD : nullptr;
+    const __half *Qg = static_cast<const __half *>(a.q);
+    const __half *Kg = static_cast<const __half *>(a.k);
+    const __half *Vg = static_cast<const __half *>(a.v);
+    const uint32_t s_base = smem_addr(sm);
+
+    if (tid == 0) {
+        for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_holder, TM_COLS);
+        tmem_relinquish();
+    }
+
+    // Chunk (row r, column group c) of a tile goes to thread r * CH + c mod 128:
+    // a thread's column group is fixed and its rows step by THREADS / CH.
+    constexpr int RSTEP = THREADS / CH;
+    const int c_own = tid % CH, r_own = tid / CH;
+    auto load_q = [&]() {
+#pragma unroll 4
+        for (int r = r_own; r < BM; r += RSTEP) {
+            const int qi = q0 + r;
+            const bool ok = qi < len;
+            const __half *src = Qg + (static_cast<size_t>(start + (ok ? qi : 0)) * a.nh + h) * HD + c_own * 8;
+            cpa16(sm + L::Q + sw128_off(BM, r, c_own * 8), src, ok);
+        }
+    };
+    // The row's own keys: slot start + j (flat) or through its block table
+    // (page sizes are powers of two: shift and mask).
+    const int pt = a.pages.page_tokens;
+    const int pshift = pt ? __ffs(pt) - 1 : 0;
+    const int32_t *ptab = pt ? a.pages.block_table + a.pages.cu_pages[row] : nullptr;
+    const size_t kv_stride = static_cast<size_t>(a.nkv) * HD;  // elements between slots
+    auto load_kv = [&](bool is_v, int kv0, int b) {
+        uint8_t *dst = sm + (is_v ? L::V0 : L::K0) + b * L::KV_BYTES;
+        const __half *own = (is_v ? Vg : Kg) + static_cast<size_t>(kh) * HD + c_own * 8;
+        const __half *pre = P ? (is_v ? CV : CK) + static_cast<size_t>(kh) * HD + c_own * 8 : nullptr;
+#pragma unroll 4
+        for (int r = r_own; r < BKV; r += RSTEP) {
+            const int ki = kv0 + r;
+            const bool ok = ki < P + len;
+            const __half *src;
+            if (ki < P) {
+                src = pre + static_cast<size_t>(ki) * kv_stride;
+            } else {
+                const int j = ok ? ki - P : 0;
+                const int slot = pt ? (ptab[j >> pshift] << pshift) + (j & (pt - 1)) : start + j;
+                src = own + static_cast<size_t>(slot) * kv_stride;
+            }
+            cpa16(dst + sw128_off(BKV, r, c_own * 8), src, ok);
+        }
+    };
+    // S = Q K^T into S buffer sb from K buffer kb (thread 0).
+    auto issue_s = [&](int kb, int sb, uint32_t tmem) {
+        const uint64_t d0 = desc_sw128(s_base, 16, 1024);
+        const uint64_t qa = d0 + (L::Q >> 4), kb0 = d0 + ((L::K0 + kb * L::KV_BYTES) >> 4);
+        constexpr uint32_t id = idesc_f16_f32(BM, BKV);
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+            const uint32_t ao = (ks >> 2) * (BM * 128) + (ks & 3) * 32;
+            const uint32_t bo = (ks >> 2) * (BKV * 128) + (ks & 3) * 32;
+            mma_f16(tmem + TM_S + sb * BKV, qa + (ao >> 4), kb0 + (bo >> 4), id, ks > 0 ? 1u : 0u);
+        }
+    };
+    // O (+)= P V from P buffer and V buffer b (thread 0); V read MN-major
+    // (64-column blocks of the head dim 64 * 128 bytes apart, 8-key groups 1024).
+    auto issue_pv = [&](int b, bool acc, uint32_t tmem) {
+        const uint64_t pa = desc_sw128(s_base + L::P0 + b * L::P_BYTES, 16, 1024);
+        const uint64_t vb = desc_sw128(s_base + L::V0 + b * L::KV_BYTES, BKV * 128, 1024);
+        constexpr uint32_t id = idesc_f16_f32_mj(BM, HD, false, true);
+#pragma unroll
+        for (int ks = 0; ks < BKV / 16; ++ks)
+            mma_f16(tmem + TM_O, pa + ((ks * 32) >> 4), vb + ((ks * 2048) >> 4), id, (acc || ks > 0) ? 1u : 0u);
+    };
+    auto wait = [&](uint64_t *bar, uint32_t parity) {
+        if (!mbar_wait(bar, parity)) {
+            set_error(a.err, kErrWaitTimeout);
+            *abort_flag = 1;
+        }
+    };
+
+    const int kv_end = P + min(len, q0 + BM);  // causal: keys up to the last query of the tile
+    const int n_tiles = (kv_end + BKV - 1) / BKV;
+    // cp.async groups per thread: {Q, K0, V0}, {K1}, then per tile i {K(i+2)}, {V(i+1)}.
+    load_q();
+    load_kv(false, 0, 0);
+    load_kv(true, 0, 0);
+    cpa_commit();
+    if (n_tiles > 1) load_kv(false, BKV, 1);
+    cpa_commit();
+    cpa_wait<1>();
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    if (tid == 0) {
+        issue_s(0, 0, tmem);
+        mma_commit(&bar_s[0]);
+    }
+
+    const int qi = q0 + tid;  // this thread's query (own index) and its absolute key limit
+    const bool q_ok = qi < len;
+    const int key_lim = min(P + qi, P + len - 1);
+    const float sl2 = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+    float m_ref = -INFINITY, l_sum = 0.f;
+    uint32_t ph_s = 0u, ph_pv = 0u;  // bit b: parity of S buffer b
+
+    for (int it = 0; it < n_tiles && !*abort_flag; ++it) {
+        const int b = it & 1, kv0 = it * BKV;
+        // 1. S of the next tile, once its keys have landed.
+        if (it + 1 < n_tiles) {
+            if (it == 0)
+                cpa_wait<0>();
+            else
+                cpa_wait<1>();
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                issue_s((it + 1) & 1, (it + 1) & 1, tmem);
+                mma_commit(&bar_s[(it + 1) & 1]);
+            }
+        }
+        // 2. This tile's scores; its K buffer is then free for tile it+2.
+        wait(&bar_s[b], (ph_s >> b) & 1u);
+        ph_s ^= 1u << b;
+        tc_fence_after();
+        if (it + 2 < n_tiles) load_kv(false, kv0 + 2 * BKV, b);
+        cpa_commit();
+        float sv[BKV];
+        {
+            float t32[32];
+            tmem_ld32(lane_base + TM_S + b * BKV, t32);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sv[j] = t32[j];
+            tmem_ld32(lane_base + TM_S + b * BKV + 32, t32);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sv[32 + j] = t32[j];
+        }
+        // 3. Mask (causal, row end, padding queries), tile max, lazy reference max.
+        float mt = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < BKV; ++j) {
+            const bool valid = q_ok && kv0 + j <= key_lim;
+            sv[j] = valid ? sv[j] * sl2 : -INFINITY;
+            mt = fmaxf(mt, sv[j]);
+        }
+        float corr = 1.f;
+        bool resc = false;
+        if (mt > m_ref + 8.f) {
+            resc = m_ref != -INFINITY;
+            corr = resc ? exp2f(m_ref - mt) : 0.f;
+            m_ref = mt;
+        }
+        // P is stored in fp16: the hardware base-2 exponential is exact enough
+        // (its argument is <= 8 here, and -inf maps to 0).
+        float psum = 0.f;
+#pragma unroll
+        for (int j = 0; j < BKV; ++j) {
+            sv[j] = ex2_approx(sv[j] - m_ref);
+            psum += sv[j];
+        }
+        l_sum = l_sum * corr + psum;
+        // 4. The previous tile's O += P V is done: O is stable, its P and V
+        // buffers are free; V of the next tile streams into that V buffer.
+        if (it > 0) {
+            wait(bar_pv, ph_pv);
+            ph_pv ^= 1u;
+            tc_fence_after();
+        }
+        if (it + 1 < n_tiles) load_kv(true, kv0 + BKV, (it + 1) & 1);
+        cpa_commit();
+        if (__any_sync(0xffffffffu, resc)) {
+            const float f = resc ? corr : 1.f;
+#pragma unroll 1
+            for (int c = 0; c < HD; c += 32) {
+                float o[32];
+                tmem_ld32(lane_base + TM_O + c, o);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] *= f;
+                tmem_st32(lane_base + TM_O + c, o);
+            }
+        }
+        // 5. P (this row's 64 probabilities, fp16) into P buffer b.
+        uint8_t *pb = sm + L::P0 + b * L::P_BYTES;
+#pragma unroll
+        for (int c8 = 0; c8 < BKV / 8; ++c8) st8h(pb + sw128_off(BM, tid, c8 * 8), sv + c8 * 8);
+        // 6. O += P V once this tile's V has landed.
+        if (it > 0) cpa_wait<2>();
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            issue_pv(b, it > 0, tmem);
+            mma_commit(bar_pv);
+        }
+    }
+    if (!*abort_flag) {
+        wait(bar_pv, ph_pv);
+        tc_fence_after();
+    }
+    cpa_wait<0>();
+    __syncthreads();
+
+    if (!*abort_flag) {
+        // Normalise, gate, store fp16 (qwen3_5.rs:711-714).
+        const size_t t = static_cast<size_t>(start + (q_ok ? qi : 0));
+        const float inv = q_ok && l_sum > 0.f ? 1.0f / l_sum : 0.f;
+        const float *gate = a.proj + t * a.ldp + h * 2 * HD + HD;
+        __half *dst = static_cast<__half *>(a.out) + t * a.ldo + h * HD;
+        const bool g4 = (a.ldp % 4) == 0;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+            float o[32];
+            tmem_ld32(lane_base + TM_O + c, o);
+            if (q_ok) {
+                float gv[32];
+                if (g4) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const float4 x = *reinterpret_cast<const float4 *>(gate + c + j);
+                        gv[j] = x.x;
+                        gv[j + 1] = x.y;
+                        gv[j + 2] = x.z;
+                        gv[j + 3] = x.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) gv[j] = gate[c + j];
+                }
+                // fp16 output: the fast exponential and division are exact enough.
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = o[j] * inv * __fdividef(1.0f, 1.0f + __expf(-gv[j]));
+#pragma unroll
+                for (int c8 = 0; c8 < 4; ++c8) st8h(reinterpret_cast<uint8_t *>(dst + c + c8 * 8), o + c8 * 8);
+            }
+        }
+    } else if (tid == 0) {
+        mma_commit(bar_drain);  // let every issued MMA finish before freeing TMEM
+        (void)mbar_wait(bar_drain, 0);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, TM_COLS);
+    }
+}
+
+template <int HD>
+void launch_t5(const AttnArgs &a, cudaStream_t s) {
+    static bool set[64] = {};
+    int dev = 0;
+    HK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !set[dev]) {
+        HK_CUDA(cudaFuncSetAttribute(attn_t5_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Tiles<HD>::SMEM));
+        if (dev >= 0 && dev < 64) set[dev] = true;
+    }
+    dim3 grid(ceil_div(a.max_len, BM), a.nh, a.n_rows);
+    attn_t5_kernel<HD><<<grid, THREADS, Tiles<HD>::SMEM, s>>>(a);
+    HK_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+bool attention_t5_supported(const AttnArgs &a) {
+    return (a.hd == 128 || a.hd == 256) && a.nkv > 0 && a.nh % a.nkv == 0 && (a.ldo % 8) == 0;
+}
+
+void launch_attention_t5(const AttnArgs &a, cudaStream_t s) {
+    if (a.hd == 256)
+        launch_t5<256>(a, s);
+    else if (a.hd == 128)
+        launch_t5<128>(a, s);
+    else
+        throw CudaError("tcgen05 attention supports head_dim 128 or 256");
+}
+
+}  // namespace hk

@@ -924,6 +924,7 @@ struct Model {
                 at.pages = pages;
                 at.pre_len = cr ? cr->pre_len : nullptr;
                 at.kv_in = in_a;
+                at.err = err;
                 if (out_a) launch_kv_store(A, at, out_a, stream);
                 ev = prof_begin();
                 launch_attention(A, at, stream);

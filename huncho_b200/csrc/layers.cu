@@ -757,6 +757,10 @@ void launch_attn_prep(int act, const AttnPrepArgs &a, cudaStream_t s) {
 void launch_attention(int act, const AttnArgs &a, cudaStream_t s) {
     if (a.n <= 0) return;
     if (a.hd > 256) throw CudaError("attention supports head_dim up to 256");
+    if (act == kActF16 && attention_t5_supported(a)) {
+        launch_attention_t5(a, s);
+        return;
+    }
     if (act == kActF16 && attention_tc_supported(a.hd)) {
         launch_attention_tc(a, s);
         return;

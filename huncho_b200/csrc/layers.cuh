@@ -157,8 +157,13 @@ struct AttnArgs {
     // type); its own tokens follow at absolute positions P, P+1, ...
     const int32_t *pre_len = nullptr;
     const uint64_t *kv_in = nullptr;
+    uint32_t *err = nullptr;  // device error word (bounded waits of the tcgen05 kernel)
 };
 void launch_attention(int act, const AttnArgs &a, cudaStream_t s);
+// The tcgen05 kernel behind launch_attention for fp16 activations and
+// head_dim 128 / 256 (TMEM accumulators, 128-query tiles).
+bool attention_t5_supported(const AttnArgs &a);
+void launch_attention_t5(const AttnArgs &a, cudaStream_t s);
 // Output snapshot K/V of each row with kv_out[row] != 0: the cached prefix
 // keys (from kv_in) then the row's own keys (from the workspace slots), as
 // K [P+L][nkv][hd] then V [P+L][nkv][hd].

@@ -221,6 +221,35 @@ def test_attention_vs_torch(lib, act, hd):
     torch.testing.assert_close(out.float(), ref, rtol=tol, atol=tol)
 
 
+@pytest.mark.parametrize("hd", [128, 256])
+@pytest.mark.parametrize("qscale", [1.0, 6.0])
+def test_attention_long_rows_vs_torch(lib, hd, qscale):
+    """fp16 attention on rows that span several 128-query and 64-key tiles
+    (1-token rows, exact tile boundaries, a ragged 700-token row), with score
+    scales that move each row's max by tens of log2 units across tiles (the
+    online softmax's rescale path)."""
+    g = torch.Generator(device="cuda").manual_seed(hd + int(qscale))
+    nh, nkv = 8, 2
+    lens = [300, 1, 128, 700, 64, 129]
+    n = sum(lens)
+    q = (torch.randn(n, nh, hd, device="cuda", generator=g) * qscale).half()
+    k = torch.randn(n, nkv, hd, device="cuda", generator=g).half()
+    v = torch.randn(n, nkv, hd, device="cuda", generator=g).half()
+    proj = torch.randn(n, nh, 2 * hd, device="cuda", generator=g)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device="cuda")
+    tok_row = torch.tensor(np.repeat(np.arange(len(lens)), lens), dtype=torch.int32, device="cuda")
+    out = torch.zeros(n, nh * hd, device="cuda", dtype=torch.half)
+    lib.hk_op_attention.argtypes = ([ctypes.c_int] + [ctypes.c_void_p] * 4 + [ctypes.c_int] + [ctypes.c_void_p] * 2
+                                    + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p])
+    rc = lib.hk_op_attention(1, _p(q), _p(k), _p(v), _p(proj), nh * 2 * hd, _p(cu), _p(tok_row), n, len(lens),
+                             max(lens), nh, nkv, hd, _p(out), nh * hd, None)
+    assert rc == 0, lib.hk_op_last_error()
+    torch.cuda.synchronize()
+    ref = _attn_ref(q.float(), k.float(), v.float(), proj.float()[:, :, hd:], lens, nh, nkv)
+    assert torch.isfinite(out.float()).all()
+    torch.testing.assert_close(out.float(), ref, rtol=5e-3, atol=5e-3)
+
+
 def _readout_inputs(g, n_tok, hidden, dp, n_dec, n_opt):
     x = torch.randn(n_tok, hidden, device="cuda", generator=g)
     w = 1.0 + 0.1 * torch.rand(hidden, device="cuda", generator=g)
