@@ -277,12 +277,7 @@ def main():
         if world > 1:
             dist.barrier()
 
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    from huncho_b200.replicas import max_over_ranks
 
     name, store = ("kev-0.8b", "bf16")
     dtype = {1: "fp32", 2: "bf16", 3: "int8w", 4: "bf16"}.get(args.config, "bf16")
