@@ -796,8 +796,37 @@ struct Model {
             ev = prof_begin();
             launch_rmsnorm(A, x, c.hidden, L.in_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream);
             prof_end(ev, 4, 0);
+            // Half-precision models: the warp-specialised delta layer kernel.
+            const bool pipe = !L.full && dtype != HK_DTYPE_FP32 && c.dk == 128 && c.dv == 128 && c.taps == 4 &&
+                              c.nk > 0 && c.nv % c.nk == 0 && (ldp % 4) == 0 && (c.conv_dim() % 4) == 0;
             gemm(L.mix_in, xn, ld_xn, n_tok, proj, ldp, kEpiStoreF32);
-            if (!L.full) {
+            if (pipe) {
+                if (out_b)
+                    launch_conv_history(proj, ldp, c.conv_dim(), c.taps, cu_seqlens, n_rows, in_b, out_b, stream);
+                DeltaRecArgs r;
+                r.cu_seqlens = cu_seqlens;
+                r.row_order = row_order;
+                r.n_rows = n_rows;
+                r.nk = c.nk;
+                r.nv = c.nv;
+                r.dk = c.dk;
+                r.dv = c.dv;
+                r.exact = 0;
+                r.state_in = in_a;
+                r.state_out = out_a;
+                r.err = err;
+                DeltaFusedInput in;
+                in.proj = proj;
+                in.ldp = ldp;
+                in.conv_dim = c.conv_dim();
+                in.conv_w = L.conv_w;
+                in.base_g = L.base_g;
+                in.dt_bias = L.dt_bias;
+                in.hist_in = in_b;
+                ev = prof_begin();
+                launch_delta_pipe(r, in, L.gnorm_w, c.eps, static_cast<__half *>(mix), ldmix, stream);
+                prof_end(ev, 1, delta_chunk_flops(n_tok, c));
+            } else if (!L.full) {
                 DeltaPrepArgs d;
                 d.proj = proj;
                 d.ldp = ldp;

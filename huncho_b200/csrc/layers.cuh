@@ -93,13 +93,19 @@ void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp,
 // the b / a projections from proj and does the conv + SiLU, the l2norm and the
 // gates itself; r.q/k/v/g/beta are unused. hist_in as in DeltaPrepArgs.
 struct DeltaFusedInput {
-    const float *proj;
-    int ldp, conv_dim;
-    const float *conv_w, *base_g, *dt_bias;
+    const float *proj = nullptr;
+    int ldp = 0, conv_dim = 0;
+    const float *conv_w = nullptr, *base_g = nullptr, *dt_bias = nullptr;
     const uint64_t *hist_in = nullptr;
 };
 void launch_delta_chunk_fused(const DeltaRecArgs &r, const DeltaFusedInput &in, const float *norm_w, float eps,
                               __half *mix, int ldmix, cudaStream_t s);
+// The warp-specialised form of the fused delta layer (4 warps prepare chunk
+// j+1's state-independent operands while 8 warps run chunk j's state-dependent
+// products); 128-wide heads, 4 taps.
+bool delta_pipe_supported(const DeltaRecArgs &r, const DeltaFusedInput &in);
+void launch_delta_pipe(const DeltaRecArgs &r, const DeltaFusedInput &in, const float *norm_w, float eps, __half *mix,
+                       int ldmix, cudaStream_t s);
 
 // out[t, h*dv + j] = rms(o)[j] * w[j] * silu(z[t, h, j]) (qwen3_5.rs:193-201,
 // 934-938); o and z fp32, out in the activation type (the out_proj input).
