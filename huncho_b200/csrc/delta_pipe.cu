@@ -223,13 +223,15 @@ __global__ void __launch_bounds__(THREADS, 1) delta_pipe_kernel(PipeArgs a) {
             bar_sync(BAR_STATE, STHREADS);  // every state warp has read U: D may overwrite it
             __half (*Dh)[LDH] = reinterpret_cast<__half (*)[LDH]>(&H.U[0][0]);
             __half (*Dl)[LDH] = Dh + C;
+            const float gm0 = H.gam[mt * 16 + g4], gm1 = H.gam[mt * 16 + g4 + 8];
 #pragma unroll
             for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int t = mt * 16 + g4 + (e >> 1) * 8, c = nb + nt * 8 + 2 * t4 + (e & 1);
-                    o[nt][e] *= H.gam[t];
-                    split_store(&Dh[t][c], &Dl[t][c], u[nt][e]);
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int t = mt * 16 + g4 + hf * 8, c = nb + nt * 8 + 2 * t4;
+                    o[nt][2 * hf] *= hf ? gm1 : gm0;
+                    o[nt][2 * hf + 1] *= hf ? gm1 : gm0;
+                    split_store2(&Dh[t][c], &Dl[t][c], u[nt][2 * hf], u[nt][2 * hf + 1]);
                 }
             bar_sync(BAR_STATE, STHREADS);  // every row of D written
             // ---- O += Mq D (three split products); Mq is lower triangular, so
@@ -513,23 +515,18 @@ __global__ void __launch_bounds__(THREADS, 1) delta_pipe_kernel(PipeArgs a) {
             float col[C];
 #pragma unroll
             for (int t = 0; t < C; ++t) {
-                float acc0 = (t == lane) ? 1.f : 0.f, acc1 = 0.f;
+                float acc[4] = {(t == lane) ? 1.f : 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int s = 0; s + 4 <= t; s += 4) {
                     const float4 a4 = *reinterpret_cast<const float4 *>(&sm.A[t][s]);
-                    acc0 = fmaf(-a4.x, col[s], acc0);
-                    acc1 = fmaf(-a4.y, col[s + 1], acc1);
-                    acc0 = fmaf(-a4.z, col[s + 2], acc0);
-                    acc1 = fmaf(-a4.w, col[s + 3], acc1);
+                    acc[0] = fmaf(-a4.x, col[s], acc[0]);
+                    acc[1] = fmaf(-a4.y, col[s + 1], acc[1]);
+                    acc[2] = fmaf(-a4.z, col[s + 2], acc[2]);
+                    acc[3] = fmaf(-a4.w, col[s + 3], acc[3]);
                 }
 #pragma unroll
-                for (int s = t & ~3; s < t; ++s) {
-                    if (s & 1)
-                        acc1 = fmaf(-sm.A[t][s], col[s], acc1);
-                    else
-                        acc0 = fmaf(-sm.A[t][s], col[s], acc0);
-                }
-                col[t] = acc0 + acc1;
+                for (int s = t & ~3; s < t; ++s) acc[s & 3] = fmaf(-sm.A[t][s], col[s], acc[s & 3]);
+                col[t] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
                 sm.T[t][lane] = __float2half_rn(col[t]);
             }
         } else {

@@ -71,6 +71,14 @@ __device__ __forceinline__ void split_store(__half *hi, __half *lo, float v) {
     *lo = __float2half_rn(v - __half2float(h));
 }
 
+// Two consecutive fp16 values (hi and lo parts of v0, v1) as 4-byte stores.
+__device__ __forceinline__ void split_store2(__half *hi, __half *lo, float v0, float v1) {
+    const __half2 h = __floats2half2_rn(v0, v1);
+    const float2 f = __half22float2(h);
+    *reinterpret_cast<__half2 *>(hi) = h;
+    *reinterpret_cast<__half2 *>(lo) = __floats2half2_rn(v0 - f.x, v1 - f.y);
+}
+
 // Four consecutive fp16 values as one 8-byte store (hi and lo parts of v).
 __device__ __forceinline__ void split_store4(__half *hi, __half *lo, const float (&v)[4]) {
     __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
