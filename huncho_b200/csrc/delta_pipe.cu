@@ -511,23 +511,32 @@ __global__ void __launch_bounds__(THREADS, 1) delta_pipe_kernel(PipeArgs a) {
         }
         bar_sync(BAR_PREP, PTHREADS);
         if (pw == 0) {
-            // ---- T = (I + A)^{-1} by forward substitution (lane = column).
-            float col[C];
+            // ---- T = (I + A)^{-1}. Diagonal 16 x 16 blocks by forward substitution
+            // (lanes 0-15: columns of T11, lanes 16-31: columns of T22), written in
+            // place over A (fp32) and into T (fp16).
+            const int o = lane & 16;
+            float col[16];
 #pragma unroll
-            for (int t = 0; t < C; ++t) {
-                float acc[4] = {(t == lane) ? 1.f : 0.f, 0.f, 0.f, 0.f};
+            for (int t = 0; t < 16; ++t) {
+                const float *arow = &sm.A[o + t][o];
+                float acc[4] = {(t == (lane & 15)) ? 1.f : 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int s = 0; s + 4 <= t; s += 4) {
-                    const float4 a4 = *reinterpret_cast<const float4 *>(&sm.A[t][s]);
+                    const float4 a4 = *reinterpret_cast<const float4 *>(arow + s);
                     acc[0] = fmaf(-a4.x, col[s], acc[0]);
                     acc[1] = fmaf(-a4.y, col[s + 1], acc[1]);
                     acc[2] = fmaf(-a4.z, col[s + 2], acc[2]);
                     acc[3] = fmaf(-a4.w, col[s + 3], acc[3]);
                 }
 #pragma unroll
-                for (int s = t & ~3; s < t; ++s) acc[s & 3] = fmaf(-sm.A[t][s], col[s], acc[s & 3]);
+                for (int s = t & ~3; s < t; ++s) acc[s & 3] = fmaf(-arow[s], col[s], acc[s & 3]);
                 col[t] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-                sm.T[t][lane] = __float2half_rn(col[t]);
+            }
+            __syncwarp();  // every lane has read its rows of A
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+                sm.A[o + t][lane] = col[t];
+                sm.T[o + t][lane] = __float2half_rn(col[t]);
             }
         } else {
             // ---- decayed keys e^{G_C - G_s} (k hi + lo), meanwhile.
@@ -544,6 +553,22 @@ __global__ void __launch_bounds__(THREADS, 1) delta_pipe_kernel(PipeArgs a) {
                 const float kd[4] = {dec * (h0.x + l0.x), dec * (h0.y + l0.y), dec * (h1.x + l1.x), dec * (h1.y + l1.y)};
                 store4(&H.Kd[r][c], kd);
             }
+        }
+        bar_sync(BAR_PREP, PTHREADS);
+        // ---- T21 = -T22 A21 T11: X = A21 T11 into the (zero) upper-right block
+        // of A, then T21 = -T22 X; thread (i, jj) of 16 x 16.
+        {
+            const int i = ptid >> 4, jj = ptid & 15;
+            float x = 0.f;
+#pragma unroll
+            for (int m = 0; m < 16; ++m) x = fmaf(sm.A[16 + i][m], sm.A[m][jj], x);
+            sm.A[i][16 + jj] = x;
+            bar_sync(BAR_PREP, PTHREADS);
+            float y = 0.f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) y = fmaf(sm.A[16 + i][16 + k], sm.A[k][16 + jj], y);
+            sm.T[16 + i][jj] = __float2half_rn(-y);
+            sm.T[i][16 + jj] = __float2half_rn(0.f);
         }
         bar_sync(BAR_PREP, PTHREADS);
         // ---- U = T (b v) (hi + lo), W = T (b gam k); warp pw owns cols 16 pw ..
