@@ -10,9 +10,10 @@ its own 32 requests (weak scaling; replicas, no collective on the data path).
 
   value  device time of K steps with inputs resident in HBM (hk_score_device),
          L2 flushed between steps (256 MiB write, outside the timed events);
-  e2e    the same K steps through the public host API (KevBackend.score_packed
-         -> hk_score: host->device copy of the inputs, device->host read of the
-         logits), plus host calibration and answers, wall clock;
+  e2e    the same K steps through the public host API (KevBackend.score_answers
+         -> hk_score_answers: host->device copy of the inputs, forward,
+         calibration and answer fields on the device, device->host read of the
+         probabilities and answers), plus the answer dicts, wall clock;
 both are the max over ranks. `--impl reference` times the CPU reference path
 (the oracle restatement of the reference's CPU fp32 forward) on rank 0.
 """
@@ -390,8 +391,10 @@ def main():
     dev_total_s = max_over_ranks(sum(step_ms) / 1000.0)
 
     # ---- e2e: the public host API, host calibration and answers included
-    h2d = sum(tok.nbytes + cu.nbytes + pos.nbytes + cup.nbytes for _, tok, cu, pos, cup, _ in packed)
-    d2h = sum(4 * int(cup[-1]) + 4 for _, _, _, _, cup, _ in packed)
+    # e2e per native batch: inputs + question types up; probabilities, answer
+    # records (16 bytes per row) and the error word down.
+    h2d = sum(tok.nbytes + cu.nbytes + pos.nbytes + cup.nbytes + 4 * len(g) for g, tok, cu, pos, cup, _ in packed)
+    d2h = sum(4 * int(cup[-1]) + 16 * len(g) + 4 for g, _, _, _, cup, _ in packed)
 
     if fork_plan is not None:
         h2d = sum(4 * len(p) + 8 for p in fork_plan[0]) + sum(
@@ -403,13 +406,13 @@ def main():
             fork_step(True)
             return
         for g, tok, cu, pos, cup, _ in packed:
-            logits = backend.score_packed(tok, cu, pos, cup)
+            # One call per native batch: forward + on-device calibration and answers.
+            probs, rec = backend.score_answers(tok, cu, pos, cup, [wl.qtypes[i] for i in g])
             for j, i in enumerate(g):
                 lo, hi = int(cup[j]), int(cup[j + 1])
-                probs = calibration.calibrate(logits[lo:hi], backend.temperature)
                 q = engine.Question(wl.qtypes[i], labels=[str(x) for x in range(hi - lo)],
                                     descriptions=["" for _ in range(hi - lo)])
-                engine.build_answer(q, engine.candidates_for(q, wl.positions[i]), probs)
+                engine.answer_from_record(q, engine.candidates_for(q, wl.positions[i]), probs[lo:hi], rec[j])
 
     e2e_step()
     barrier()
@@ -466,8 +469,11 @@ def main():
                        "suffix_tokens_per_step": sum(int(a[1][-1]) for _, a in fork_plan[2]) * world}
                       if fork_plan is not None else {})},
         "e2e": {"value": reqs * args.steps / e2e_total_s, "unit": "requests/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "includes": "hk_score (H2D inputs, forward, D2H logits) + host "
-                                                      "calibration and answers"},
+                "d2h_bytes_per_step": d2h,
+                "includes": ("hk_score_cached branches (H2D inputs, forward, D2H logits) + host calibration and "
+                             "answers" if fork_plan is not None else
+                             "hk_score_answers (H2D inputs and question types, forward, on-device calibration and "
+                             "answer fields, D2H probabilities and answers) + answer dicts")},
         "gpu_launches": int(launches),
         "roofline": {"kernel": "gemm_f16_tc (tcgen05 projections)", "bound": "tensor", "achieved": achieved,
                      "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",

@@ -21,9 +21,12 @@ HK_DTYPE = {"fp32": 0, "bf16": 1, "int8w": 2, "fp16": 3}
 HK_MAX_ROWS = 64
 HK_MAX_CACHED_ROWS = 256
 HK_CACHE_BRANCH, HK_CACHE_CONTINUE, HK_CACHE_PREFILL = 0, 1, 2
+HK_QUESTION = {"choice": 0, "noul": 1, "score": 2}
+HK_ANSWER_OK, HK_ANSWER_NONFINITE_LOGITS, HK_ANSWER_NONFINITE_PROBS = 0, 1, 2
 
 EXPORTED = (
-    "hk_create", "hk_replica", "hk_capabilities_get", "hk_score", "hk_score_device", "hk_score_cached",
+    "hk_create", "hk_replica", "hk_capabilities_get", "hk_score", "hk_score_answers", "hk_score_device",
+    "hk_score_cached",
     "hk_prefill", "hk_fork", "hk_release_cache", "hk_cache_info",
     "hk_synchronize", "hk_kernel_launches", "hk_set_kv_page_tokens", "hk_profile_enable", "hk_profile_read",
     "hk_last_error",
@@ -38,6 +41,12 @@ class HkCapabilities(ctypes.Structure):
         ("vocab_size", ctypes.c_int32), ("pointer_dim", ctypes.c_int32), ("temperature", ctypes.c_float),
         ("lora_rank", ctypes.c_int32),
     ]
+
+
+class HkAnswer(ctypes.Structure):
+    """hk_answer: one question's answer fields."""
+    _fields_ = [("best", ctypes.c_int32), ("status", ctypes.c_int32), ("confidence", ctypes.c_float),
+                ("value", ctypes.c_float)]
 
 
 _lib = None
@@ -62,6 +71,9 @@ def load(path: Path | None = None) -> ctypes.CDLL:
     lib.hk_capabilities_get.restype = i32
     lib.hk_score.argtypes = [vp, i32, pu32, pi32, pi32, pi32, pf]
     lib.hk_score.restype = i32
+    lib.hk_score_answers.argtypes = [vp, i32, pu32, pi32, pi32, pi32, pi32, ctypes.c_float, pf, pf,
+                                     ctypes.POINTER(HkAnswer)]
+    lib.hk_score_answers.restype = i32
     lib.hk_score_device.argtypes = [vp, i32, pi32, pi32, vp, vp, vp, vp, vp]
     lib.hk_score_device.restype = i32
     pu64, u64 = ctypes.POINTER(ctypes.c_uint64), ctypes.c_uint64

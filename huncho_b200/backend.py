@@ -334,6 +334,43 @@ class KevBackend:
             cup.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
         return out[:int(cup[-1])]
 
+    def score_answers(self, tokens, cu_seqlens, positions, cu_positions, question_types,
+                      temperature: Optional[float] = None, with_logits: bool = False):
+        """hk_score_answers: one question per row, calibrated on the device.
+
+        Returns (probabilities [sum n_pos] fp32, answers: structured array with
+        fields best, status, confidence, value per row[, raw logits]). Question
+        types are "choice", "noul" ([no, yes]) or "score", or their HK_QUESTION
+        codes; the temperature defaults to the package's.
+        """
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint32)
+        cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        cup = np.ascontiguousarray(cu_positions, dtype=np.int32)
+        qt = np.ascontiguousarray([_native.HK_QUESTION[q] if isinstance(q, str) else int(q)
+                                   for q in question_types], dtype=np.int32)
+        n_rows = len(cu) - 1
+        if len(qt) != n_rows:
+            raise BackendError("one question type per row is required")
+        t = self.temperature if temperature is None else float(temperature)
+        p = int(cup[-1])
+        probs = np.empty(max(p, 1), np.float32)
+        logits = np.empty(max(p, 1), np.float32) if with_logits else None
+        answers = (_native.HkAnswer * max(n_rows, 1))()
+        pf = ctypes.POINTER(ctypes.c_float)
+        self._check(self._lib.hk_score_answers(
+            self._h, n_rows, tokens.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)),
+            cu.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), pos.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+            cup.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), qt.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+            ctypes.c_float(t), logits.ctypes.data_as(pf) if with_logits else None, probs.ctypes.data_as(pf),
+            answers))
+        rec = np.array([(a.best, a.status, a.confidence, a.value) for a in answers[:n_rows]],
+                       dtype=[("best", np.int32), ("status", np.int32), ("confidence", np.float32),
+                              ("value", np.float32)])
+        if with_logits:
+            return probs[:p], rec, logits[:p]
+        return probs[:p], rec
+
     def score_device(self, cu_seqlens_host, cu_positions_host, d_tokens: int, d_cu_seqlens: int,
                      d_positions: int, d_out: int, stream: int = 0) -> None:
         """hk_score_device: inputs/outputs are device pointers; asynchronous on `stream`."""

@@ -328,6 +328,9 @@ struct Model {
     float *dq = nullptr, *dkk = nullptr, *dvv = nullptr, *dg = nullptr, *db = nullptr, *dout = nullptr;
     void *aq = nullptr, *ak = nullptr, *av = nullptr;
     float *hn = nullptr, *rproj = nullptr, *logits = nullptr;
+    float *probs = nullptr;           // calibrated probabilities (hk_score_answers)
+    AnswerRec *answers = nullptr;     // [cap_rows]
+    int32_t *qtype_dev = nullptr;     // [cap_rows]
     uint32_t *err = nullptr;
     // device batch description (see build_meta_kernel)
     int32_t *meta = nullptr;
@@ -734,6 +737,9 @@ struct Model {
         hn = dev_alloc<float>(R * c.hidden, ws);
         rproj = dev_alloc<float>(R * dp, ws);
         logits = dev_alloc<float>(R, ws);
+        probs = dev_alloc<float>(R, ws);
+        answers = dev_alloc<AnswerRec>(cap_rows, ws);
+        qtype_dev = dev_alloc<int32_t>(cap_rows, ws);
         meta_cap = 4 * N + 6 * static_cast<size_t>(cap_rows) + 4 * R + 64 + N;  // + block table
         meta = dev_alloc<int32_t>(meta_cap, ws);
     }
@@ -1246,11 +1252,23 @@ static int score_device_impl(hk::Model &m, int n_rows, const int32_t *cu_h, cons
 
 }  // extern "C"
 
-// The host-buffer scoring path shared by hk_score and hk_score_cached. pre[r]
-// is row r's cached prefix length (0 without a cache); cr the device table.
+static_assert(sizeof(hk_answer) == sizeof(hk::AnswerRec), "hk_answer and AnswerRec share one layout");
+
+// Calibrated answers requested with a scoring call (hk_score_answers).
+struct AnswerReq {
+    const int32_t *qtypes;
+    float temperature;
+    float *probs;
+    hk_answer *answers;
+};
+
+// The host-buffer scoring path shared by hk_score, hk_score_cached and
+// hk_score_answers. pre[r] is row r's cached prefix length (0 without a
+// cache); cr the device table; aq the answers to compute on the device.
 static void score_host(hk::Model &m, int n_rows, const uint32_t *tokens, const int32_t *cu_seqlens,
                        const int32_t *positions, const int32_t *cu_positions, float *out_logits,
-                       const std::vector<int> *pre, const hk::Model::CacheRefs *cr) {
+                       const std::vector<int> *pre, const hk::Model::CacheRefs *cr,
+                       const AnswerReq *aq = nullptr) {
     // Validation mirrors forward_independent_batch (qwen3_5.rs:3143-3171)
     // and Backend::forward (qwen3_5.rs:2669-2705).
     if (n_rows < 1 || n_rows > (pre ? HK_MAX_CACHED_ROWS : HK_MAX_ROWS))
@@ -1276,12 +1294,28 @@ static void score_host(hk::Model &m, int n_rows, const uint32_t *tokens, const i
             if (positions[j] < 0 || positions[j] >= len)
                 throw hk::ApiError(HK_ERR_BACKEND, "Qwen3.5 readout position is outside the token sequence");
     }
+    if (aq) {  // calibration.rs:198-218 (temperature), one question per row
+        if (!std::isfinite(aq->temperature) || !(aq->temperature > 0.f))
+            throw hk::ApiError(HK_ERR_ARGUMENT, "temperature must be positive and finite");
+        for (int r = 0; r < n_rows; ++r) {
+            const int np = cu_positions[r + 1] - cu_positions[r], qt = aq->qtypes[r];
+            if (qt != HK_QUESTION_CHOICE && qt != HK_QUESTION_NOUL && qt != HK_QUESTION_SCORE)
+                throw hk::ApiError(HK_ERR_ARGUMENT, "unknown question type");
+            if (np < 1 || (qt == HK_QUESTION_NOUL && np != 2))
+                throw hk::ApiError(HK_ERR_ARGUMENT, "a question needs one readout position per option "
+                                                    "(noul: exactly two, [no, yes])");
+        }
+    }
     const int n = cu_seqlens[n_rows], p = cu_positions[n_rows];
     HK_CUDA(cudaSetDevice(m.device));
     m.ensure_workspace(n, n_rows, p);
     hk::MetaLayout L(n_rows, n, p);
     const size_t in_words = L.pos;  // ids | cu | positions | cu_pos
-    const size_t bytes = in_words * 4 + static_cast<size_t>(p) * 4 + 64;
+    // pinned: inputs | logits | error word | question types | probabilities | answers
+    const size_t bytes = in_words * 4 + static_cast<size_t>(p) * 4 + 64 +
+                         (aq ? static_cast<size_t>(n_rows) * 4 + static_cast<size_t>(p) * 4 +
+                                   static_cast<size_t>(n_rows) * sizeof(hk_answer) + 64
+                             : 0);
     if (bytes > m.pinned_cap) {
         if (m.pinned) cudaFreeHost(m.pinned);
         m.pinned = nullptr;
@@ -1298,7 +1332,27 @@ static void score_host(hk::Model &m, int n_rows, const uint32_t *tokens, const i
     score_device_impl(m, n_rows, cu_seqlens, cu_positions, m.stream, cr);
     float *res = reinterpret_cast<float *>(st + in_words);
     uint32_t *errw = reinterpret_cast<uint32_t *>(res + p);
-    if (p) HK_CUDA(cudaMemcpyAsync(res, m.logits, static_cast<size_t>(p) * 4, cudaMemcpyDeviceToHost, m.stream));
+    int32_t *qt_h = reinterpret_cast<int32_t *>(errw + 16);
+    float *pr_h = reinterpret_cast<float *>(qt_h + n_rows);
+    hk_answer *ans_h = reinterpret_cast<hk_answer *>(pr_h + p + 8);
+    if (aq) {
+        std::memcpy(qt_h, aq->qtypes, static_cast<size_t>(n_rows) * 4);
+        HK_CUDA(cudaMemcpyAsync(m.qtype_dev, qt_h, static_cast<size_t>(n_rows) * 4, cudaMemcpyHostToDevice, m.stream));
+        hk::AnswerArgs a;
+        a.logits = m.logits;
+        a.cu_positions = m.meta + L.cu_pos;
+        a.qtype = m.qtype_dev;
+        a.n_rows = n_rows;
+        a.temperature = aq->temperature;
+        a.probs = m.probs;
+        a.out = m.answers;
+        hk::launch_answers(a, m.stream);
+        HK_CUDA(cudaMemcpyAsync(pr_h, m.probs, static_cast<size_t>(p) * 4, cudaMemcpyDeviceToHost, m.stream));
+        HK_CUDA(cudaMemcpyAsync(ans_h, m.answers, static_cast<size_t>(n_rows) * sizeof(hk_answer),
+                                cudaMemcpyDeviceToHost, m.stream));
+    }
+    if (p && out_logits)
+        HK_CUDA(cudaMemcpyAsync(res, m.logits, static_cast<size_t>(p) * 4, cudaMemcpyDeviceToHost, m.stream));
     HK_CUDA(cudaMemcpyAsync(errw, m.err, 4, cudaMemcpyDeviceToHost, m.stream));
     HK_CUDA(cudaStreamSynchronize(m.stream));
     if (*errw) {
@@ -1306,7 +1360,11 @@ static void score_host(hk::Model &m, int n_rows, const uint32_t *tokens, const i
         HK_CUDA(cudaStreamSynchronize(m.stream));
         throw hk::ApiError(HK_ERR_CUDA, "device error flag " + std::to_string(*errw) + " set during the forward");
     }
-    if (p) std::memcpy(out_logits, res, static_cast<size_t>(p) * 4);
+    if (p && out_logits) std::memcpy(out_logits, res, static_cast<size_t>(p) * 4);
+    if (aq) {
+        std::memcpy(aq->probs, pr_h, static_cast<size_t>(p) * 4);
+        std::memcpy(aq->answers, ans_h, static_cast<size_t>(n_rows) * sizeof(hk_answer));
+    }
 }
 
 extern "C" {
@@ -1317,6 +1375,19 @@ int hk_score(hk_model *h, int n_rows, const uint32_t *tokens, const int32_t *cu_
     hk::Model &m = *h->m;
     return guarded(h, [&]() -> int {
         score_host(m, n_rows, tokens, cu_seqlens, positions, cu_positions, out_logits, nullptr, nullptr);
+        return HK_OK;
+    });
+}
+
+int hk_score_answers(hk_model *h, int n_rows, const uint32_t *tokens, const int32_t *cu_seqlens,
+                     const int32_t *positions, const int32_t *cu_positions, const int32_t *question_types,
+                     float temperature, float *out_logits, float *out_probs, hk_answer *out_answers) {
+    if (!h || !h->m || !cu_seqlens || !cu_positions || !question_types || !out_probs || !out_answers)
+        return HK_ERR_ARGUMENT;
+    hk::Model &m = *h->m;
+    return guarded(h, [&]() -> int {
+        const AnswerReq aq{question_types, temperature, out_probs, out_answers};
+        score_host(m, n_rows, tokens, cu_seqlens, positions, cu_positions, out_logits, nullptr, nullptr, &aq);
         return HK_OK;
     });
 }

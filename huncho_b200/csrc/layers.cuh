@@ -200,4 +200,23 @@ struct ReadoutArgs {
 };
 void launch_readout(const ReadoutArgs &a, cudaStream_t s);
 
+// Calibrated probabilities and typed answers of every question of a batch
+// (answers.cu). Layout of AnswerRec equals the C ABI's hk_answer.
+enum : int { kQuestionChoice = 0, kQuestionNoul = 1, kQuestionScore = 2 };
+enum : int { kAnswerNonfiniteLogits = 1, kAnswerNonfiniteProbs = 2 };
+struct AnswerRec {
+    int32_t best, status;
+    float confidence, value;
+};
+struct AnswerArgs {
+    const float *logits;          // [cu_positions[n_rows]] raw pointer logits
+    const int32_t *cu_positions;  // [n_rows + 1]
+    const int32_t *qtype;         // [n_rows] kQuestion*
+    int n_rows;
+    float temperature;
+    float *probs;     // [cu_positions[n_rows]]
+    AnswerRec *out;   // [n_rows]
+};
+void launch_answers(const AnswerArgs &a, cudaStream_t s);
+
 }  // namespace hk

@@ -100,3 +100,47 @@ def score_rows(backend, rows: Sequence[Sequence[int]], positions: Sequence[Seque
             raw = o.values[:, 0]
             out.append((raw, calibration.calibrate(raw, t)))
     return out
+
+
+def answer_from_record(q: Question, candidates: Sequence[Candidate], probabilities, record) -> dict:
+    """The build_answer dict from a device answer record (hk_answer: best,
+    status, confidence, value) and the device probabilities."""
+    if int(record["status"]) != 0:
+        raise CalibrationError("temperature scaling produced nonfinite probabilities"
+                               if int(record["status"]) == 2 else "logits must be finite")
+    p = np.asarray(probabilities, dtype=np.float32)
+    if len(candidates) != p.size:
+        raise CalibrationError(f"candidate/probability count mismatch: {len(candidates)} vs {p.size}")
+    conf, value, best = float(record["confidence"]), float(record["value"]), int(record["best"])
+    if q.type == "choice":
+        return {"type": "choice", "choice": candidates[best].label, "confidence": conf,
+                "probabilities": {c.label: float(p[c.index]) for c in candidates}}
+    if q.type == "score":
+        return {"type": "score", "score": value, "confidence": conf,
+                "legend": {c.label: (c.description or "") for c in candidates},
+                "probabilities": {c.label: float(p[c.index]) for c in candidates}}
+    if q.type == "noul":
+        return {"type": "noul", "noul": value}
+    raise ValueError(f"unknown question type {q.type}")
+
+
+def score_questions(backend, rows: Sequence[Sequence[int]], positions: Sequence[Sequence[int]],
+                    questions: Sequence[Question], temperature: Optional[float] = None) -> list:
+    """Answers of independent question rows, calibrated on the device.
+
+    The same answers as score_rows + build_answer (calibration.rs:36-64,
+    87-147; engine.rs:1448-1513), computed for each group of at most
+    `batch_limits().max_rows` rows by one hk_score_answers call.
+    """
+    from .backend import pack_rows
+    limit = backend.batch_limits().max_rows
+    out = []
+    for s in range(0, len(rows), limit):
+        rs, ps, qs = rows[s:s + limit], positions[s:s + limit], questions[s:s + limit]
+        probs, rec = backend.score_answers(*pack_rows(rs, ps), [q.type for q in qs], temperature=temperature)
+        k = 0
+        for q, pos, r in zip(qs, ps, rec):
+            n = len(pos)
+            out.append(answer_from_record(q, candidates_for(q, pos), probs[k:k + n], r))
+            k += n
+    return out

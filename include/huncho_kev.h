@@ -106,6 +106,43 @@ int hk_score(hk_model *m, int n_rows, const uint32_t *tokens, const int32_t *cu_
              const int32_t *positions, const int32_t *cu_positions, float *out_logits);
 
 /*
+ * hk_score plus calibrated answers computed on the device, one question per
+ * row (the reference calibrates on the host after Backend::forward; the
+ * arithmetic is its own: crates/huncho-core/src/calibration.rs:36-64
+ * temperature softmax with fp32 exponentials and an fp64 sum and division,
+ * 87-95 first-maximum argmax, 114-127 peak confidence, 131-147 Kev's score
+ * confidence, 172-218 validation; Engine::build_answer,
+ * crates/huncho-core/src/engine.rs:1448-1513).
+ *   question_types [n_rows] HK_QUESTION_CHOICE, HK_QUESTION_NOUL (exactly two
+ *                  options, in the order [no, yes]) or HK_QUESTION_SCORE
+ *                  (options are the levels 0, 1, ...)
+ *   temperature    the package temperature (finite and > 0, else
+ *                  HK_ERR_ARGUMENT)
+ *   out_logits     [cu_positions[n_rows]] raw pointer logits, or NULL
+ *   out_probs      [cu_positions[n_rows]] calibrated probabilities
+ *   out_answers    [n_rows]
+ * Every question needs at least one option, else HK_ERR_ARGUMENT. A question
+ * whose logits or probabilities are not finite gets status
+ * HK_ANSWER_NONFINITE_LOGITS / HK_ANSWER_NONFINITE_PROBS (the reference
+ * rejects such a request with a calibration error).
+ */
+#define HK_QUESTION_CHOICE 0
+#define HK_QUESTION_NOUL 1
+#define HK_QUESTION_SCORE 2
+#define HK_ANSWER_OK 0
+#define HK_ANSWER_NONFINITE_LOGITS 1
+#define HK_ANSWER_NONFINITE_PROBS 2
+typedef struct hk_answer {
+    int32_t best;     /* first-maximum option index (choice: the chosen label) */
+    int32_t status;   /* HK_ANSWER_* */
+    float confidence; /* peak confidence; Kev's score confidence for score questions */
+    float value;      /* noul: P(yes); score: sum_i i * p_i; choice: p[best] */
+} hk_answer;
+int hk_score_answers(hk_model *m, int n_rows, const uint32_t *tokens, const int32_t *cu_seqlens,
+                     const int32_t *positions, const int32_t *cu_positions, const int32_t *question_types,
+                     float temperature, float *out_logits, float *out_probs, hk_answer *out_answers);
+
+/*
  * Cached prefixes (prefill / fork). A cache handle names the model state after
  * a token sequence: every delta layer's recurrent state and conv tail, every
  * attention layer's K/V (the reference's LayerCache, qwen3_5.rs:1111-1125),

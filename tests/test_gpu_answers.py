@@ -1,0 +1,142 @@
+"""Calibrated answers on the device (hk_score_answers) against the host
+calibration and answer code, which follows the reference's calibration.rs and
+Engine::build_answer (and is pinned to the upstream golden probabilities in
+test_oracle_golden.py).
+
+The device repeats every fp32 step of the host in the same order, with no
+fused multiply-adds; its fp32 exponential is the fp64 one rounded to fp32, so
+probabilities may differ from the host's in the last bit of an exponential:
+the gate is 3e-7 on probabilities, 1e-6 on confidences and values, and the
+same chosen option.
+"""
+import json
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+from huncho_b200 import _native, calibration, engine, synth
+from huncho_b200.backend import pack_rows
+
+from conftest import GOLDEN
+
+
+def _backend(path, dtype, max_context=4096):
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from huncho_b200.backend import KevBackend
+    return KevBackend(path, device=0, dtype=dtype, max_context=max_context)
+
+
+def _question(qtype, n):
+    if qtype == "noul":
+        return engine.Question("noul")
+    if qtype == "choice":
+        return engine.Question("choice", labels=[f"L{i}" for i in range(n)])
+    return engine.Question("score", descriptions=[f"level {i}" for i in range(n)])
+
+
+def _check(b, rows, positions, qtypes, temperature=None):
+    packed = pack_rows(rows, positions)
+    probs, ans, logits = b.score_answers(*packed, qtypes, temperature=temperature, with_logits=True)
+    raw = b.score_packed(*packed)
+    np.testing.assert_array_equal(logits, raw)  # the same forward
+    t = b.temperature if temperature is None else temperature
+    k = 0
+    for i, (pos, qt) in enumerate(zip(positions, qtypes)):
+        n = len(pos)
+        host_p = calibration.calibrate(raw[k:k + n], t)
+        dev_p = probs[k:k + n]
+        assert np.abs(dev_p - host_p).max() <= 3e-7, (qt, dev_p, host_p)
+        q = _question(qt, n)
+        cands = engine.candidates_for(q, pos)
+        host = engine.build_answer(q, cands, host_p)
+        assert ans["status"][i] == _native.HK_ANSWER_OK
+        assert ans["best"][i] == calibration.argmax(host_p.tolist())
+        # A noul answer carries P(yes) only; its confidence field is the peak one.
+        conf = host["confidence"] if "confidence" in host else calibration.confidence_peak(host_p)
+        assert abs(float(ans["confidence"][i]) - conf) <= 1e-6
+        if qt == "noul":
+            assert abs(float(ans["value"][i]) - host["noul"]) <= 1e-6
+        elif qt == "score":
+            assert abs(float(ans["value"][i]) - host["score"]) <= 1e-6
+        else:
+            assert cands[int(ans["best"][i])].label == host["choice"]
+            assert abs(float(ans["value"][i]) - float(host_p[int(ans["best"][i])])) <= 3e-7
+        k += n
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_golden_rows_answers_match_host(native_lib, dtype):
+    golden = json.loads((GOLDEN / "golden.json").read_text())
+    b = _backend(GOLDEN, dtype, max_context=512)
+    rows = [r["tokens"] for c in golden["cases"] for r in c["rows"]]
+    positions = [r["positions"] for c in golden["cases"] for r in c["rows"]]
+    for qt in ("choice", "score"):
+        _check(b, rows, positions, [qt] * len(rows))
+    two = [(r, p) for r, p in zip(rows, positions) if len(p) == 2]
+    if two:
+        _check(b, [r for r, _ in two], [p for _, p in two], ["noul"] * len(two))
+    _check(b, rows, positions, ["score"] * len(rows), temperature=0.37)
+
+
+@pytest.mark.parametrize("name,dtype,store", [("kev-mini", "bf16", "bf16"), ("kev-0.8b-l4", "bf16", "bf16")])
+def test_benchmark_questions_answers_match_host(native_lib, synth_root, name, dtype, store):
+    d = synth.write_model(synth_root / f"{name}-{store}", name=name, seed=0, store=store)
+    b = _backend(d, dtype)
+    wl = synth.make_workload(2, b.vocab_size, seed=3, n_requests=12)
+    _check(b, wl.rows, wl.positions, list(wl.qtypes))
+
+
+def test_answer_arguments_and_nonfinite_status(native_lib, synth_root):
+    from huncho_b200.errors import BackendError
+    d = synth.write_model(synth_root / "kev-mini-bf16", name="kev-mini", seed=0, store="bf16")
+    b = _backend(d, "bf16")
+    rng = np.random.default_rng(0)
+    rows = [rng.integers(0, b.vocab_size, 20).tolist() for _ in range(3)]
+    pos = [[3, 9], [1, 4, 19], [7, 8]]
+    packed = pack_rows(rows, pos)
+    for bad_t in (0.0, -1.0, float("nan"), float("inf")):
+        with pytest.raises(BackendError):
+            b.score_answers(*packed, ["noul", "choice", "noul"], temperature=bad_t)
+    with pytest.raises(BackendError):  # noul needs exactly two options
+        b.score_answers(*packed, ["noul", "noul", "noul"])
+    with pytest.raises(BackendError):
+        b.score_answers(*packed, ["noul", 7, "noul"])
+    with pytest.raises(BackendError):  # one type per row
+        b.score_answers(*packed, ["noul", "choice"])
+    with pytest.raises(BackendError):  # a question without options
+        b.score_answers(*pack_rows(rows, [[3], [], [7]]), ["choice"] * 3)
+    # A subnormal temperature makes 1/T infinite: (l - max) / T is NaN for the
+    # maximum, so every question is rejected as the host rejects it.
+    probs, ans = b.score_answers(*packed, ["noul", "choice", "score"], temperature=1e-45)
+    assert all(s == _native.HK_ANSWER_NONFINITE_PROBS for s in ans["status"])
+    raw = b.score_packed(*packed)
+    from huncho_b200.errors import CalibrationError
+    with pytest.raises(CalibrationError), np.errstate(over="ignore", invalid="ignore"):
+        calibration.calibrate(raw[:2], np.float32(1e-45))
+
+
+def test_score_questions_equals_host_answers(native_lib, synth_root):
+    """engine.score_questions (device calibration, groups of <= 64 rows) gives
+    the answers of score_rows + build_answer."""
+    d = synth.write_model(synth_root / "kev-mini-bf16", name="kev-mini", seed=0, store="bf16")
+    b = _backend(d, "bf16")
+    wl = synth.make_workload(2, b.vocab_size, seed=5, n_requests=30)  # 90 rows: two groups
+    qs = [_question(t, len(p)) for t, p in zip(wl.qtypes, wl.positions)]
+    got = engine.score_questions(b, wl.rows, wl.positions, qs)
+    host = engine.score_rows(b, wl.rows, wl.positions)
+    assert len(got) == len(host) == len(wl.rows)
+    for q, pos, g, (_, hp) in zip(qs, wl.positions, got, host):
+        h = engine.build_answer(q, engine.candidates_for(q, pos), hp)
+        assert g["type"] == h["type"]
+        for key in ("choice",):
+            if key in h:
+                assert g[key] == h[key]
+        for key in ("noul", "score", "confidence"):
+            if key in h:
+                assert abs(g[key] - h[key]) <= 1e-6
+        for lab, v in h.get("probabilities", {}).items():
+            assert abs(g["probabilities"][lab] - v) <= 3e-7
