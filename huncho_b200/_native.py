@@ -17,7 +17,7 @@ HK_ERR_PACKAGE = -3
 HK_ERR_CUDA = -4
 HK_ERR_ARGUMENT = -5
 
-HK_DTYPE = {"fp32": 0, "bf16": 1, "int8w": 2, "fp16": 3}
+HK_DTYPE = {"fp32": 0, "bf16": 1, "int8w": 2, "fp16": 3, "q8_0-fp32": 4, "q4_0-fp32": 5}
 HK_MAX_ROWS = 64
 HK_MAX_CACHED_ROWS = 256
 HK_CACHE_BRANCH, HK_CACHE_CONTINUE, HK_CACHE_PREFILL = 0, 1, 2

@@ -37,4 +37,12 @@ void gemm_f16_tc(const GemmArgs &a, cudaStream_t s, int num_sms);
 // fp32 X and W on CUDA cores (the fp32 model path).
 void gemm_f32_simt(const GemmArgs &a, cudaStream_t s);
 
+// Packed projections (GGML Q8_0 / Q4_0 weights as int8 block values [N, kp]
+// and fp32 block scales [N, kp/32]): the fp32 input rows quantized to Q8_0
+// (q int8 [M, kp], d fp32 [M, kp/32]; columns >= K are zero), then
+// out[m, n] (+)= sum over blocks in order of (float(int dot) * d_w) * d_x.
+void launch_quantize_rows(const float *x, int ldx, int M, int K, int kp, int8_t *q, float *d, cudaStream_t s);
+void gemm_q8(const int8_t *xq, const float *xd, const int8_t *wq, const float *wd, int M, int N, int kp, float *out,
+             int ldo, bool residual, cudaStream_t s);
+
 }  // namespace hk

@@ -28,6 +28,7 @@
 #include "json.hpp"
 #include "layers.cuh"
 #include "safetensors.hpp"
+#include "gguf.hpp"
 
 namespace hk {
 
@@ -181,9 +182,38 @@ float f16_bits_to_f32(uint16_t h) {
     return r;
 }
 
-// All base tensors of a model dir plus the adapter (merged on access).
+// All base tensors of a model dir plus the adapter (merged on access), or the
+// tensors of a packed package's backbone.gguf (merged at conversion).
 class WeightSource {
   public:
+    struct Packed {};
+    WeightSource(const std::string &dir, Packed) : dir_(dir) {
+        try {
+            gguf_.reset(new GgufFile(dir + "/backbone.gguf"));
+        } catch (const std::exception &e) {
+            throw ApiError(HK_ERR_PACKAGE, std::string("packed Kev backbone: ") + e.what());
+        }
+        for (auto &kv : gguf_->tensors()) {
+            std::string k;
+            if (!canonical_weight_name(kv.first, k) || k.rfind("lm_head.", 0) == 0) continue;
+            if (kv.second.type == kGgufF32) {
+                views_.emplace_back(new TensorView);
+                TensorView &v = *views_.back();
+                v.dtype = "F32";
+                v.shape = kv.second.shape;
+                v.data = kv.second.data;
+                v.nbytes = kv.second.nbytes;
+                base_[k] = &v;
+            } else {
+                packed_[k] = &kv.second;
+            }
+        }
+    }
+    const GgufFile *gguf() const { return gguf_.get(); }
+    const GgufTensor *packed(const std::string &k) const {
+        auto it = packed_.find(k);
+        return it == packed_.end() ? nullptr : it->second;
+    }
     WeightSource(const std::string &dir) : dir_(dir) {
         DIR *d = opendir(dir.c_str());
         if (!d) throw ApiError(HK_ERR_PACKAGE, "cannot open model directory " + dir);
@@ -273,6 +303,9 @@ class WeightSource {
 
   private:
     std::string dir_;
+    std::unique_ptr<GgufFile> gguf_;
+    std::vector<std::unique_ptr<TensorView>> views_;
+    std::unordered_map<std::string, const GgufTensor *> packed_;
     std::vector<std::unique_ptr<SafeTensors>> shards_;
     std::unordered_map<std::string, const TensorView *> base_;
     std::unique_ptr<SafeTensors> adapter_;
@@ -286,6 +319,10 @@ struct Mat {
     void *w = nullptr;
     float *scale = nullptr;  // int8-weight models: per row
     int rows = 0, cols = 0, ld = 0;
+    // Packed profiles: int8 block values [rows, kp] and fp32 block scales [rows, kp / 32].
+    int8_t *q = nullptr;
+    float *qd = nullptr;
+    int kp = 0;
 };
 
 struct Layer {
@@ -328,6 +365,11 @@ struct Model {
     float *dq = nullptr, *dkk = nullptr, *dvv = nullptr, *dg = nullptr, *db = nullptr, *dout = nullptr;
     void *aq = nullptr, *ak = nullptr, *av = nullptr;
     float *hn = nullptr, *rproj = nullptr, *logits = nullptr;
+    // Packed profiles: Q8_0 activation rows for the projection in flight.
+    int8_t *xq = nullptr;
+    float *xd = nullptr;
+    int max_kp = 0;
+    std::map<std::string, int> packed_widths;  // huncho.input_widths
     float *probs = nullptr;           // calibrated probabilities (hk_score_answers)
     AnswerRec *answers = nullptr;     // [cap_rows]
     int32_t *qtype_dev = nullptr;     // [cap_rows]
@@ -475,8 +517,11 @@ struct Model {
         prof_recs.push_back({a, b, cls, work});
     }
 
-    int act() const { return dtype == HK_DTYPE_FP32 ? kActF32 : kActF16; }
-    size_t esz() const { return dtype == HK_DTYPE_FP32 ? 4 : 2; }
+    bool packed() const { return dtype == HK_DTYPE_Q8_0 || dtype == HK_DTYPE_Q4_0; }
+    // The fp32 model path: fp32 weights, or the packed profiles (fp32 activations).
+    bool f32_model() const { return dtype == HK_DTYPE_FP32 || packed(); }
+    int act() const { return f32_model() ? kActF32 : kActF16; }
+    size_t esz() const { return f32_model() ? 4 : 2; }
     // The checkpoint value in the model dtype (the reference casts every
     // tensor to it at load): bf16 for the bf16 and int8-weight models.
     float model_round(float v) const {
@@ -522,6 +567,7 @@ struct Model {
     // weight format. `order` optionally permutes output rows (SwiGLU interleave).
     Mat pack(const WeightSource &src, const std::vector<std::pair<std::string, int>> &parts, int K,
              const std::vector<int> *order = nullptr) {
+        if (packed()) return pack_blocks(src, parts, K);
         int R = 0;
         for (auto &p : parts) R += p.second;
         std::vector<float> full(static_cast<size_t>(R) * K);
@@ -576,6 +622,56 @@ struct Model {
         return m;
     }
 
+    // Packed projections: the artifact's Q8_0 / Q4_0 blocks of each part,
+    // rows concatenated, as int8 values (Q4_0 as q - 8) and fp32 scales.
+    Mat pack_blocks(const WeightSource &src, const std::vector<std::pair<std::string, int>> &parts, int K) {
+        const uint32_t want = dtype == HK_DTYPE_Q8_0 ? kGgufQ8_0 : kGgufQ4_0;
+        const int kp = round_up(K, 32), nb = kp / 32;
+        int R = 0;
+        for (auto &p : parts) R += p.second;
+        std::vector<int8_t> q(static_cast<size_t>(R) * kp);
+        std::vector<float> d(static_cast<size_t>(R) * nb);
+        int r0 = 0;
+        for (auto &p : parts) {
+            const GgufTensor *t = src.packed(p.first);
+            if (!t) throw ApiError(HK_ERR_PACKAGE, "packed projection `" + p.first + "` missing");
+            if (t->type != want)
+                throw ApiError(HK_ERR_PACKAGE, "packed projection `" + p.first + "` has another block type");
+            auto wit = packed_widths.find(p.first);
+            if (t->shape.size() != 2 || t->shape[0] != p.second || t->shape[1] != kp || wit == packed_widths.end() ||
+                wit->second != K)
+                throw ApiError(HK_ERR_PACKAGE, "packed projection `" + p.first + "` shape mismatch");
+            const int per = want == kGgufQ8_0 ? 34 : 18;
+            for (int r = 0; r < p.second; ++r)
+                for (int b = 0; b < nb; ++b) {
+                    const uint8_t *blk = t->data + (static_cast<size_t>(r) * nb + b) * per;
+                    uint16_t h;
+                    std::memcpy(&h, blk, 2);
+                    d[static_cast<size_t>(r0 + r) * nb + b] = f16_bits_to_f32(h);
+                    int8_t *dst = &q[static_cast<size_t>(r0 + r) * kp + b * 32];
+                    if (want == kGgufQ8_0) {
+                        std::memcpy(dst, blk + 2, 32);
+                    } else {
+                        for (int j = 0; j < 16; ++j) {
+                            dst[j] = static_cast<int8_t>((blk[2 + j] & 0x0F) - 8);
+                            dst[16 + j] = static_cast<int8_t>((blk[2 + j] >> 4) - 8);
+                        }
+                    }
+                }
+            r0 += p.second;
+        }
+        Mat m;
+        m.rows = R;
+        m.cols = K;
+        m.ld = kp;
+        m.kp = kp;
+        m.q = dev_alloc<int8_t>(q.size(), allocs);
+        HK_CUDA(cudaMemcpy(m.q, q.data(), q.size(), cudaMemcpyHostToDevice));
+        m.qd = upload_f32(d);
+        max_kp = std::max(max_kp, kp);
+        return m;
+    }
+
     // A small fp32 tensor, rounded to the model dtype first (the reference
     // loader casts every tensor to it) and kept in fp32 on the device.
     std::vector<float> small(const WeightSource &src, const std::string &k, std::vector<int64_t> shape) {
@@ -591,11 +687,29 @@ struct Model {
 
     void load(const std::string &model_dir) {
         dir = model_dir;
-        cfg = KevConfig::from_json(json::parse(read_file(model_dir + "/config.json")));
+        std::unique_ptr<WeightSource> srcp(packed() ? new WeightSource(model_dir, WeightSource::Packed{})
+                                                    : new WeightSource(model_dir));
+        const WeightSource &src = *srcp;
+        if (packed()) {
+            // The artifact's profile must be the requested one (load_quantized_kev).
+            const GgufFile &g = *src.gguf();
+            const char *profile = dtype == HK_DTYPE_Q8_0 ? "kev-projections-q8_0-fp32-v1" : "kev-projections-q4_0-fp32-v1";
+            auto q = g.strings().find("huncho.quantization");
+            if (q == g.strings().end() || q->second != profile)
+                throw ApiError(HK_ERR_PACKAGE, std::string("packed Kev artifact is not ") + profile);
+            auto cj = g.strings().find("huncho.config_json");
+            auto wj = g.strings().find("huncho.input_widths");
+            if (cj == g.strings().end() || wj == g.strings().end())
+                throw ApiError(HK_ERR_PACKAGE, "packed Kev artifact lacks its config or input widths");
+            cfg = KevConfig::from_json(json::parse(cj->second));
+            json::Value widths = json::parse(wj->second);
+            for (auto &kv : widths.obj) packed_widths[kv.first] = static_cast<int>(kv.second.num);
+        } else {
+            cfg = KevConfig::from_json(json::parse(read_file(model_dir + "/config.json")));
+        }
         const KevConfig &c = cfg;
         if (c.nv % c.nk != 0) throw ApiError(HK_ERR_UNSUPPORTED, "value heads must be a multiple of key heads");
         if (c.nh % c.nkv != 0) throw ApiError(HK_ERR_UNSUPPORTED, "query heads must be a multiple of kv heads");
-        WeightSource src(model_dir);
         lora_rank = src.lora_rank();
         // Pointer head (kev.rs:118-165): fp32, shapes [dp, hidden] and [dp].
         json::Value meta = json::parse(read_file(model_dir + "/kev_head.json"));
@@ -631,7 +745,7 @@ struct Model {
         {
             std::vector<float> e = src.get("model.language_model.embed_tokens.weight",
                                            {static_cast<int64_t>(c.vocab), c.hidden});
-            if (dtype == HK_DTYPE_FP32) {
+            if (f32_model()) {
                 float *d = dev_alloc<float>(e.size(), allocs);
                 HK_CUDA(cudaMemcpy(d, e.data(), e.size() * 4, cudaMemcpyHostToDevice));
                 embed = d;
@@ -652,7 +766,7 @@ struct Model {
                 inv[i] = std::pow(static_cast<float>(c.theta), -(2.0f * static_cast<float>(i)) / static_cast<float>(rd));
             inv_freq = upload_f32(inv);
         }
-        fused_swiglu = dtype != HK_DTYPE_FP32 && (c.ffn % kSwiGLUBlock) == 0;
+        fused_swiglu = !f32_model() && (c.ffn % kSwiGLUBlock) == 0;
         std::vector<int> gu_order;
         if (fused_swiglu) {
             for (int b = 0; b < c.ffn / kSwiGLUBlock; ++b) {
@@ -737,6 +851,10 @@ struct Model {
         hn = dev_alloc<float>(R * c.hidden, ws);
         rproj = dev_alloc<float>(R * dp, ws);
         logits = dev_alloc<float>(R, ws);
+        if (max_kp > 0) {
+            xq = dev_alloc<int8_t>(N * max_kp, ws);
+            xd = dev_alloc<float>(N * (max_kp / 32), ws);
+        }
         probs = dev_alloc<float>(R, ws);
         answers = dev_alloc<AnswerRec>(cap_rows, ws);
         qtype_dev = dev_alloc<int32_t>(cap_rows, ws);
@@ -759,10 +877,16 @@ struct Model {
         a.epilogue = epi;
         a.err = err;
         cudaEvent_t ev = prof_begin();
-        if (dtype == HK_DTYPE_FP32)
+        if (W.q) {
+            if (epi != kEpiStoreF32 && epi != kEpiResidual)
+                throw ApiError(HK_ERR_UNSUPPORTED, "packed projections store fp32 outputs only");
+            launch_quantize_rows(static_cast<const float *>(xin), ldx, M, W.cols, W.kp, xq, xd, stream);
+            gemm_q8(xq, xd, W.q, W.qd, M, W.rows, W.kp, static_cast<float *>(out), ldo, epi == kEpiResidual, stream);
+        } else if (f32_model()) {
             gemm_f32_simt(a, stream);
-        else
+        } else {
             gemm_f16_tc(a, stream, num_sms);
+        }
         prof_end(ev, 0, 2.0 * M * W.rows * W.cols);
     }
 
@@ -803,7 +927,7 @@ struct Model {
             launch_rmsnorm(A, x, c.hidden, L.in_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream);
             prof_end(ev, 4, 0);
             // Half-precision models: the warp-specialised delta layer kernel.
-            const bool pipe = !L.full && dtype != HK_DTYPE_FP32 && c.dk == 128 && c.dv == 128 && c.taps == 4 &&
+            const bool pipe = !L.full && !f32_model() && c.dk == 128 && c.dv == 128 && c.taps == 4 &&
                               c.nk > 0 && c.nv % c.nk == 0 && (ldp % 4) == 0 && (c.conv_dim() % 4) == 0;
             gemm(L.mix_in, xn, ld_xn, n_tok, proj, ldp, kEpiStoreF32);
             if (pipe) {
@@ -853,10 +977,10 @@ struct Model {
                 d.beta = db;
                 d.tok_row = tok_row;
                 d.hist_in = in_b;
-                d.fast = dtype != HK_DTYPE_FP32;
+                d.fast = !f32_model();
                 if (out_b)
                     launch_conv_history(proj, ldp, c.conv_dim(), c.taps, cu_seqlens, n_rows, in_b, out_b, stream);
-                if (dtype != HK_DTYPE_FP32 && c.dk == 128 && c.dv == 128 && c.taps == 4 && c.nv <= 32 &&
+                if (!f32_model() && c.dk == 128 && c.dv == 128 && c.taps == 4 && c.nv <= 32 &&
                     (ldp % 4) == 0) {
                     // The chunked recurrence with the input stage and the gated norm fused.
                     DeltaRecArgs r;
@@ -906,7 +1030,7 @@ struct Model {
                     r.dk = c.dk;
                     r.dv = c.dv;
                     r.out = dout;
-                    r.exact = dtype == HK_DTYPE_FP32;
+                    r.exact = f32_model();
                     r.state_in = in_a;
                     r.state_out = out_a;
                     ev = prof_begin();
@@ -1125,7 +1249,8 @@ int guarded(hk_model *h, F &&f) {
 
 int create_impl(const std::string &dir, int device, int dtype, int max_context, hk_model **out) {
     *out = nullptr;
-    if (dtype != HK_DTYPE_FP32 && dtype != HK_DTYPE_BF16 && dtype != HK_DTYPE_INT8W && dtype != HK_DTYPE_FP16) {
+    if (dtype != HK_DTYPE_FP32 && dtype != HK_DTYPE_BF16 && dtype != HK_DTYPE_INT8W && dtype != HK_DTYPE_FP16 &&
+        dtype != HK_DTYPE_Q8_0 && dtype != HK_DTYPE_Q4_0) {
         tl_create_error = "unsupported dtype";
         return HK_ERR_UNSUPPORTED;
     }

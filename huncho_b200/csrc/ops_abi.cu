@@ -65,6 +65,17 @@ int hk_op_gemm(int dtype, int epilogue, int M, int N, int K, const void *x, int 
     });
 }
 
+int hk_op_gemm_packed(int M, int N, int K, int kp, const float *x, int ldx, const int8_t *w_q, const float *w_d,
+                      int8_t *x_q, float *x_d, float *out, int ldo, int residual, void *stream) {
+    return op_guard([&] {
+        if (M < 0 || N < 0 || K < 0 || kp <= 0 || kp % 32 != 0 || K > kp || ldx < K || ldo < N)
+            throw std::runtime_error("hk_op_gemm_packed: bad shape");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        hk::launch_quantize_rows(x, ldx, M, K, kp, x_q, x_d, s);
+        hk::gemm_q8(x_q, x_d, w_q, w_d, M, N, kp, out, ldo, residual != 0, s);
+    });
+}
+
 int hk_op_delta_recurrent(const float *q, const float *k, const float *v, const float *g, const float *beta,
                           const int32_t *cu_seqlens, int n_rows, int nk, int nv, int dk, int dv, int exact,
                           float *out, void *stream) {

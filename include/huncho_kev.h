@@ -44,12 +44,25 @@ extern "C" {
  *                   (scale = max|w| / 127, fp32 scales, applied in the GEMM
  *                   epilogue); other tensors as HK_DTYPE_BF16.
  *   HK_DTYPE_FP16   fp16 weights and tensor-core operands.
+ *   HK_DTYPE_Q8_0 / HK_DTYPE_Q4_0
+ *                   the reference's packed profiles "q8_0-fp32" / "q4_0-fp32"
+ *                   (Qwen3_5Backend::load_quantized_kev, crates/huncho-backend/
+ *                   src/qwen_quantized.rs:395-...): model_dir holds
+ *                   backbone.gguf (the converter's artifact, qwen_quantized.rs:
+ *                   91-193: merged backbone, projections in GGML Q8_0 / Q4_0
+ *                   blocks of 32, everything else fp32) plus the pointer head
+ *                   files. Projections quantize their fp32 inputs to Q8_0 and
+ *                   sum per-block integer dots (int8 tensor cores); all other
+ *                   math is the fp32 model's. An artifact of the other scheme
+ *                   -> HK_ERR_PACKAGE.
  * In the half-precision models the residual stream, projection outputs and
  * all elementwise math stay fp32; only tensor-core operands are fp16. */
 #define HK_DTYPE_FP32 0
 #define HK_DTYPE_BF16 1
 #define HK_DTYPE_INT8W 2
 #define HK_DTYPE_FP16 3
+#define HK_DTYPE_Q8_0 4
+#define HK_DTYPE_Q4_0 5
 
 /* The reference's hard limit on independent rows per native batch
  * (qwen3_5.rs:3143-3148; BatchLimits default, backend.rs:108-121). */

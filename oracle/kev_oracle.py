@@ -270,6 +270,97 @@ class KevModel:
     meta: dict = field(default_factory=dict)
 
 
+# ---------------------------------------------------------------------------
+# Packed (GGML Q8_0 / Q4_0) projections of the reference's quantized profile
+# (qwen_quantized.rs; Projection::Packed, qwen3_5.rs:320-369)
+# ---------------------------------------------------------------------------
+
+@dataclass
+class PackedWeight:
+    """One packed projection: int8 block values q [N, nb, 32] (Q4_0 as q - 8),
+    fp32 block scales d [N, nb] (the stored fp16 values), logical input width."""
+    q: np.ndarray
+    d: np.ndarray
+    width: int
+
+
+def q8_0_rows(x):
+    """Q8_0 quantization of fp32 rows [M, K] (K % 32 == 0): per block
+    d = max|x| / 127, q = roundf(x * (1/d)), d stored as fp16. Returns
+    (q int8 [M, nb, 32], d fp32 [M, nb])."""
+    x = np.asarray(x, F32)
+    m, k = x.shape
+    b = x.reshape(m, k // 32, 32)
+    amax = np.max(np.abs(b), axis=2).astype(F32)
+    d = (amax / F32(127.0)).astype(F32)
+    inv = np.zeros_like(d)
+    nz = d != 0
+    inv[nz] = (F32(1.0) / d[nz]).astype(F32)
+    v = (b * inv[:, :, None]).astype(F32).astype(np.float64)
+    q = (np.sign(v) * np.floor(np.abs(v) + 0.5)).clip(-128, 127).astype(np.int8)
+    return q, d.astype(np.float16).astype(F32)
+
+
+def packed_linear(x, pw: PackedWeight):
+    """candle's CPU QMatMul (the generic vec_dot): the input rows are padded
+    with zeros to the packed width and quantized to Q8_0; per output, over the
+    blocks in order, sumf += (float(sum_i q_w q_x) * d_w) * d_x in fp32."""
+    x = np.asarray(x, F32)
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    nb = pw.q.shape[1]
+    if x2.shape[1] != pw.width:
+        raise ValueError("packed projection input width mismatch")
+    xp = np.zeros((x2.shape[0], nb * 32), F32)
+    xp[:, :pw.width] = x2
+    qx, dx = q8_0_rows(xp)
+    acc = np.zeros((x2.shape[0], pw.q.shape[0]), F32)
+    qw = pw.q.astype(np.int32)
+    for b in range(nb):
+        sumi = qx[:, b, :].astype(np.int32) @ qw[:, b, :].T
+        term = ((sumi.astype(F32) * pw.d[None, :, b]).astype(F32) * dx[:, b:b + 1]).astype(F32)
+        acc = (acc + term).astype(F32)
+    return acc.reshape(*lead, pw.q.shape[0])
+
+
+def load_packed_model(model_dir, dtype: str) -> KevModel:
+    """A packed package (backbone.gguf + pointer head files): dense tensors
+    fp32, projections packed; the reference's load_quantized_kev profile
+    (fp32 activations, qwen_quantized.rs:395-...)."""
+    from huncho_b200 import gguf  # the container format (a file-format contract)
+    d = Path(model_dir)
+    meta, tensors = gguf.read(d / "backbone.gguf")
+    want = {"q8_0-fp32": ("kev-projections-q8_0-fp32-v1", gguf.TYPE_Q8_0),
+            "q4_0-fp32": ("kev-projections-q4_0-fp32-v1", gguf.TYPE_Q4_0)}
+    if dtype not in want or meta.get("huncho.quantization") != want[dtype][0]:
+        raise ValueError(f"artifact profile {meta.get('huncho.quantization')} does not match {dtype}")
+    cfg = Config.from_value(json.loads(meta["huncho.config_json"]))
+    widths = json.loads(meta["huncho.input_widths"])
+    w = {}
+    for name, (t, shape, raw) in tensors.items():
+        if t == gguf.TYPE_F32:
+            w[name] = np.frombuffer(raw, "<f4").astype(F32).reshape(shape)
+            continue
+        if t != want[dtype][1]:
+            raise ValueError(f"{name}: block type {t} in a {dtype} artifact")
+        rows, kp = shape
+        nb = kp // 32
+        per = 34 if t == gguf.TYPE_Q8_0 else 18
+        rec = np.frombuffer(raw, np.uint8).reshape(rows, nb, per)
+        scale = rec[:, :, :2].copy().view("<f2").reshape(rows, nb).astype(F32)
+        if t == gguf.TYPE_Q8_0:
+            q = rec[:, :, 2:].copy().view(np.int8)
+        else:
+            nib = rec[:, :, 2:]
+            q = np.concatenate([(nib & 0x0F).astype(np.int16) - 8, (nib >> 4).astype(np.int16) - 8],
+                               axis=2).astype(np.int8)
+        w[name] = PackedWeight(q=q, d=scale, width=int(widths[name]))
+    meta_h = json.loads((d / "kev_head.json").read_text())
+    head = {k: v.astype(F32) for k, v in read_safetensors(d / "pointer_head.safetensors").items()}
+    return KevModel(cfg=cfg, w=w, head=head, temperature=float(F32(meta_h.get("temperature", 1.0))),
+                    head_dim=int(meta_h.get("head_dim", 256)), dtype=dtype, meta=meta_h)
+
+
 def load_model(model_dir, dtype: str = "fp32") -> KevModel:
     """Load base weights, merge LoRA in fp32, then apply the model dtype.
 
@@ -283,6 +374,8 @@ def load_model(model_dir, dtype: str = "fp32") -> KevModel:
     fp32 (kev.rs:124-165).
     """
     d = Path(model_dir)
+    if dtype in ("q8_0-fp32", "q4_0-fp32"):
+        return load_packed_model(d, dtype)
     cfg = Config.from_value(json.loads((d / "config.json").read_text()))
     w = {}
     for p in sorted(d.glob("*.safetensors")):
@@ -395,6 +488,8 @@ def apply_partial_rotary(x, cos, sin, rd):
 
 
 def linear(x, w):
+    if isinstance(w, PackedWeight):
+        return packed_linear(x, w)
     return (x.astype(F32) @ w.T.astype(F32)).astype(F32)
 
 
