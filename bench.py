@@ -255,6 +255,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=None,
                     help="requests per GPU (default: the config's); smaller cases are for profiling")
+    ap.add_argument("--packed", choices=["q8_0-fp32", "q4_0-fp32"], default=None,
+                    help="run the workload on the reference's packed profile: the synthetic model converted "
+                         "(fp32 weights, projections in GGML Q8_0 / Q4_0 blocks, fp32 activations)")
     ap.add_argument("--prefix-cache", action="store_true",
                     help="score each request's questions as branches of its cached shared prefix (the reference "
                          "engine's prefix_cache option: prefill + fork); default: independent rows")
@@ -282,13 +285,20 @@ def main():
 
     name, store = ("kev-0.8b", "bf16")
     dtype = {1: "fp32", 2: "bf16", 3: "int8w", 4: "bf16"}.get(args.config, "bf16")
-    if args.config == 1:
+    if args.config == 1 or args.packed:
         store = "fp32"
     if args.config == 5:
         name = "kev-4b"
     d = model_dir_for(name, store, args.seed)
     if rank == 0:
         synth.write_model(d, name, args.seed, store)
+    if args.packed:
+        from huncho_b200 import quantize
+        dtype = args.packed
+        pd = Path(str(d) + "-" + args.packed)
+        if rank == 0 and not (pd / "backbone.gguf").exists():
+            quantize.write_package(d, args.packed, pd)
+        d = pd
     barrier()
     wl = synth.make_workload(args.config, synth.SPECS[name]["vocab_size"], seed=args.seed + rank,
                              n_requests=args.requests)
@@ -450,7 +460,7 @@ def main():
     line = {
         "metric": "scored requests/s", "value": value, "unit": "requests/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dev_total_s / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if dtype != "fp32" else "f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": {"fp32": "f32", "q8_0-fp32": "q8_0 x f32", "q4_0-fp32": "q4_0 x f32"}.get(dtype, "bf16"),
         "data": "synthetic",
         "prompt_tokens_per_s": toks_all * args.steps / dev_total_s,
         "p50_request_latency_ms": statistics.median(step_ms),
@@ -475,7 +485,9 @@ def main():
                              "hk_score_answers (H2D inputs and question types, forward, on-device calibration and "
                              "answer fields, D2H probabilities and answers) + answer dicts")},
         "gpu_launches": int(launches),
-        "roofline": {"kernel": "gemm_f16_tc (tcgen05 projections)", "bound": "tensor", "achieved": achieved,
+        "roofline": {"kernel": ("gemm_q8 (int8 mma.sync packed projections; int8 ops against the bf16 peak, no "
+                                "measured int8 peak)" if args.packed else "gemm_f16_tc (tcgen05 projections)"),
+                     "bound": "tensor", "achieved": achieved,
                      "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                      "frac": (achieved / pk["bf16_tflops_sustained"]) if achieved else None,
                      "traffic": traffic, "peak_source": pk["source"] + " (sustained: kernels timed inside a step)",
