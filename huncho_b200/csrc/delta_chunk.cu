@@ -60,12 +60,6 @@ struct Smem {
     float sq[C][D], sk[C][D], sv[C][D];
     float sz[C][D];  // z rows of the chunk whose gated output is pending
     float sg[C], sb[C];
-    // RAW input: the staging above holds pre-conv projection rows [C][q|k|v]
-    // of this head; the conv history (last 3 rows, double-buffered by chunk
-    // parity), the head's conv weights and the raw b / a projections.
-    float hist[2][3][3 * D];
-    float cw[3][4][D];  // [tensor][tap][channel]
-    float sbr[C], sar[C];
 };
 
 struct ChunkArgs {
@@ -84,14 +78,10 @@ struct ChunkArgs {
     int ldmix;
     // Per-row addresses of the initial / final state [nv][128][128] fp32, or 0.
     const uint64_t *state_in, *state_out;
-    // RAW: the input stage fused in (conv + SiLU, l2norm, gates from proj).
-    const float *conv_w, *base_g, *dt_bias;  // [conv_dim][4], [nv], [nv]
-    const uint64_t *hist_in;                 // per row: prefix conv history [3][conv_dim] fp32, or 0
-    int key_dim, value_dim, conv_dim;
 };
 
 
-template <bool GATED_OUT, bool RAW>
+template <bool GATED_OUT>
 __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
@@ -128,29 +118,6 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
                 cp4(&sm.sb[r], a.beta + t * a.nv + h, ok);
         }
     };
-    // RAW: this head's pre-conv q | k | v projection columns.
-    const int ch_q = kh * D, ch_k = a.key_dim + kh * D, ch_v = 2 * a.key_dim + h * D;
-    auto prefetch_raw = [&](int c0) {
-        const int nn = min(C, end - c0);
-        float *sraw = &sm.sq[0][0];  // [C][3D] over the q|k|v staging
-        for (int i = tid; i < C * (3 * D / 4); i += THREADS) {
-            const int r = i / (3 * D / 4), w = i % (3 * D / 4), which = w / (D / 4), c = (w % (D / 4)) * 4;
-            const bool ok = r < nn;
-            const size_t t = static_cast<size_t>(c0 + (ok ? r : 0));
-            const int ch = which == 0 ? ch_q : which == 1 ? ch_k : ch_v;
-            cp16(sraw + r * 3 * D + which * D + c, a.proj + t * a.ldp + ch + c, ok);
-        }
-        if (tid < 2 * C) {
-            const int r = tid % C;
-            const bool ok = r < nn;
-            const size_t t = static_cast<size_t>(c0 + (ok ? r : 0));
-            const float *pb = a.proj + t * a.ldp + a.conv_dim + a.value_dim;
-            if (tid < C)
-                cp4(&sm.sbr[r], pb + h, ok);
-            else
-                cp4(&sm.sar[r], pb + a.nv + h, ok);
-        }
-    };
     auto prefetch_z = [&](int c0) {
         if (!GATED_OUT) return;
         const int nn = min(C, end - c0);
@@ -185,31 +152,10 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
         for (int nt = 0; nt < 16; ++nt) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0.f;
         for (int i = tid; i < D * LDH; i += THREADS) (&sm.S[0][0])[i] = __float2half_rn(0.f);
     }
-    if (RAW) {
-        for (int i = tid; i < 3 * D; i += THREADS) {
-            const int which = i / D, c = i % D;
-            const float4 w4 = *reinterpret_cast<const float4 *>(
-                a.conv_w + static_cast<size_t>((which == 0 ? ch_q : which == 1 ? ch_k : ch_v) + c) * 4);
-            sm.cw[which][0][c] = w4.x;
-            sm.cw[which][1][c] = w4.y;
-            sm.cw[which][2][c] = w4.z;
-            sm.cw[which][3][c] = w4.w;
-        }
-        // The conv history entering the row: its cached prefix's last inputs, or zero.
-        const float *hist = reinterpret_cast<const float *>(a.hist_in ? a.hist_in[row] : 0);
-        for (int i = tid; i < 3 * 3 * D; i += THREADS) {
-            const int j = i / (3 * D), rem = i % (3 * D), which = rem / D, c = rem % D;
-            const int ch = (which == 0 ? ch_q : which == 1 ? ch_k : ch_v) + c;
-            sm.hist[0][j][rem] = hist ? hist[static_cast<size_t>(j) * a.conv_dim + ch] : 0.f;
-        }
-        prefetch_raw(start);
-    } else {
-        prefetch_qkv(start);
-    }
+    prefetch_qkv(start);
     prefetch_z(start);
     cp_commit();
 
-    const float bg_h = RAW ? a.base_g[h] : 0.f, dt_h = RAW ? a.dt_bias[h] : 0.f;
     // This thread's gated-norm weights (columns nb + 8 nt + 2 t4 + {0, 1}).
     const int nb = warp * 16;
     float nwr[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
@@ -227,15 +173,8 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
         // ---- P0: gates. Every warp scans g in registers (lane = row; padding
         // rows carry g = 0, beta = 0); warp 0 also publishes G, gam, beta for the
         // later phases, which read them after the next barrier.
-        float gv, bv;
-        if (RAW) {  // beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias)
-            const bool ok = lane < n;
-            bv = ok ? sigmoid_f(sm.sbr[lane]) : 0.f;
-            gv = ok ? bg_h * logf(expf(sm.sar[lane] + dt_h) + 1.0f) : 0.f;
-        } else {
-            gv = sm.sg[lane];
-            bv = sm.sb[lane];
-        }
+        float gv = sm.sg[lane];
+        const float bv = sm.sb[lane];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const float up = __shfl_up_sync(0xffffffffu, gv, o);
@@ -247,99 +186,24 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
             sm.gam[lane] = gamv;
             sm.beta[lane] = bv;
         }
-        // ---- P0b: operands from the staging buffers.
-        const int hcur = ((c0 - start) / C) & 1;
-        if (RAW) {
-            // Warp w takes rows 4w .. 4w+3: causal conv over [history ; chunk]
-            // (taps in ascending order) sliding over rows 4w-3 .. 4w+3, SiLU, then
-            // per row the l2norm of q (scaled by 1/sqrt(128)) and k across the warp.
-            const float *sraw = &sm.sq[0][0];  // [C][3D]
-            const int r0 = 4 * warp;
+        // ---- P0b: operands from the staging buffers; warp w fills rows w, w+8, ...
 #pragma unroll
-            for (int which = 0; which < 3; ++which) {
-                float4 w4[4], x4[7];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) w4[j] = *reinterpret_cast<const float4 *>(&sm.cw[which][j][4 * lane]);
-#pragma unroll
-                for (int i = 0; i < 7; ++i) {
-                    const int idx = r0 - 3 + i;
-                    x4[i] = idx >= 0 ? *reinterpret_cast<const float4 *>(sraw + idx * 3 * D + which * D + 4 * lane)
-                                     : *reinterpret_cast<const float4 *>(&sm.hist[hcur][3 + idx][which * D + 4 * lane]);
-                }
-                float y[4][4], ss[4];
-#pragma unroll
-                for (int rr = 0; rr < 4; ++rr) {
-                    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float4 x = x4[rr + j], w = w4[j];
-                        acc[0] = fmaf(w.x, x.x, acc[0]);
-                        acc[1] = fmaf(w.y, x.y, acc[1]);
-                        acc[2] = fmaf(w.z, x.z, acc[2]);
-                        acc[3] = fmaf(w.w, x.w, acc[3]);
-                    }
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) y[rr][c] = silu_fast(acc[c]);
-                    ss[rr] = y[rr][0] * y[rr][0] + y[rr][1] * y[rr][1] + y[rr][2] * y[rr][2] + y[rr][3] * y[rr][3];
-                }
-                if (which < 2) {  // the four rows' sums of squares in one butterfly
-#pragma unroll
-                    for (int o = 16; o >= 1; o >>= 1)
-#pragma unroll
-                        for (int rr = 0; rr < 4; ++rr) ss[rr] += __shfl_xor_sync(0xffffffffu, ss[rr], o);
-                }
-#pragma unroll
-                for (int rr = 0; rr < 4; ++rr) {
-                    const int r = r0 + rr;
-                    const float b = __shfl_sync(0xffffffffu, bv, r);
-                    if (which == 2) {
-                        const float bvv[4] = {b * y[rr][0], b * y[rr][1], b * y[rr][2], b * y[rr][3]};
-                        split_store4(&sm.Vh[r][4 * lane], &sm.Vl[r][4 * lane], bvv);
-                    } else {
-                        const float inv = which == 0 ? rsqrtf(ss[rr] + 1e-6f) * rsqrtf(static_cast<float>(D))
-                                                     : rsqrtf(ss[rr] + 1e-6f);
-                        const float nv4[4] = {y[rr][0] * inv, y[rr][1] * inv, y[rr][2] * inv, y[rr][3] * inv};
-                        if (which == 0) {
-                            split_store4(&sm.Qh[r][4 * lane], &sm.Ql[r][4 * lane], nv4);
-                        } else {
-                            split_store4(&sm.Kh[r][4 * lane], &sm.Kl[r][4 * lane], nv4);
-                            const float bg = b * __shfl_sync(0xffffffffu, gamv, r);
-                            const float bkk[4] = {bg * nv4[0], bg * nv4[1], bg * nv4[2], bg * nv4[3]};
-                            store4(&sm.BK[r][4 * lane], bkk);
-                        }
-                    }
-                }
-                if (warp == WARPS - 1) {  // rows C-3 .. C-1: the next chunk's history
-#pragma unroll
-                    for (int i = 0; i < 3; ++i)
-                        *reinterpret_cast<float4 *>(&sm.hist[hcur ^ 1][i][which * D + 4 * lane]) = x4[4 + i];
-                }
-            }
-        } else {
-            // Warp w fills rows w, w+8, ...
-#pragma unroll
-            for (int r = warp; r < C; r += WARPS) {
-                const float4 q4 = *reinterpret_cast<const float4 *>(&sm.sq[r][4 * lane]);
-                const float4 k4 = *reinterpret_cast<const float4 *>(&sm.sk[r][4 * lane]);
-                const float4 v4 = *reinterpret_cast<const float4 *>(&sm.sv[r][4 * lane]);
-                const float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
-                const float b = __shfl_sync(0xffffffffu, bv, r), bg = b * __shfl_sync(0xffffffffu, gamv, r);
-                const float bvv[4] = {b * v4.x, b * v4.y, b * v4.z, b * v4.w};
-                const float bkk[4] = {bg * kv[0], bg * kv[1], bg * kv[2], bg * kv[3]};
-                split_store4(&sm.Qh[r][4 * lane], &sm.Ql[r][4 * lane], qv);
-                split_store4(&sm.Kh[r][4 * lane], &sm.Kl[r][4 * lane], kv);
-                split_store4(&sm.Vh[r][4 * lane], &sm.Vl[r][4 * lane], bvv);
-                store4(&sm.BK[r][4 * lane], bkk);
-            }
+        for (int r = warp; r < C; r += WARPS) {
+            const float4 q4 = *reinterpret_cast<const float4 *>(&sm.sq[r][4 * lane]);
+            const float4 k4 = *reinterpret_cast<const float4 *>(&sm.sk[r][4 * lane]);
+            const float4 v4 = *reinterpret_cast<const float4 *>(&sm.sv[r][4 * lane]);
+            const float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
+            const float b = __shfl_sync(0xffffffffu, bv, r), bg = b * __shfl_sync(0xffffffffu, gamv, r);
+            const float bvv[4] = {b * v4.x, b * v4.y, b * v4.z, b * v4.w};
+            const float bkk[4] = {bg * kv[0], bg * kv[1], bg * kv[2], bg * kv[3]};
+            split_store4(&sm.Qh[r][4 * lane], &sm.Ql[r][4 * lane], qv);
+            split_store4(&sm.Kh[r][4 * lane], &sm.Kl[r][4 * lane], kv);
+            split_store4(&sm.Vh[r][4 * lane], &sm.Vl[r][4 * lane], bvv);
+            store4(&sm.BK[r][4 * lane], bkk);
         }
         __syncthreads();
         // The staging buffers are free again: fetch the next chunk's inputs.
-        if (c0 + C < end) {
-            if (RAW)
-                prefetch_raw(c0 + C);
-            else
-                prefetch_qkv(c0 + C);
-        }
+        if (c0 + C < end) prefetch_qkv(c0 + C);
         cp_commit();
         // ---- P1: K K^T (warps 0-3) and Q K^T (warps 4-7); 16 rows x 16 cols per warp.
         {
@@ -612,19 +476,19 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
     }
 }
 
-template <bool GO, bool RAW>
+template <bool GO>
 void launch_kernel(const ChunkArgs &a, cudaStream_t s) {
     const size_t smem = sizeof(Smem);
     static bool set[64] = {};
     int dev = 0;
     HK_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64 || !set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(delta_chunk_kernel<GO, RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        HK_CUDA(cudaFuncSetAttribute(delta_chunk_kernel<GO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
         if (dev >= 0 && dev < 64) set[dev] = true;
     }
     dim3 grid(a.n_rows, a.nv);
-    delta_chunk_kernel<GO, RAW><<<grid, THREADS, smem, s>>>(a);
+    delta_chunk_kernel<GO><<<grid, THREADS, smem, s>>>(a);
     HK_LAUNCH_CHECK();
 }
 
@@ -648,7 +512,7 @@ void launch_delta_chunk(const DeltaRecArgs &r, cudaStream_t s) {
     a.out = r.out;
     a.state_in = r.state_in;
     a.state_out = r.state_out;
-    launch_kernel<false, false>(a, s);
+    launch_kernel<false>(a, s);
 }
 
 void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp, int zoff, const float *norm_w,
@@ -674,35 +538,8 @@ void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp,
     a.ldmix = ldmix;
     a.state_in = r.state_in;
     a.state_out = r.state_out;
-    launch_kernel<true, false>(a, s);
+    launch_kernel<true>(a, s);
 }
 
-void launch_delta_chunk_fused(const DeltaRecArgs &r, const DeltaFusedInput &in, const float *norm_w, float eps,
-                              __half *mix, int ldmix, cudaStream_t s) {
-    if (r.n_rows <= 0) return;
-    ChunkArgs a{};
-    a.cu_seqlens = r.cu_seqlens;
-    a.row_order = r.row_order;
-    a.n_rows = r.n_rows;
-    a.nk = r.nk;
-    a.nv = r.nv;
-    a.proj = in.proj;
-    a.ldp = in.ldp;
-    a.zoff = in.conv_dim;
-    a.conv_w = in.conv_w;
-    a.base_g = in.base_g;
-    a.dt_bias = in.dt_bias;
-    a.hist_in = in.hist_in;
-    a.key_dim = r.nk * D;
-    a.value_dim = r.nv * D;
-    a.conv_dim = in.conv_dim;
-    a.norm_w = norm_w;
-    a.eps = eps;
-    a.mix = mix;
-    a.ldmix = ldmix;
-    a.state_in = r.state_in;
-    a.state_out = r.state_out;
-    launch_kernel<true, true>(a, s);
-}
 
 }  // namespace hk

@@ -980,67 +980,33 @@ struct Model {
                 d.fast = !f32_model();
                 if (out_b)
                     launch_conv_history(proj, ldp, c.conv_dim(), c.taps, cu_seqlens, n_rows, in_b, out_b, stream);
-                if (!f32_model() && c.dk == 128 && c.dv == 128 && c.taps == 4 && c.nv <= 32 &&
-                    (ldp % 4) == 0) {
-                    // The chunked recurrence with the input stage and the gated norm fused.
-                    DeltaRecArgs r;
-                    r.q = dq;
-                    r.k = dkk;
-                    r.v = dvv;
-                    r.g = dg;
-                    r.beta = db;
-                    r.cu_seqlens = cu_seqlens;
-                    r.row_order = row_order;
-                    r.n_rows = n_rows;
-                    r.nk = c.nk;
-                    r.nv = c.nv;
-                    r.dk = c.dk;
-                    r.dv = c.dv;
-                    r.out = dout;
-                    r.exact = 0;
-                    r.state_in = in_a;
-                    r.state_out = out_a;
-                    r.err = err;
-                    DeltaFusedInput in;
-                    in.proj = proj;
-                    in.ldp = ldp;
-                    in.conv_dim = c.conv_dim();
-                    in.conv_w = L.conv_w;
-                    in.base_g = L.base_g;
-                    in.dt_bias = L.dt_bias;
-                    in.hist_in = in_b;
-                    ev = prof_begin();
-                    launch_delta_chunk_fused(r, in, L.gnorm_w, c.eps, static_cast<__half *>(mix), ldmix, stream);
-                    prof_end(ev, 1, delta_chunk_flops(n_tok, c));
-                } else {
-                    ev = prof_begin();
-                    launch_delta_prep(d, stream);
-                    prof_end(ev, 3, 0);
-                    DeltaRecArgs r;
-                    r.q = dq;
-                    r.k = dkk;
-                    r.v = dvv;
-                    r.g = dg;
-                    r.beta = db;
-                    r.cu_seqlens = cu_seqlens;
-                    r.row_order = row_order;
-                    r.n_rows = n_rows;
-                    r.nk = c.nk;
-                    r.nv = c.nv;
-                    r.dk = c.dk;
-                    r.dv = c.dv;
-                    r.out = dout;
-                    r.exact = f32_model();
-                    r.state_in = in_a;
-                    r.state_out = out_a;
-                    ev = prof_begin();
-                    launch_delta_recurrent(r, stream);
-                    prof_end(ev, 1, 4.0 * n_tok * c.nv * c.dk * c.dv);
-                    ev = prof_begin();
-                    launch_gated_norm(A, dout, proj + c.conv_dim(), ldp, L.gnorm_w, c.eps, n_tok, c.nv, c.dv, mix, ldmix,
-                                      stream);
-                    prof_end(ev, 4, 0);
-                }
+                ev = prof_begin();
+                launch_delta_prep(d, stream);
+                prof_end(ev, 3, 0);
+                DeltaRecArgs r;
+                r.q = dq;
+                r.k = dkk;
+                r.v = dvv;
+                r.g = dg;
+                r.beta = db;
+                r.cu_seqlens = cu_seqlens;
+                r.row_order = row_order;
+                r.n_rows = n_rows;
+                r.nk = c.nk;
+                r.nv = c.nv;
+                r.dk = c.dk;
+                r.dv = c.dv;
+                r.out = dout;
+                r.exact = f32_model();
+                r.state_in = in_a;
+                r.state_out = out_a;
+                ev = prof_begin();
+                launch_delta_recurrent(r, stream);
+                prof_end(ev, 1, 4.0 * n_tok * c.nv * c.dk * c.dv);
+                ev = prof_begin();
+                launch_gated_norm(A, dout, proj + c.conv_dim(), ldp, L.gnorm_w, c.eps, n_tok, c.nv, c.dv, mix, ldmix,
+                                  stream);
+                prof_end(ev, 4, 0);
             } else {
                 AttnPrepArgs p;
                 p.proj = proj;

@@ -88,18 +88,15 @@ void launch_delta_chunk(const DeltaRecArgs &a, cudaStream_t s);
 // beta pre-computed.
 void launch_delta_chunk_gated(const DeltaRecArgs &r, const float *proj, int ldp, int zoff, const float *norm_w,
                               float eps, __half *mix, int ldmix, cudaStream_t s);
-// The same with the input stage fused in (half-precision models, 128-wide
-// heads, 4 taps): the kernel reads this head's pre-conv q | k | v columns and
-// the b / a projections from proj and does the conv + SiLU, the l2norm and the
-// gates itself; r.q/k/v/g/beta are unused. hist_in as in DeltaPrepArgs.
+// The delta layer's input stage inputs for the fused kernel below: the fp32
+// in-projection rows (ldp per row: qkv | z | b | a), conv weights, gates'
+// parameters and each row's prefix conv history (as in DeltaPrepArgs).
 struct DeltaFusedInput {
     const float *proj = nullptr;
     int ldp = 0, conv_dim = 0;
     const float *conv_w = nullptr, *base_g = nullptr, *dt_bias = nullptr;
     const uint64_t *hist_in = nullptr;
 };
-void launch_delta_chunk_fused(const DeltaRecArgs &r, const DeltaFusedInput &in, const float *norm_w, float eps,
-                              __half *mix, int ldmix, cudaStream_t s);
 // The warp-specialised form of the fused delta layer (4 warps prepare chunk
 // j+1's state-independent operands while 8 warps run chunk j's state-dependent
 // products); 128-wide heads, 4 taps.
