@@ -449,6 +449,96 @@ __global__ void attn_prep_kernel(AttnPrepArgs a) {
     }
 }
 
+// The same input stage with one warp per token: each lane holds 4 consecutive
+// dims of every head (float4 loads, 8- or 16-byte stores), the token's rotary
+// cos/sin are computed once for all heads, and the rotate-half partner dims
+// come from another lane by shuffle. Per element the arithmetic is that of
+// attn_prep_kernel. HD = 128 or 256; rd a multiple of 8 and <= 128.
+template <typename T, int HD>
+__global__ void attn_prep_vec_kernel(AttnPrepArgs a) {
+    constexpr int NCH = HD / 128;  // float4 chunks per lane and head
+    const long t_l = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (t_l >= a.n) return;
+    const int t = static_cast<int>(t_l);
+    const float *proj = a.proj + static_cast<size_t>(t) * a.ldp;
+    const int row = a.tok_row[t];
+    const int kvs = kv_slot(a.pages, row, t - a.pos[t], a.pos[t]);
+    const float pos = static_cast<float>(a.pos[t] + (a.pre_len ? a.pre_len[row] : 0));
+    const int half = a.rd / 2, qh = half / 4;  // lanes per rotary half
+    const bool rot_lane = lane < a.rd / 4;
+    const int partner = lane < qh ? lane + qh : lane - qh;
+    float cs[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+    if (rot_lane) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = 4 * lane + j, fi = i < half ? i : i - half;
+            sincosf(pos * a.inv_freq[fi], &sn[j], &cs[j]);
+        }
+    }
+    auto ld4 = [](const float *p) { return *reinterpret_cast<const float4 *>(p); };
+    auto st4 = [](T *dst, const float (&v)[4]) {
+        if constexpr (sizeof(T) == 4) {
+            *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+            const __half2 a2 = __floats2half2_rn(v[0], v[1]), b2 = __floats2half2_rn(v[2], v[3]);
+            *reinterpret_cast<uint2 *>(dst) =
+                make_uint2(*reinterpret_cast<const uint32_t *>(&a2), *reinterpret_cast<const uint32_t *>(&b2));
+        }
+    };
+    float4 wq[NCH], wk[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        wq[c] = ld4(a.qn_w + 128 * c + 4 * lane);
+        wk[c] = ld4(a.kn_w + 128 * c + 4 * lane);
+    }
+    auto norm_rope = [&](const float *src, const float4 (&w)[NCH], T *dst) {
+        float x[NCH][4];
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+            const float4 v = ld4(src + 128 * c + 4 * lane);
+            x[c][0] = v.x, x[c][1] = v.y, x[c][2] = v.z, x[c][3] = v.w;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ss += x[c][j] * x[c][j];
+        }
+        ss = warp_sum(ss);
+        const float denom = sqrtf(ss / static_cast<float>(HD) + a.eps);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+            const float wv[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) x[c][j] = (x[c][j] / denom) * wv[j];
+        }
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = __shfl_sync(0xffffffffu, x[0][j], partner);
+        if (rot_lane) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float rot = lane < qh ? -o[j] : o[j];
+                x[0][j] = x[0][j] * cs[j] + rot * sn[j];
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) st4(dst + 128 * c + 4 * lane, x[c]);
+    };
+    for (int h = 0; h < a.nh; ++h)
+        norm_rope(proj + h * 2 * HD, wq, static_cast<T *>(a.q) + (static_cast<size_t>(t) * a.nh + h) * HD);
+    const float *kp = proj + a.nh * 2 * HD, *vp = kp + a.nkv * HD;
+    for (int h = 0; h < a.nkv; ++h)
+        norm_rope(kp + h * HD, wk, static_cast<T *>(a.k) + (static_cast<size_t>(kvs) * a.nkv + h) * HD);
+    for (int h = 0; h < a.nkv; ++h) {
+        T *dst = static_cast<T *>(a.v) + (static_cast<size_t>(kvs) * a.nkv + h) * HD;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+            const float4 v = ld4(vp + h * HD + 128 * c + 4 * lane);
+            const float vv[4] = {v.x, v.y, v.z, v.w};
+            st4(dst + 128 * c + 4 * lane, vv);
+        }
+    }
+}
+
 // ------------------------------------------------------------------ attention (SIMT)
 // One warp per (query token, query head), online softmax over the keys of
 // its row up to itself; used for the fp32 model and for head sizes the
@@ -744,6 +834,22 @@ void launch_gated_norm(int act, const float *o, const float *z, int ldz, const f
 
 void launch_attn_prep(int act, const AttnPrepArgs &a, cudaStream_t s) {
     if (a.n <= 0) return;
+    if ((a.hd == 128 || a.hd == 256) && a.rd % 8 == 0 && a.rd >= 8 && a.rd <= 128 && a.ldp % 4 == 0) {
+        const int grid = ceil_div(static_cast<long>(a.n), 8);
+        if (act == kActF32) {
+            if (a.hd == 256)
+                attn_prep_vec_kernel<float, 256><<<grid, 256, 0, s>>>(a);
+            else
+                attn_prep_vec_kernel<float, 128><<<grid, 256, 0, s>>>(a);
+        } else {
+            if (a.hd == 256)
+                attn_prep_vec_kernel<__half, 256><<<grid, 256, 0, s>>>(a);
+            else
+                attn_prep_vec_kernel<__half, 128><<<grid, 256, 0, s>>>(a);
+        }
+        HK_LAUNCH_CHECK();
+        return;
+    }
     const int slots = a.nh + 2 * a.nkv;
     const int grid = ceil_div(static_cast<long>(a.n) * slots, 8);
     const size_t smem = sizeof(float) * 8 * a.hd;
