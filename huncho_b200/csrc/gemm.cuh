@@ -34,6 +34,9 @@ struct GemmArgs {
 
 // fp16 X and W on tcgen05 tensor cores (TMA-fed, TMEM accumulators), fp32 accumulation.
 void gemm_f16_tc(const GemmArgs &a, cudaStream_t s, int num_sms);
+// The same on CTA pairs (clusters of two CTAs sharing one cta_group::2 MMA on
+// 256 x 256 tiles; half the operand loads per MMA work of gemm_f16_tc).
+void gemm_f16_tc_pair(const GemmArgs &a, cudaStream_t s, int num_sms);
 // fp32 X and W on CUDA cores (the fp32 model path).
 void gemm_f32_simt(const GemmArgs &a, cudaStream_t s);
 

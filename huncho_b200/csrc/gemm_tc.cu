@@ -19,7 +19,9 @@
 //               them with TMA bulk-tensor stores -- or TMA reduce-add into the
 //               fp32 residual stream -- so global writes are full lines.
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
-// No cluster multicast is used; every CTA loads its own tiles.
+// No cluster multicast is used; every CTA loads its own tiles. A CTA-pair form
+// of the same kernel (cta_group::2, 256 x 256 tiles; see gemm_f16_tc2_kernel)
+// runs the launches whose MMAs wait on operand loads.
 #include <cuda.h>
 
 #include <cstring>
@@ -355,6 +357,330 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+
+// The same GEMM on CTA pairs (cta_group::2): a cluster of two CTAs computes a
+// 256 x 256 tile with one MMA stream issued by the first CTA. Each CTA loads
+// 128 rows of X and 128 rows of W (its half of the tile's N) per 64-wide K
+// block, so every shared-memory byte feeds twice the MMA work of the single-CTA
+// kernel and six 32 KB stages fit. Both CTAs' loads complete on the first
+// CTA's `full` barrier; the first CTA's commits arrive on both CTAs' `empty`
+// and `tfull` barriers; the epilogue warps of both CTAs release an
+// accumulator on the first CTA's `tempty`. Each CTA's TMEM holds its 128 rows
+// of the tile, drained by its own epilogue as in the single-CTA kernel.
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = BM * BK * 2;  // 16 KB: this CTA's 128 rows of X
+constexpr int P_B_BYTES = BM * BK * 2;  // 16 KB: this CTA's 128 rows of W
+constexpr int P_SMEM_BYTES = P_STAGES * (P_A_BYTES + P_B_BYTES) + EPI_BYTES + 1024 + 256;
+static_assert(P_SMEM_BYTES <= 232448, "shared memory of one CTA");
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_f16_tc2_kernel(const __grid_constant__ CUtensorMap tm_x,
+                         const __grid_constant__ CUtensorMap tm_w,
+                         const __grid_constant__ CUtensorMap tm_o, TcParams p) {
+    using namespace sm100;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + P_STAGES * P_A_BYTES;
+    uint8_t *sE = sB + P_STAGES * P_B_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sE + EPI_BYTES);
+    uint64_t *empty = full + P_STAGES;
+    uint64_t *tfull = empty + P_STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+    const int num_tiles = p.m_tiles * p.n_tiles;  // m_tiles counts 256-row tiles here
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 8);  // one arrival per epilogue warp of both CTAs
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_w);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_holder, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();  // both CTAs' barriers initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer (both CTAs)
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued = 0;
+            for (int tile = pair; tile < num_tiles && !*abort_flag; tile += n_pairs) {
+                const int m_blk = p.n_fast ? tile / p.n_tiles : tile % p.m_tiles;
+                const int n_blk = p.n_fast ? tile % p.n_tiles : tile / p.m_tiles;
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait_cluster(&empty[stage], phase ^ 1)) {
+                        set_error(p.err, kErrWaitTimeout);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    const uint32_t bar0 = mapa_shared(smem_addr(&full[stage]), 0);
+                    if (rank == 0) mbar_expect_tx(&full[stage], 2 * (P_A_BYTES + P_B_BYTES));
+                    tma_load_2d_pair(sA + stage * P_A_BYTES, &tm_x, bar0, kb * BK,
+                                     m_blk * (2 * BM) + static_cast<int>(rank) * BM);
+                    tma_load_2d_pair(sB + stage * P_B_BYTES, &tm_w, bar0, kb * BK,
+                                     n_blk * BN + static_cast<int>(rank) * BM);
+                    ++issued;
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // Wait until the MMAs released every stage this CTA filled (their
+            // completions arrive on this CTA's `empty` barriers), so no arrival
+            // is still on its way when the CTA exits.
+            for (int i = 0; i < P_STAGES && issued > 0 && !*abort_flag; ++i) {
+                if (!mbar_wait_cluster(&empty[stage], phase ^ 1)) {
+                    set_error(p.err, kErrWaitTimeout);
+                    break;
+                }
+                if (++stage == P_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            // ------------------------------------------------ MMA issuer (first CTA)
+            constexpr uint32_t idesc = idesc_f16_f32(2 * BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            const uint32_t peer = 1;
+            for (int tile = pair; tile < num_tiles && !*abort_flag; tile += n_pairs) {
+                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1)) {
+                    set_error(p.err, kErrWaitTimeout);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait_cluster(&full[stage], phase)) {
+                        set_error(p.err, kErrWaitTimeout);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_addr(sA + stage * P_A_BYTES);
+                    const uint32_t b0 = smem_addr(sB + stage * P_B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        mma_f16_pair(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32), idesc,
+                                     (kb | k) != 0);
+                    mma_commit_pair(smem_addr(&empty[stage]));
+                    mma_commit_pair(mapa_shared(smem_addr(&empty[stage]), peer));
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (*abort_flag) {
+                    mma_commit_pair(smem_addr(drain));
+                    (void)mbar_wait(drain, 0);
+                    break;
+                }
+                mma_commit_pair(smem_addr(&tfull[acc]));
+                mma_commit_pair(mapa_shared(smem_addr(&tfull[acc]), peer));
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1;
+            }
+        }
+    } else {
+        // ---------------------------------------------------- epilogue
+        const int quarter = warp & 3;  // TMEM lanes this warp may access
+        uint8_t *const slab0 = sE + (warp - 2) * 2 * EPI_BUF_BYTES;
+        int sb = 0;  // staging buffer to fill next
+        auto slab = [&]() { return slab0 + sb * EPI_BUF_BYTES; };
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        // Hand a filled slab to the TMA unit (lane 0), keeping at most one older
+        // store in flight on the other buffer.
+        auto issue = [&](int x, int y) {
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                if (EPI == kEpiResidual)
+                    tma_reduce_add_2d(&tm_o, slab(), x, y);
+                else
+                    tma_store_2d(&tm_o, slab(), x, y);
+                bulk_commit();
+            }
+            sb ^= 1;
+        };
+        auto reuse_wait = [&]() {
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+        };
+        for (int tile = pair; tile < num_tiles; tile += n_pairs) {
+            if (!mbar_wait_cluster(&tfull[acc], acc_phase)) {
+                set_error(p.err, kErrWaitTimeout);
+                *abort_flag = 1;
+                break;
+            }
+            if (*abort_flag) break;
+            tc_fence_after();
+            const int m_blk = p.n_fast ? tile / p.n_tiles : tile % p.m_tiles;
+            const int n_blk = p.n_fast ? tile % p.n_tiles : tile / p.m_tiles;
+            const int row0 = m_blk * (2 * BM) + static_cast<int>(rank) * BM + quarter * 32;
+            const int row = row0 + lane;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+            const bool row_ok = row < p.M;
+            const bool slab_ok = row0 < p.M;
+            if (EPI == kEpiSwiGLU) {
+                // Tile columns [0,128) are gate rows, [128,256) the matching up rows;
+                // each round produces 64 fp16 outputs per row.
+#pragma unroll 1
+                for (int c = 0; c < BN / 2; c += 64) {
+                    uint32_t packed[32];
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        float g[32], u[32];
+                        tmem_ld32(t_row + c + 32 * hh, g);
+                        tmem_ld32(t_row + BN / 2 + c + 32 * hh, u);
+                        const int wcol = n_blk * BN + c + 32 * hh;  // weight row of g[0]
+                        if (p.scale) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                g[i] *= __ldg(p.scale + wcol + i);
+                                u[i] *= __ldg(p.scale + wcol + BN / 2 + i);
+                            }
+                        }
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            __half2 h2 = __floats2half2_rn(silu_fast(g[2 * i]) * u[2 * i],
+                                                           silu_fast(g[2 * i + 1]) * u[2 * i + 1]);
+                            packed[16 * hh + i] = *reinterpret_cast<uint32_t *>(&h2);
+                        }
+                    }
+                    const int ocol = n_blk * (BN / 2) + c;
+                    if (p.tma_out) {
+                        if (!slab_ok || ocol >= p.N / 2) continue;
+                        reuse_wait();
+                        uint4 ch[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) ch[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                        stage_row(slab(), lane, ch);
+                        issue(ocol, row0);
+                    } else if (row_ok) {
+                        __half *dst = reinterpret_cast<__half *>(p.out) + static_cast<size_t>(row) * p.ldo + ocol;
+                        const __half *hv = reinterpret_cast<const __half *>(packed);
+                        for (int i = 0; i < 64 && ocol + i < p.N / 2; ++i) dst[i] = hv[i];
+                    }
+                }
+            } else if (EPI == kEpiStore) {
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 64) {
+                    const int col = n_blk * BN + c;
+                    uint32_t packed[32];
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        float v[32];
+                        tmem_ld32(t_row + c + 32 * hh, v);
+                        if (p.scale) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (col + 32 * hh + i < p.N) v[i] *= __ldg(p.scale + col + 32 * hh + i);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            __half2 h2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+                            packed[16 * hh + i] = *reinterpret_cast<uint32_t *>(&h2);
+                        }
+                    }
+                    if (p.tma_out) {
+                        if (!slab_ok || col >= p.N) continue;
+                        reuse_wait();
+                        uint4 ch[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) ch[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                        stage_row(slab(), lane, ch);
+                        issue(col, row0);
+                    } else if (row_ok) {
+                        __half *dst = reinterpret_cast<__half *>(p.out) + static_cast<size_t>(row) * p.ldo + col;
+                        const __half *hv = reinterpret_cast<const __half *>(packed);
+                        for (int i = 0; i < 64 && col + i < p.N; ++i) dst[i] = hv[i];
+                    }
+                }
+            } else {
+                // fp32 outputs: store, or add into the residual stream.
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    float v[32];
+                    tmem_ld32(t_row + c, v);
+                    const int col = n_blk * BN + c;
+                    const int valid = p.N - col;
+                    if (p.scale) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (i < valid) v[i] *= __ldg(p.scale + col + i);
+                    }
+                    if (p.tma_out) {
+                        if (!slab_ok || valid <= 0) continue;
+                        reuse_wait();
+                        uint4 ch[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            ch[i] = make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]),
+                                               __float_as_uint(v[4 * i + 2]), __float_as_uint(v[4 * i + 3]));
+                        stage_row(slab(), lane, ch);
+                        issue(col, row0);
+                    } else if (row_ok && valid > 0) {
+                        float *dst = reinterpret_cast<float *>(p.out) + static_cast<size_t>(row) * p.ldo + col;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (i < valid) dst[i] = (EPI == kEpiResidual) ? dst[i] + v[i] : v[i];
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&tempty[acc]), 0));
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+        }
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    cluster_sync_all();  // no arrival into either CTA is pending; both epilogues are done
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
@@ -448,10 +774,81 @@ void launch(const GemmArgs &a, cudaStream_t s, int num_sms) {
     HK_LAUNCH_CHECK();
 }
 
+template <int EPI>
+void launch_pair(const GemmArgs &a, cudaStream_t s, int num_sms) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    HK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        HK_CUDA(cudaFuncSetAttribute(gemm_f16_tc2_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     P_SMEM_BYTES));
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    CUtensorMap tx = make_map(a.x, a.M, a.K, a.ldx, BM);
+    CUtensorMap tw = make_map(a.w, a.N, a.K, a.ldw, BM);  // each CTA loads 128 rows of W
+    TcParams p;
+    p.M = a.M;
+    p.N = a.N;
+    p.K = a.K;
+    p.m_tiles = ceil_div(a.M, 2 * BM);
+    p.n_tiles = ceil_div(a.N, BN);
+    p.n_fast = p.n_tiles <= 8 ? 1 : 0;
+    p.k_blocks = ceil_div(a.K, BK);
+    p.out = a.out;
+    p.ldo = a.ldo;
+    p.scale = a.scale;
+    const int elem = (EPI == kEpiStore || EPI == kEpiSwiGLU) ? 2 : 4;
+    p.vec_ok = ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0) && ((a.ldo * elem) % 16 == 0);
+    p.err = a.err;
+    CUtensorMap to;
+    std::memset(&to, 0, sizeof(to));
+    const bool f32 = (EPI == kEpiResidual || EPI == kEpiStoreF32);
+    const int out_cols = (EPI == kEpiSwiGLU) ? a.N / 2 : a.N;
+    p.tma_out = make_out_map(to, a.out, a.M, out_cols, a.ldo, f32) ? 1 : 0;
+    const int tiles = p.m_tiles * p.n_tiles;
+    const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    HK_CUDA(cudaLaunchKernelEx(&cfg, gemm_f16_tc2_kernel<EPI>, tx, tw, to, p));
+    HK_LAUNCH_CHECK();
+}
+
 }  // namespace
+
+void gemm_f16_tc_pair(const GemmArgs &a, cudaStream_t s, int num_sms) {
+    if (a.M <= 0 || a.N <= 0 || a.K <= 0) return;
+    if (a.epilogue == kEpiSwiGLU && (a.N % BN) != 0)
+        throw CudaError("fused SwiGLU GEMM needs N to be a multiple of 256");
+    switch (a.epilogue) {
+        case kEpiStore: launch_pair<kEpiStore>(a, s, num_sms); break;
+        case kEpiResidual: launch_pair<kEpiResidual>(a, s, num_sms); break;
+        case kEpiSwiGLU: launch_pair<kEpiSwiGLU>(a, s, num_sms); break;
+        case kEpiStoreF32: launch_pair<kEpiStoreF32>(a, s, num_sms); break;
+        default: throw CudaError("unknown GEMM epilogue");
+    }
+}
 
 void gemm_f16_tc(const GemmArgs &a, cudaStream_t s, int num_sms) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return;
+    // CTA pairs where the single-CTA kernel waits on its operand loads: the
+    // fp32-store projections (the widest outputs) and long-K residual ones
+    // (measured on the cfg2 shapes: +7% and +1.5%; the SwiGLU and K = 2048
+    // residual launches gain nothing or lose, and stay on single CTAs).
+    if (a.M >= 512 && num_sms >= 2 &&
+        (a.epilogue == kEpiStoreF32 || (a.epilogue == kEpiResidual && a.K >= 3072))) {
+        gemm_f16_tc_pair(a, s, num_sms);
+        return;
+    }
     if (a.epilogue == kEpiSwiGLU && (a.N % BN) != 0)
         throw CudaError("fused SwiGLU GEMM needs N to be a multiple of 256");
     switch (a.epilogue) {

@@ -60,8 +60,10 @@ int hk_op_gemm(int dtype, int epilogue, int M, int N, int K, const void *x, int 
             hk::gemm_f32_simt(a, s);
         else if (dtype == 1)
             hk::gemm_f16_tc(a, s, current_sms());
+        else if (dtype == 2)
+            hk::gemm_f16_tc_pair(a, s, current_sms());
         else
-            throw std::runtime_error("hk_op_gemm: dtype must be 0 (fp32) or 1 (fp16)");
+            throw std::runtime_error("hk_op_gemm: dtype must be 0 (fp32), 1 (fp16) or 2 (fp16, CTA pairs)");
     });
 }
 

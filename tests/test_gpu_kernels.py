@@ -358,3 +358,23 @@ def test_delta_chunked_long_context_stress(lib):
     ref = _delta_oracle(q, k, v, g, b, cu, nk, nv)
     assert np.isfinite(got).all()
     assert np.abs(got - ref).max() <= 2e-3 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("epi,M,N,K", [(3, 300, 520, 200), (0, 300, 520, 200), (2, 300, 512, 200), (1, 300, 520, 200),
+                                       (3, 13, 8224, 1024), (1, 257, 1024, 3584), (2, 2048, 7168, 1024),
+                                       (1, 1000, 1024, 2048)])
+def test_tc_gemm_cta_pairs_equal_single_cta(lib, epi, M, N, K):
+    """The CTA-pair form (cta_group::2, 256 x 256 tiles; hk_op_gemm dtype 2)
+    against the single-CTA kernel (dtype 1, which keeps these shapes on single
+    CTAs): the same K-block order, so bit-identical outputs for every epilogue,
+    ragged M and N included."""
+    g = torch.Generator(device="cuda").manual_seed(M + N + K + epi)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
+    cols = N // 2 if epi == 2 else N
+    dt = torch.float16 if epi in (0, 2) else torch.float32
+    base = torch.randn(M, cols, device="cuda", generator=g).to(dt)
+    single, pair = base.clone(), base.clone()
+    gemm(lib, 1, epi, x, w, single)
+    gemm(lib, 2, epi, x, w, pair)
+    assert torch.equal(single, pair)
