@@ -24,3 +24,20 @@ class PackageError(HunchoError):
 class CalibrationError(HunchoError):
     """Error::Calibration."""
     kind = "calibration"
+
+
+class RequestError(HunchoError):
+    """Error::Request: the request itself is invalid (error.rs:16-17)."""
+    kind = "request"
+
+
+class UnavailableError(HunchoError):
+    """JobResult::Unavailable (huncho-api coalesce.rs:13-17): the batch queue
+    is full or closed, so the request was not admitted."""
+    kind = "unavailable"
+
+
+class WorkerFailedError(HunchoError):
+    """JobResult::WorkerFailed: the collation worker failed outside the
+    backend (the group's callers all receive it)."""
+    kind = "worker_failed"
