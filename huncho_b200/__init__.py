@@ -3,13 +3,15 @@
 The compute path is libhuncho_kev.so (CUDA kernels + the C ABI of
 include/huncho_kev.h); this package holds the host-side mirror of the
 reference's Backend trait (backend.py), its calibration and answer semantics
-(calibration.py, engine.py), the synthetic workload generator (synth.py) and
-the in-tree build (build.py).
+(calibration.py, engine.py), cross-request collation (collate.py), replica
+pools and sharding (replicas.py), the synthetic workload generator (synth.py)
+and the in-tree build (build.py).
 """
-from .errors import BackendError, CalibrationError, HunchoError, PackageError, UnsupportedError
+from .errors import (BackendError, CalibrationError, HunchoError, PackageError, RequestError, UnavailableError,
+                     UnsupportedError, WorkerFailedError)
 
-__all__ = ["BackendError", "CalibrationError", "HunchoError", "PackageError", "UnsupportedError",
-           "KevBackend", "ForwardInput", "ForwardOutput"]
+__all__ = ["BackendError", "CalibrationError", "HunchoError", "PackageError", "RequestError", "UnavailableError",
+           "UnsupportedError", "WorkerFailedError", "KevBackend", "ForwardInput", "ForwardOutput"]
 
 
 def __getattr__(name):
