@@ -5,16 +5,23 @@ Workload (default, config 2 of the benchmark definition): the Qwen3.5-0.8B-shape
 Kev scorer in bf16 (random-init weights from a fixed seed), 32 requests with
 lengths uniform in [64, 512]; each asks a 4-option choice, a noul and a 5-level
 score, so one step scores 96 independent rows (~27.6k prompt tokens) split into
-two native batches of 48 rows. Under torchrun every rank (one per GPU) scores
-its own 32 requests (weak scaling; replicas, no collective on the data path).
+two native batches of 48 rows. Each GPU holds `--replicas` (default 2) model
+handles that share the weights (hk_replica), each with its own workspace and
+CUDA stream; a step's native batches are dealt to them round-robin and run
+concurrently, so one batch's kernel tails and launch gaps overlap the other's
+work. Under torchrun every rank (one per GPU) scores its own 32 requests (weak
+scaling; replicas, no collective on the data path).
 
   value  device time of K steps with inputs resident in HBM (hk_score_device),
          L2 flushed between steps (256 MiB write, outside the timed events);
   e2e    the same K steps through the public host API (KevBackend.score_answers
          -> hk_score_answers: host->device copy of the inputs, forward,
          calibration and answer fields on the device, device->host read of the
-         probabilities and answers), plus the answer dicts, wall clock;
-both are the max over ranks. `--impl reference` times the CPU reference path
+         probabilities and answers; one host thread per replica), plus the
+         answer dicts, wall clock;
+both are the max over ranks. The kernel roofline comes from a serial pass of
+the same K steps (one handle, one stream) with per-launch CUDA events, since
+launches on concurrent streams overlap. `--impl reference` times the CPU reference path
 (the oracle restatement of the reference's CPU fp32 forward) on rank 0.
 """
 from __future__ import annotations
@@ -27,6 +34,7 @@ import subprocess
 import sys
 import threading
 import time
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 import numpy as np
@@ -258,6 +266,9 @@ def main():
     ap.add_argument("--packed", choices=["q8_0-fp32", "q4_0-fp32"], default=None,
                     help="run the workload on the reference's packed profile: the synthetic model converted "
                          "(fp32 weights, projections in GGML Q8_0 / Q4_0 blocks, fp32 activations)")
+    ap.add_argument("--replicas", type=int, default=2,
+                    help="model handles per GPU sharing the weights, each on its own stream; the step's native "
+                         "batches run on them concurrently (1 = one handle, batches in sequence)")
     ap.add_argument("--prefix-cache", action="store_true",
                     help="score each request's questions as branches of its cached shared prefix (the reference "
                          "engine's prefix_cache option: prefill + fork); default: independent rows")
@@ -308,6 +319,17 @@ def main():
         backend.with_kv_page_tokens(16, shuffle_seed=1 + rank)  # 16-token pages, shuffled block table
 
     groups = groups_of(wl.rows, backend.batch_limits().max_rows)
+    n_rep = max(1, min(args.replicas, len(wl.rows)))
+    if args.prefix_cache:
+        n_rep = 1  # the prefix-cache step is synchronous host code on one handle
+    if n_rep > len(groups):  # at least one native batch per replica
+        size = -(-len(wl.rows) // n_rep)
+        groups = [list(range(i, min(len(wl.rows), i + size))) for i in range(0, len(wl.rows), size)]
+    n_rep = min(n_rep, len(groups))
+    backends = [backend] + [backend.replica() for _ in range(n_rep - 1)]
+    if args.config == 4:
+        for k, b in enumerate(backends[1:]):
+            b.with_kv_page_tokens(16, shuffle_seed=2 + k + rank)
     packed = []
     for g in groups:
         tok, cu, pos, cup = pack_rows([wl.rows[i] for i in g], [wl.positions[i] for i in g])
@@ -321,10 +343,30 @@ def main():
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
 
-    def device_step():
+    rep_streams = [torch.cuda.Stream() for _ in range(n_rep)]
+
+    def serial_step():
         for g, tok, cu, pos, cup, dev in packed:
             backend.score_device(cu, cup, dev["tok"].data_ptr(), dev["cu"].data_ptr(), dev["pos"].data_ptr(),
                                  dev["out"].data_ptr(), stream.cuda_stream)
+
+    def device_step():
+        if n_rep == 1:
+            serial_step()
+            return
+        # Fork the replica streams off the timing stream and join them back.
+        go = torch.cuda.Event()
+        go.record(stream)
+        for rs in rep_streams:
+            rs.wait_event(go)
+        for j, (g, tok, cu, pos, cup, dev) in enumerate(packed):
+            backends[j % n_rep].score_device(cu, cup, dev["tok"].data_ptr(), dev["cu"].data_ptr(),
+                                             dev["pos"].data_ptr(), dev["out"].data_ptr(),
+                                             rep_streams[j % n_rep].cuda_stream)
+        for rs in rep_streams:
+            done = torch.cuda.Event()
+            done.record(rs)
+            stream.wait_event(done)
 
     # Prefix-cache mode: per request, the longest common prefix of its rows
     # that leaves every readout in the suffix is prefilled once; each question
@@ -375,8 +417,8 @@ def main():
     # ---- timed region: device-resident inputs
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    launches0 = backend.kernel_launches
-    backend.profile(fork_plan is None)
+    launches0 = sum(b.kernel_launches for b in backends)
+    backend.profile(fork_plan is None and n_rep == 1)
     barrier()
     torch.cuda.synchronize()
     host_ms = []
@@ -396,9 +438,29 @@ def main():
     barrier()
     backend.profile(False)
     prof = backend.profile_read()
-    launches = backend.kernel_launches - launches0
+    launches = sum(b.kernel_launches for b in backends) - launches0
     step_ms = host_ms if fork_plan is not None else [s.elapsed_time(e) for s, e in zip(starts, ends)]
     dev_total_s = max_over_ranks(sum(step_ms) / 1000.0)
+
+    # ---- serial pass for the kernel roofline: the same steps on one handle and
+    # one stream, each launch bracketed by CUDA events (concurrent streams would
+    # make those intervals overlap).
+    serial_ms = None
+    if n_rep > 1:
+        s_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        s_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        serial_step()  # sizes the first handle's workspace for every batch
+        torch.cuda.synchronize()
+        backend.profile(True)
+        for k in range(args.steps):
+            flush.zero_()
+            s_starts[k].record(stream)
+            serial_step()
+            s_ends[k].record(stream)
+        torch.cuda.synchronize()
+        backend.profile(False)
+        prof = backend.profile_read()
+        serial_ms = [a.elapsed_time(b) for a, b in zip(s_starts, s_ends)]
 
     # ---- e2e: the public host API, host calibration and answers included
     # e2e per native batch: inputs + question types up; probabilities, answer
@@ -411,13 +473,24 @@ def main():
             a[0].nbytes + a[1].nbytes + a[2].nbytes + a[3].nbytes + 8 * len(g) for g, a in fork_plan[2])
         d2h = sum(4 * int(a[3][-1]) + 4 for _, a in fork_plan[2]) + 8 * len(fork_plan[0])
 
+    def e2e_batches(r):
+        # Replica r's native batches, one call each: forward + on-device
+        # calibration and answers (the call releases the GIL while it runs).
+        out = []
+        for j in range(r, len(packed), n_rep):
+            g, tok, cu, pos, cup, _ = packed[j]
+            probs, rec = backends[r].score_answers(tok, cu, pos, cup, [wl.qtypes[i] for i in g])
+            out.append((g, cup, probs, rec))
+        return out
+
+    pool = ThreadPoolExecutor(max_workers=n_rep) if n_rep > 1 else None
+
     def e2e_step():
         if fork_plan is not None:
             fork_step(True)
             return
-        for g, tok, cu, pos, cup, _ in packed:
-            # One call per native batch: forward + on-device calibration and answers.
-            probs, rec = backend.score_answers(tok, cu, pos, cup, [wl.qtypes[i] for i in g])
+        done = (list(pool.map(e2e_batches, range(n_rep))) if pool is not None else [e2e_batches(0)])
+        for g, cup, probs, rec in (x for part in done for x in part):
             for j, i in enumerate(g):
                 lo, hi = int(cup[j]), int(cup[j + 1])
                 q = engine.Question(wl.qtypes[i], labels=[str(x) for x in range(hi - lo)],
@@ -471,6 +544,7 @@ def main():
                       "branches" if fork_plan is not None else ""), "model": name,
                    "rows_per_step": len(wl.rows) * world,
                    "tokens_per_step": toks_all, "native_batches_per_step": len(groups),
+                   "replicas_per_gpu": n_rep,
                    "l2": "flushed between steps (256 MiB write, outside the timed events); weights 1 GB > L2",
                    "parallelism": f"replicas x{world}",
                    **({"timing": "host clock around the synchronous native calls (prefill, branch scoring, "
@@ -483,7 +557,8 @@ def main():
                 "includes": ("hk_score_cached branches (H2D inputs, forward, D2H logits) + host calibration and "
                              "answers" if fork_plan is not None else
                              "hk_score_answers (H2D inputs and question types, forward, on-device calibration and "
-                             "answer fields, D2H probabilities and answers) + answer dicts")},
+                             "answer fields, D2H probabilities and answers; one host thread per replica) + "
+                             "answer dicts")},
         "gpu_launches": int(launches),
         "roofline": {"kernel": ("gemm_q8 (int8 mma.sync packed projections; int8 ops against the bf16 peak, no "
                                 "measured int8 peak)" if args.packed else "gemm_f16_tc (tcgen05 projections)"),
@@ -491,7 +566,14 @@ def main():
                      "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                      "frac": (achieved / pk["bf16_tflops_sustained"]) if achieved else None,
                      "traffic": traffic, "peak_source": pk["source"] + " (sustained: kernels timed inside a step)",
-                     "launches": int(gemm_n)},
+                     "launches": int(gemm_n),
+                     "timed_over": ("a serial pass of the same steps after the timed region (one handle, one "
+                                    "stream; the timed region runs replicas on concurrent streams)"
+                                    if serial_ms else "the timed region")},
+        **({"serial_pass": {"ms_per_step": statistics.mean(serial_ms),
+                            "requests_per_s_this_gpu": wl.n_requests * len(serial_ms) / (sum(serial_ms) / 1000.0),
+                            "note": "the same steps with the native batches in sequence on one handle"}}
+           if serial_ms else {}),
         "time_shares": {k: round(v[0] / total_prof_ms, 4) for k, v in prof.items()} if total_prof_ms else {},
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -500,6 +582,10 @@ def main():
     line["clocks"] = clk.summary()
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if pool is not None:
+        pool.shutdown()
+    for b in backends[1:]:
+        b.close()
     backend.close()
     if world > 1:
         dist.destroy_process_group()
