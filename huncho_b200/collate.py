@@ -23,7 +23,7 @@ from __future__ import annotations
 import queue
 import threading
 import time
-from concurrent.futures import Future
+from concurrent.futures import Future, ThreadPoolExecutor, wait
 from dataclasses import dataclass, field
 from typing import Callable, List, Optional, Sequence
 
@@ -132,12 +132,18 @@ def packed_groups(inputs, budget: int, limits: Optional[BatchLimits] = None, pre
 def eval_batched(backend, rows: Sequence[Sequence[int]], positions: Sequence[Sequence[int]],
                  questions: Sequence[engine.Question], budget: int, *, percent: int = 0, packed: bool = True,
                  origins: Optional[Sequence[int]] = None, temperature: Optional[float] = None,
-                 stats: Optional[EvalStats] = None) -> list:
+                 stats: Optional[EvalStats] = None, replicas: Sequence = ()) -> list:
     """Answers of independent question rows run as budgeted native batches
     (engine.rs:1005-1140): rows are ordered by length (stable), grouped, and
     each group is one device call with on-device calibration; answers come
     back in input order. `origins[i]` names the request of row i, so batches
-    that mix requests are counted."""
+    that mix requests are counted.
+
+    `replicas` are further handles of the same model (`KevBackend.replica()`,
+    shared weights, own workspace and stream): the batches are dealt to
+    `backend` and them round-robin, and each handle's share runs on its own
+    host thread (the native call releases the GIL), so batches overlap on the
+    GPU. Any batch's failure fails the call, after every thread has ended."""
     if budget <= 0 or not 0 <= percent <= 100:
         raise RequestError("batch token budget must be positive and padding percent 0..100")
     if not (len(rows) == len(positions) == len(questions)):
@@ -153,6 +159,7 @@ def eval_batched(backend, rows: Sequence[Sequence[int]], positions: Sequence[Seq
     groups = (packed_groups(items, budget, limits) if packed
               else padded_groups(items, budget, percent, limits))
     answers: list = [None] * len(rows)
+    jobs = []
     for group in groups:
         idx = [i for i, _ in group]
         lengths = [len(rows[i]) for i in idx]
@@ -169,10 +176,31 @@ def eval_batched(backend, rows: Sequence[Sequence[int]], positions: Sequence[Seq
             stats.batch_calls += 1
             if origins is not None and any(origins[i] != origins[idx[0]] for i in idx):
                 stats.cross_request_batches += 1
-        rs, ps, qs = [rows[i] for i in idx], [positions[i] for i in idx], [questions[i] for i in idx]
-        probs, rec = backend.score_answers(*pack_rows(rs, ps), [q.type for q in qs], temperature=temperature)
-        if len(rec) != count:
-            raise HunchoError("batch backend returned the wrong number of sequences")
+        jobs.append((idx, [rows[i] for i in idx], [positions[i] for i in idx], [questions[i] for i in idx]))
+
+    handles = [backend, *replicas]
+    n_threads = min(len(handles), len(jobs))
+
+    def run(h):
+        out = []
+        for j in range(h, len(jobs), n_threads):
+            idx, rs, ps, qs = jobs[j]
+            probs, rec = handles[h].score_answers(*pack_rows(rs, ps), [q.type for q in qs],
+                                                  temperature=temperature)
+            if len(rec) != len(idx):
+                raise HunchoError("batch backend returned the wrong number of sequences")
+            out.append((j, probs, rec))
+        return out
+
+    if n_threads > 1:
+        with ThreadPoolExecutor(max_workers=n_threads) as pool:
+            futures = [pool.submit(run, h) for h in range(n_threads)]
+            wait(futures)
+        results = [x for f in futures for x in f.result()]
+    else:
+        results = run(0) if jobs else []
+    for j, probs, rec in results:
+        idx, _, ps, qs = jobs[j]
         k = 0
         for i, q, pos, r in zip(idx, qs, ps, rec):
             n = len(pos)
@@ -183,7 +211,7 @@ def eval_batched(backend, rows: Sequence[Sequence[int]], positions: Sequence[Seq
 
 def eval_collated(backend, requests: Sequence[ScoringRequest], budget: int, *, percent: int = 0,
                   packed: bool = True, temperature: Optional[float] = None,
-                  stats: Optional[EvalStats] = None) -> List[ScoringResponse]:
+                  stats: Optional[EvalStats] = None, replicas: Sequence = ()) -> List[ScoringResponse]:
     """Several requests' questions run as shared native batches, each request
     getting its own answers and usage back (engine.rs:554-706). The whole
     group is checked before any work; a failure of any batch fails the group."""
@@ -201,7 +229,7 @@ def eval_collated(backend, requests: Sequence[ScoringRequest], budget: int, *, p
         questions.extend(req.questions)
         origins.extend([k] * len(req.rows))
     answers = eval_batched(backend, rows, positions, questions, budget, percent=percent, packed=packed,
-                           origins=origins, temperature=temperature, stats=stats)
+                           origins=origins, temperature=temperature, stats=stats, replicas=replicas)
     out, s = [], 0
     for req in requests:
         n = len(req.rows)

@@ -339,3 +339,39 @@ def test_batch_queue_full_closed_and_pool_closed():
     q.close()
     with pytest.raises(RequestError):
         collate.BatchQueue(_pool(), capacity=0, max_requests=1, wait_ms=0, tokens=1)
+
+
+class BarrierBackend(FakeBackend):
+    """A fake whose first call waits for the other handles' first calls: it
+    only returns if the handles run concurrently."""
+
+    def __init__(self, barrier, **kw):
+        super().__init__(**kw)
+        self.barrier = barrier
+
+    def score_answers(self, *a, **kw):
+        if not self.calls:
+            self.barrier.wait(timeout=10)
+        return super().score_answers(*a, **kw)
+
+
+def test_eval_batched_over_replica_handles_runs_them_concurrently():
+    rng = np.random.default_rng(11)
+    reqs = [_request(rng, 4) for _ in range(6)]
+    barrier = threading.Barrier(3)
+    handles = [BarrierBackend(barrier) for _ in range(3)]
+    stats = collate.EvalStats()
+    got = collate.eval_collated(handles[0], reqs, 300, replicas=handles[1:], stats=stats)
+    assert stats.forward_calls >= 3 and all(len(h.calls) >= 1 for h in handles)
+    assert sum(len(h.calls) for h in handles) == stats.forward_calls
+    one = collate.eval_collated(FakeBackend(), reqs, 300)
+    for a, b in zip(got, one):
+        assert a.prompt_tokens == b.prompt_tokens
+        for x, y in zip(a.answers, b.answers):
+            _same_answers(x, y)
+    # a failing handle fails the call after the others finish
+    poisoned = collate.ScoringRequest([[5, 999_999, 5]], [[0, 1]], [engine.Question("noul")])
+    bad = [FakeBackend(fail_token=999_999) for _ in range(2)]
+    with pytest.raises(BackendError):
+        collate.eval_collated(bad[0], reqs + [poisoned], 300, replicas=bad[1:])
+    assert all(h.calls for h in bad)
