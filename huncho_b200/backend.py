@@ -125,7 +125,8 @@ class KevBackend:
         )
 
     def replica(self, device: Optional[int] = None) -> "KevBackend":
-        """The same immutable weights (on `device`, default the same GPU), fresh state."""
+        """The same model (on `device`, default the same GPU) with fresh state;
+        the package is loaded again, so the replica holds its own weight copy."""
         h = ctypes.c_void_p()
         dev = self.device if device is None else device
         rc = self._lib.hk_replica(self._h, dev, ctypes.byref(h))

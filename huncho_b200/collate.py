@@ -139,8 +139,8 @@ def eval_batched(backend, rows: Sequence[Sequence[int]], positions: Sequence[Seq
     back in input order. `origins[i]` names the request of row i, so batches
     that mix requests are counted.
 
-    `replicas` are further handles of the same model (`KevBackend.replica()`,
-    shared weights, own workspace and stream): the batches are dealt to
+    `replicas` are further handles of the same model (`KevBackend.replica()`:
+    the package loaded again, own weights, workspace and stream): the batches are dealt to
     `backend` and them round-robin, and each handle's share runs on its own
     host thread (the native call releases the GIL), so batches overlap on the
     GPU. Any batch's failure fails the call, after every thread has ended."""

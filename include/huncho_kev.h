@@ -93,8 +93,10 @@ typedef struct hk_capabilities {
  */
 int hk_create(const char *model_dir, int device, int dtype, int max_context, hk_model **out);
 
-/* The same immutable weights on another GPU, with fresh mutable state.
- * Replaces Backend::replica (backend.rs:217-222; qwen3_5.rs:2515-2535). */
+/* The same model on `device` (another GPU or the source's own), with fresh
+ * mutable state: the package is loaded again, so the new handle holds its own
+ * copy of the (identical) weights. Replaces Backend::replica
+ * (backend.rs:217-222; qwen3_5.rs:2515-2535). */
 int hk_replica(const hk_model *src, int device, hk_model **out);
 
 /* Replaces Backend::capabilities (qwen3_5.rs:2541-2653). */
