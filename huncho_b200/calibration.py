@@ -3,10 +3,14 @@
 Temperature softmax keeps the reference's mixed precision exactly: the
 exponential of (l - max) * (1/T) is fp32, the sum and the division run in fp64
 in input order, and each probability is rounded back to fp32
-(calibration.rs:43-64).
+(calibration.rs:43-64). The fp32 exponential is the C library's `expf`, the
+function Rust's `f32::exp` calls on Linux; numpy's own float32 `exp` differs
+from it in the last bit for a large share of inputs.
 """
 from __future__ import annotations
 
+import ctypes
+import ctypes.util
 import math
 
 import numpy as np
@@ -14,6 +18,16 @@ import numpy as np
 from .errors import CalibrationError
 
 F32 = np.float32
+
+_libm = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+_expf = _libm.expf
+_expf.restype = ctypes.c_float
+_expf.argtypes = [ctypes.c_float]
+
+
+def expf(x) -> np.ndarray:
+    """Elementwise C-library fp32 exponential of a float32 array."""
+    return np.array([_expf(v) for v in np.asarray(x, dtype=F32).ravel().tolist()], dtype=F32)
 
 
 def bucket_size(n_options: int) -> str:
@@ -34,7 +48,8 @@ def softmax_temperature(logits, temperature) -> np.ndarray:
         return l.copy()
     inv_t = F32(1.0) / F32(temperature)
     mx = F32(np.max(l))
-    e = np.exp(((l - mx) * inv_t).astype(F32)).astype(F32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        e = expf(((l - mx) * inv_t).astype(F32))
     s = 0.0
     for v in e.tolist():
         s += v

@@ -680,14 +680,22 @@ def score_row(m: KevModel, tokens, positions) -> np.ndarray:
 # Calibration and answers (huncho-core calibration.rs, engine.rs)
 # ---------------------------------------------------------------------------
 
+_libm = ctypes.CDLL("libm.so.6")
+_libm.expf.restype = ctypes.c_float
+_libm.expf.argtypes = [ctypes.c_float]
+
+
 def softmax_temperature(logits, temperature) -> np.ndarray:
-    """calibration.rs:43-64: fp32 exp of (l - max) * (1/T); fp64 sum and divide; fp32 result."""
+    """calibration.rs:43-64: fp32 exp of (l - max) * (1/T); fp64 sum and divide; fp32 result.
+    The fp32 exp is the C library's expf, which Rust's f32::exp calls on Linux."""
     l = np.asarray(logits, dtype=F32)
     if l.size == 0:
         return l.copy()
     inv_t = F32(1.0) / F32(temperature)
     mx = F32(np.max(l))
-    e = np.exp(((l - mx) * inv_t).astype(F32)).astype(F32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        z = ((l - mx) * inv_t).astype(F32)
+    e = np.array([_libm.expf(v) for v in z.tolist()], dtype=F32)
     s = 0.0
     for v in e:
         s += float(v)
