@@ -108,3 +108,14 @@ def test_small_cases_and_host_exponential():
     exact = np.exp(xs.astype(np.float64))
     assert np.all(np.abs(host.astype(np.float64) - exact) <= 0.51 * np.spacing(host).astype(np.float64))
     assert math.isclose(float(calibration.expf(np.array([0.0], F32))[0]), 1.0)
+
+
+def test_confidence_known_answers():
+    """The reference's confidence values (calibration.rs:447-461)."""
+    for probs, want, tol in (([0.61, 0.35, 0.04], 0.42, 0.01), ([0.0, 0.57, 0.43], 0.35, 0.01),
+                             ([0.0, 0.89, 0.11], 0.84, 0.01), ([0.84, 0.10, 0.06], 0.76, 0.01),
+                             ([1.0, 0.0], 1.0, 1e-6), ([0.5, 0.5], 0.0, 1e-6)):
+        assert abs(calibration.confidence_peak(probs) - want) < tol
+    assert abs(calibration.confidence_entropy([1.0, 0.0]) - 1.0) < 1e-6
+    assert abs(calibration.confidence_entropy([0.5, 0.5]) - 0.0) < 1e-6
+    assert calibration.argmax([0.2, 0.4, 0.4]) == 1  # first maximum
