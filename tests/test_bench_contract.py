@@ -35,3 +35,19 @@ def test_reference_arm_other_ranks_exit_quietly():
     r = _run({"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"}, "--steps", "1", "--warmup", "0", "--gpus", "2")
     assert r.returncode == 0, r.stderr[-2000:]
     assert not [x for x in r.stdout.splitlines() if x.startswith("{")]
+
+
+def test_cpu_baseline_reports_rate_tokens_and_p50(synth_root):
+    """The CPU leg of the GPU arm (oracle on a bounded sample) on a small model:
+    requests/s, tokens/s and a p50 request latency over whole requests."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from huncho_b200 import synth
+    d = synth.write_model(synth_root / "kev-mini-bf16", name="kev-mini", seed=0, store="bf16")
+    wl = synth.make_workload(2, synth.SPECS["kev-mini"]["vocab_size"], seed=2, n_requests=3)
+    order = [i for r in range(wl.n_requests) for i in range(len(wl.rows)) if wl.request_of[i] == r]
+    cb = bench.cpu_baseline(d, "bf16", wl, order, max_seconds=60.0)
+    assert cb["value"] > 0 and cb["tokens_per_s"] > 0 and cb["kind"] == "port" and cb["cores"] >= 1
+    assert cb["p50_request_latency_ms"] > 0 and "3 requests" in cb["sample"]
+    cp = bench.cpu_baseline(d, "bf16", wl, order, max_seconds=60.0, prefix_cache=True)
+    assert cp["value"] > 0 and cp["p50_request_latency_ms"] > 0
