@@ -309,15 +309,16 @@ def test_batch_queue_failure_fails_only_its_group():
 
 def test_batch_queue_full_closed_and_pool_closed():
     rng = np.random.default_rng(7)
-    gate = threading.Event()
+    gate, started = threading.Event(), threading.Event()
 
     def slow(backend, requests, budget):
+        started.set()
         gate.wait(10)
         return [collate.ScoringResponse([], 0) for _ in requests]
 
     q = collate.BatchQueue(_pool(), capacity=1, max_requests=1, wait_ms=0, tokens=100, evaluate=slow)
     first = q.submit(_request(rng, 1))
-    time.sleep(0.1)  # the worker holds the first request
+    assert started.wait(10)  # the worker holds the first request
     second = q.submit(_request(rng, 1))  # fills the queue
     third = q.submit(_request(rng, 1))
     with pytest.raises(UnavailableError):
@@ -333,7 +334,8 @@ def test_batch_queue_full_closed_and_pool_closed():
     q = collate.BatchQueue(pool, capacity=4, max_requests=2, wait_ms=10, tokens=100)
     with pytest.raises(WorkerFailedError):
         q.submit(_request(rng, 1)).result(timeout=10)
-    time.sleep(0.05)
+    q._worker.join(10)
+    assert not q._worker.is_alive()
     with pytest.raises(UnavailableError):  # the worker stopped: nothing is admitted any more
         q.submit(_request(rng, 1)).result(timeout=1)
     q.close()
