@@ -32,7 +32,6 @@ import os
 import statistics
 import subprocess
 import sys
-import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path

@@ -6,7 +6,6 @@ the same choices and probabilities within the batch-invariance gate of
 padded_batch.rs:25-83 (1e-4), through `eval_collated` directly and through
 the `BatchQueue` worker thread (batch.rs:85-193) over a two-replica pool.
 """
-import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
