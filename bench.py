@@ -9,8 +9,11 @@ two native batches of 48 rows. Each GPU holds `--replicas` (default 2) model
 handles (hk_replica: the same package loaded again, so each handle has its own
 copy of the weights, workspace and CUDA stream); a step's native batches are dealt to them round-robin and run
 concurrently, so one batch's kernel tails and launch gaps overlap the other's
-work. Under torchrun every rank (one per GPU) scores its own 32 requests (weak
-scaling; replicas, no collective on the data path).
+work. Under torchrun one request pool is generated from one seed (32 requests
+per GPU for configs 1-4: weak scaling; config 5's fixed 4096 requests: strong
+scaling) and split over the ranks by `replicas.shard_by_tokens`, the batcher's
+token-balanced plan; each rank (one per GPU) scores its share (replicas, no
+collective on the data path).
 
   value  device time of K steps with inputs resident in HBM (hk_score_device),
          L2 flushed between steps (256 MiB write, outside the timed events);
@@ -143,15 +146,102 @@ def request_plan(wl):
     return plan
 
 
+# Kernel (class) names of the half-precision models' forward, by profile class.
+KERNEL_NAMES = {
+    "gemm": "gemm_f16_tc_kernel + gemm_f16_tc2_kernel (tcgen05 projections)",
+    "delta": "delta_pipe_kernel (fused delta layer: conv, gates, chunked rule, gated norm)",
+    "attention": "attn_t5_kernel (tcgen05 causal GQA attention)",
+    "delta_prep": "delta_prep_vec_kernel (fp32 model's delta input stage)",
+    "other": "swiglu / gated_norm / conv_history kernels",
+    "rmsnorm": "rmsnorm_reg_kernel",
+    "attn_prep": "attn_prep_vec_kernel (q/k norm, partial RoPE, K/V store)",
+    "readout": "readout_norm / readout_proj / pointer_logits kernels",
+    "embed": "embed_kernel",
+}
+TENSOR_CLASSES = ("gemm", "delta", "attention")
+
+
+def kernel_rooflines(prof, pk, dtype):
+    """One entry per kernel class that launched: launches, average CUDA-event
+    time per launch, algorithmic FLOPs and HBM bytes per launch, achieved
+    TFLOP/s and GB/s, and the fractions of the measured peaks (sustained bf16
+    tensor peak; HBM copy bandwidth). `bound` names the roofline that limits
+    the kernel's design."""
+    out = []
+    total_ms = sum(v[0] for v in prof.values()) or 1.0
+    for cls, (ms, fl, by, n) in prof.items():
+        if not n or ms <= 0:
+            continue
+        sec = ms / 1e3
+        e = {"kernel": KERNEL_NAMES.get(cls, cls), "class": cls, "launches": int(n), "avg_ms": ms / n,
+             "share": round(ms / total_ms, 4),
+             "bound": "tensor" if cls in TENSOR_CLASSES and dtype not in ("fp32",) else "hbm"}
+        if fl:
+            e["flops_per_launch"] = fl / n
+            e["achieved_tflops"] = fl / sec / 1e12
+            e["frac_tensor"] = e["achieved_tflops"] / pk["bf16_tflops_sustained"]
+        if by:
+            e["bytes_per_launch"] = by / n
+            e["achieved_gbs"] = by / sec / 1e9
+            e["frac_hbm"] = e["achieved_gbs"] / pk["hbm_gbs"]
+        out.append(e)
+    return out
+
+
+def latency_summary(step_ms):
+    """Mean and nearest-rank p50 / p95 / p99 of the step times (every request
+    of a step completes when its step ends); the shape of the reference's
+    bench report (crates/huncho-cli/src/bench.rs:290-315)."""
+    xs = sorted(step_ms)
+
+    def pct(p):
+        return xs[min(len(xs) - 1, max(0, int(np.ceil(p / 100.0 * len(xs))) - 1))]
+
+    return {"mean": statistics.mean(xs), "p50": pct(50), "p95": pct(95), "p99": pct(99), "n": len(xs)}
+
+
+def subset_workload(pool, requests):
+    """The rows of `requests` (indices into the pool), renumbered 0.."""
+    keep = {r: k for k, r in enumerate(requests)}
+    idx = [i for i, r in enumerate(pool.request_of) if r in keep]
+    return synth.Workload(name=pool.name, rows=[pool.rows[i] for i in idx],
+                          positions=[pool.positions[i] for i in idx], qtypes=[pool.qtypes[i] for i in idx],
+                          request_of=[keep[pool.request_of[i]] for i in idx], n_requests=len(requests))
+
+
 def model_dir_for(name, store, seed):
     return synth.default_dir(name, seed, store)
+
+
+def host_cores() -> int:
+    """Host cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def use_all_cores(cores: int):
+    """Let the CPU legs use every host core: the oracle's C recurrence threads
+    and NumPy's BLAS pool (torchrun exports OMP_NUM_THREADS=1, which would
+    otherwise leave BLAS on one thread). Returns the BLAS limiter (a context
+    manager)."""
+    from oracle import kev_oracle as ko
+    from threadpoolctl import threadpool_limits
+    ko.set_threads(cores)
+    return threadpool_limits(limits=cores, user_api="blas")
 
 
 def cpu_baseline(model_dir, dtype, wl, rows_idx, max_seconds=30.0, prefix_cache=False):
     """The CPU oracle on a bounded sample of the workload (whole rows; with
     prefix_cache whole requests: prefix once, each question as a branch)."""
+    cores = host_cores()
+    with use_all_cores(cores):
+        return _cpu_baseline(model_dir, dtype, wl, rows_idx, max_seconds, prefix_cache, cores)
+
+
+def _cpu_baseline(model_dir, dtype, wl, rows_idx, max_seconds, prefix_cache, cores):
     from oracle import kev_oracle as ko
-    ko.set_threads(os.cpu_count() or 1)
     m = ko.load_model(model_dir, dtype)
     if prefix_cache:
         t0 = time.perf_counter()
@@ -167,7 +257,7 @@ def cpu_baseline(model_dir, dtype, wl, rows_idx, max_seconds=30.0, prefix_cache=
             if time.perf_counter() - t0 > max_seconds:
                 break
         dt = time.perf_counter() - t0
-        return {"value": done / dt, "unit": "requests/s", "cores": os.cpu_count(), "kind": "port",
+        return {"value": done / dt, "unit": "requests/s", "cores": cores, "kind": "port",
                 "tokens_per_s": toks / dt, "p50_request_latency_ms": 1000.0 * statistics.median(lat),
                 "sample": f"{done} whole requests ({toks} prompt tokens) of the workload, CPU fp32 oracle with "
                           f"prefix caches (prefix once, each question a branch) on the same weights, {dt:.1f} s"}
@@ -191,7 +281,7 @@ def cpu_baseline(model_dir, dtype, wl, rows_idx, max_seconds=30.0, prefix_cache=
             break
     dt = time.perf_counter() - t0
     rows_per_req = len(wl.rows) / wl.n_requests
-    return {"value": (done / rows_per_req) / dt, "unit": "requests/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": (done / rows_per_req) / dt, "unit": "requests/s", "cores": cores, "kind": "port",
             "tokens_per_s": toks / dt,
             "p50_request_latency_ms": 1000.0 * statistics.median(lat) if lat else None,
             "sample": f"{done} question rows ({toks} tokens) of the workload, CPU fp32 oracle on the same weights, "
@@ -201,10 +291,15 @@ def cpu_baseline(model_dir, dtype, wl, rows_idx, max_seconds=30.0, prefix_cache=
 def reference_arm(args, rank, world):
     if rank != 0:
         return 0
+    cores = host_cores()
+    with use_all_cores(cores):
+        return _reference_arm(args, cores)
+
+
+def _reference_arm(args, cores):
     from oracle import kev_oracle as ko
     name, store, dtype = "kev-0.8b", "bf16", "bf16"
     d = synth.write_model(model_dir_for(name, store, args.seed), name, args.seed, store)
-    ko.set_threads(os.cpu_count() or 1)
     m = ko.load_model(d, dtype)
     wl = synth.make_workload(args.config, m.cfg.vocab_size, seed=args.seed)
     rows_per_req = len(wl.rows) / wl.n_requests
@@ -230,7 +325,7 @@ def reference_arm(args, rank, world):
             "config": {"workload": f"cfg{args.config}: Kev-0.8B, 32 requests x (choice-4, noul, score-5), lengths "
                                    "U[64,512]; prefix cache: each request's shared prefix once, questions as branches",
                        "model": "kev-0.8b (bf16 weights, fp32 math)", "step": "one whole request per step"},
-            "cpu_baseline": {"value": value, "unit": "requests/s", "cores": os.cpu_count(), "kind": "port",
+            "cpu_baseline": {"value": value, "unit": "requests/s", "cores": cores, "kind": "port",
                              "sample": f"{len(times)} whole requests, {toks} prompt tokens; the CPU oracle restating "
                                        "the reference CPU fp32 Kev forward with its prefix caches (the Rust reference "
                                        "cannot be built here)"},
@@ -255,7 +350,7 @@ def reference_arm(args, rank, world):
         "config": {"workload": f"cfg{args.config}: Kev-0.8B, 32 requests x (choice-4, noul, score-5), "
                                 "lengths U[64,512]", "model": "kev-0.8b (bf16 weights, fp32 math)",
                    "step": "one question row (1/3 request) per step"},
-        "cpu_baseline": {"value": value, "unit": "requests/s", "cores": os.cpu_count(), "kind": "port",
+        "cpu_baseline": {"value": value, "unit": "requests/s", "cores": cores, "kind": "port",
                          "sample": f"{len(times)} question rows, {toks} tokens; the CPU oracle restating the "
                                    "reference CPU fp32 Kev forward (the Rust reference cannot be built here)"},
         "e2e": {"value": value, "unit": "requests/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -323,8 +418,18 @@ def main():
             quantize.write_package(d, args.packed, pd)
         d = pd
     barrier()
-    wl = synth.make_workload(args.config, synth.SPECS[name]["vocab_size"], seed=args.seed + rank,
-                             n_requests=args.requests)
+    from huncho_b200.replicas import shard_by_tokens
+    # One request pool from one seed, split over the ranks by the batcher's
+    # token-balanced plan: 32 (cfg 2) requests per GPU for configs 1-4 (weak
+    # scaling), config 5's fixed pool of 4096 requests (strong scaling).
+    strong = args.config == 5
+    per_gpu = args.requests or {1: 1, 2: 32, 3: 64, 4: 8, 5: 4096}[args.config]
+    pool = synth.make_workload(args.config, synth.SPECS[name]["vocab_size"], seed=args.seed,
+                               n_requests=per_gpu if strong else per_gpu * world)
+    req_tokens = [0] * pool.n_requests
+    for r, row in zip(pool.request_of, pool.rows):
+        req_tokens[r] += len(row)
+    wl = subset_workload(pool, shard_by_tokens(req_tokens, world)[rank])
     max_len = max(len(r) for r in wl.rows)
     backend = KevBackend(d, device=local, dtype=dtype, max_context=max(8192, max_len))
     if args.config == 4:
@@ -529,11 +634,13 @@ def main():
         backend.score_packed(*one)
         lat.append(time.perf_counter() - ts)
 
-    reqs = wl.n_requests * world
-    toks_all = n_tok * world
+    # Whole-job totals: the pool every rank scored a share of.
+    reqs = pool.n_requests
+    toks_all = pool.n_tokens
+    rows_all = len(pool.rows)
     value = reqs * args.steps / dev_total_s
     pk = peaks()
-    gemm_ms, gemm_flops, gemm_n = prof["gemm"]
+    gemm_ms, gemm_flops, _gemm_bytes, gemm_n = prof["gemm"]
     achieved = (gemm_flops / 1e12) / (gemm_ms / 1e3) if gemm_ms > 0 else None
     traffic = None  # DRAM bytes per GEMM launch from the committed full-size ncu capture
     tf = ROOT / "profiles" / "gemm_f16_tc_kernel_cfg2_dram.md"
@@ -545,20 +652,24 @@ def main():
     line = {
         "metric": "scored requests/s", "value": value, "unit": "requests/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dev_total_s / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": {"fp32": "f32", "q8_0-fp32": "q8_0 x f32", "q4_0-fp32": "q4_0 x f32"}.get(dtype, "bf16"),
+        "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": {"fp32": "f32", "q8_0-fp32": "q8_0 x f32", "q4_0-fp32": "q4_0 x f32"}.get(dtype, "bf16"),
         "data": "synthetic",
         "prompt_tokens_per_s": toks_all * args.steps / dev_total_s,
+        "questions_per_s": rows_all * args.steps / dev_total_s,
         "p50_request_latency_ms": statistics.median(step_ms),
+        "latency_ms": latency_summary(step_ms),
         "p50_single_request_latency_ms": 1000.0 * statistics.median(lat),
         "step_ms": [round(x, 3) for x in step_ms],
         "config": {"workload": WORKLOADS[args.config].format(n=wl.n_requests, dtype=dtype)
                    + ("; prefix cache: each request's shared prefix prefilled once, questions scored as its "
                       "branches" if fork_plan is not None else ""), "model": name,
-                   "rows_per_step": len(wl.rows) * world,
+                   "rows_per_step": rows_all, "requests_per_step": reqs,
                    "tokens_per_step": toks_all, "native_batches_per_step": len(groups),
                    "replicas_per_gpu": n_rep,
                    "l2": "flushed between steps (256 MiB write, outside the timed events); weights 1 GB > L2",
                    "parallelism": f"replicas x{world}",
+                   "sharding": ("one pool of {} requests (seed {}) split by shard_by_tokens; this rank: {} requests, "
+                                "{} tokens".format(reqs, args.seed, wl.n_requests, n_tok)),
                    **({"timing": "host clock around the synchronous native calls (prefill, branch scoring, "
                                  "release); inputs uploaded inside them", "prefill_tokens_per_step":
                        sum(len(p) for p in fork_plan[0]) * world,
@@ -586,7 +697,9 @@ def main():
                             "requests_per_s_this_gpu": wl.n_requests * len(serial_ms) / (sum(serial_ms) / 1000.0),
                             "note": "the same steps with the native batches in sequence on one handle"}}
            if serial_ms else {}),
-        "time_shares": {k: round(v[0] / total_prof_ms, 4) for k, v in prof.items()} if total_prof_ms else {},
+        "time_shares": {k: round(v[0] / total_prof_ms, 4) for k, v in prof.items() if v[3]}
+        if total_prof_ms else {},
+        "roofline_per_kernel": kernel_rooflines(prof, pk, dtype),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         order = [i for r in range(wl.n_requests) for i in range(len(wl.rows)) if wl.request_of[i] == r]

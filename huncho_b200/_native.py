@@ -96,7 +96,7 @@ def load(path: Path | None = None) -> ctypes.CDLL:
     lib.hk_profile_enable.argtypes = [vp, i32]
     lib.hk_profile_enable.restype = i32
     lib.hk_profile_read.argtypes = [vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
-                                    ctypes.POINTER(ctypes.c_int64), i32]
+                                    ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64), i32]
     lib.hk_profile_read.restype = i32
     lib.hk_last_error.argtypes = [vp]
     lib.hk_last_error.restype = ctypes.c_char_p

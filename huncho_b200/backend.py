@@ -383,18 +383,20 @@ class KevBackend:
             ctypes.c_void_p(d_cu_seqlens), ctypes.c_void_p(d_positions), ctypes.c_void_p(d_out),
             ctypes.c_void_p(stream)))
 
-    PROFILE_CLASSES = ("gemm", "delta_recurrence", "attention", "delta_prep", "other")
+    PROFILE_CLASSES = ("gemm", "delta", "attention", "delta_prep", "other", "rmsnorm", "attn_prep", "readout",
+                       "embed")
 
     def profile(self, enable: bool) -> None:
         """Bracket every launch with CUDA events (see hk_profile_enable)."""
         self._check(self._lib.hk_profile_enable(self._h, 1 if enable else 0))
 
     def profile_read(self) -> dict:
-        """{class: (milliseconds, algorithmic work, launches)} since the last read."""
+        """{class: (milliseconds, algorithmic FLOPs, algorithmic HBM bytes, launches)} since the last read."""
         n = len(self.PROFILE_CLASSES)
-        ms, work, cnt = (ctypes.c_double * n)(), (ctypes.c_double * n)(), (ctypes.c_int64 * n)()
-        self._check(self._lib.hk_profile_read(self._h, ms, work, cnt, n))
-        return {c: (ms[i], work[i], cnt[i]) for i, c in enumerate(self.PROFILE_CLASSES)}
+        ms, fl, by, cnt = ((ctypes.c_double * n)(), (ctypes.c_double * n)(), (ctypes.c_double * n)(),
+                           (ctypes.c_int64 * n)())
+        self._check(self._lib.hk_profile_read(self._h, ms, fl, by, cnt, n))
+        return {c: (ms[i], fl[i], by[i], cnt[i]) for i, c in enumerate(self.PROFILE_CLASSES)}
 
     def synchronize(self) -> None:
         self._check(self._lib.hk_synchronize(self._h))

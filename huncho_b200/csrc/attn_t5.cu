@@ -360,14 +360,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_t5_kernel(AttnArgs a) {
 
 template <int HD>
 void launch_t5(const AttnArgs &a, cudaStream_t s) {
-    static bool set[64] = {};
-    int dev = 0;
-    HK_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(attn_t5_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Tiles<HD>::SMEM));
-        if (dev >= 0 && dev < 64) set[dev] = true;
-    }
+    static SmemOptIn opt_in;
+    opt_in.ensure(attn_t5_kernel<HD>, Tiles<HD>::SMEM);
     dim3 grid(ceil_div(a.max_len, BM), a.nh, a.n_rows);
     attn_t5_kernel<HD><<<grid, THREADS, Tiles<HD>::SMEM, s>>>(a);
     HK_LAUNCH_CHECK();

@@ -230,14 +230,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(AttnArgs a) {
 template <int HD>
 void launch_hd(const AttnArgs &a, cudaStream_t s) {
     constexpr size_t smem = sizeof(__half) * (BQ + 2 * BKV) * (HD + 8);
-    static bool set[64] = {};
-    int dev = 0;
-    HK_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(smem)));
-        if (dev >= 0 && dev < 64) set[dev] = true;
-    }
+    static SmemOptIn opt_in;
+    opt_in.ensure(attn_tc_kernel<HD>, static_cast<int>(smem));
     dim3 grid(ceil_div(a.max_len, BQ), a.nh, a.n_rows);
     attn_tc_kernel<HD><<<grid, THREADS, smem, s>>>(a);
     HK_LAUNCH_CHECK();

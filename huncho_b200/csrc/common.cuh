@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdio>
 #include <stdexcept>
 #include <string>
@@ -85,6 +86,23 @@ __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f 
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 
 inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }
+
+// Raises a kernel's dynamic shared-memory limit once per device. Handles on
+// several host threads launch concurrently, so the per-device flags are
+// atomics (a lost race only repeats the idempotent attribute call).
+struct SmemOptIn {
+    static constexpr int kMaxDevices = 64;
+    std::atomic<bool> done[kMaxDevices] = {};
+    template <typename Kernel>
+    void ensure(Kernel *kernel, int bytes) {
+        int dev = 0;
+        HK_CUDA(cudaGetDevice(&dev));
+        const bool tracked = dev >= 0 && dev < kMaxDevices;
+        if (tracked && done[dev].load(std::memory_order_acquire)) return;
+        HK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+        if (tracked) done[dev].store(true, std::memory_order_release);
+    }
+};
 
 // Sets the message hk_op_last_error() returns on the calling thread.
 void set_op_error(const std::string &msg);

@@ -479,14 +479,8 @@ __global__ void __launch_bounds__(THREADS, 1) delta_chunk_kernel(ChunkArgs a) {
 template <bool GO>
 void launch_kernel(const ChunkArgs &a, cudaStream_t s) {
     const size_t smem = sizeof(Smem);
-    static bool set[64] = {};
-    int dev = 0;
-    HK_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(delta_chunk_kernel<GO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(smem)));
-        if (dev >= 0 && dev < 64) set[dev] = true;
-    }
+    static SmemOptIn opt_in;
+    opt_in.ensure(delta_chunk_kernel<GO>, static_cast<int>(smem));
     dim3 grid(a.n_rows, a.nv);
     delta_chunk_kernel<GO><<<grid, THREADS, smem, s>>>(a);
     HK_LAUNCH_CHECK();

@@ -647,13 +647,8 @@ void launch_delta_pipe(const DeltaRecArgs &r, const DeltaFusedInput &in, const f
     a.state_out = r.state_out;
     a.hist_in = in.hist_in;
     const int smem = static_cast<int>(sizeof(Smem));
-    static bool set[64] = {};
-    int dev = 0;
-    HK_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(delta_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        if (dev >= 0 && dev < 64) set[dev] = true;
-    }
+    static SmemOptIn opt_in;
+    opt_in.ensure(delta_pipe_kernel, smem);
     dim3 grid(r.n_rows, r.nv);
     delta_pipe_kernel<<<grid, THREADS, smem, s>>>(a);
     HK_LAUNCH_CHECK();

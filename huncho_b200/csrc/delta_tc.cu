@@ -612,13 +612,8 @@ __global__ void __launch_bounds__(THREADS, 1) delta_tc_kernel(TcArgs a) {
 
 template <bool GATED>
 void launch_tc(const TcArgs &a, cudaStream_t s) {
-    static bool set[64] = {};
-    int dev = 0;
-    HK_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(delta_tc_kernel<GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-        if (dev >= 0 && dev < 64) set[dev] = true;
-    }
+    static SmemOptIn opt_in;
+    opt_in.ensure(delta_tc_kernel<GATED>, SMEM_BYTES);
     dim3 grid(a.n_rows, a.nv);
     delta_tc_kernel<GATED><<<grid, THREADS, SMEM_BYTES, s>>>(a);
     HK_LAUNCH_CHECK();

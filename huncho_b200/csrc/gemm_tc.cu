@@ -739,14 +739,8 @@ bool make_out_map(CUtensorMap &m, const void *base, int rows, int cols, int ld, 
 
 template <int EPI>
 void launch(const GemmArgs &a, cudaStream_t s, int num_sms) {
-    static bool attr_set[64] = {};  // the attribute is per device
-    int dev = 0;
-    HK_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(gemm_f16_tc_kernel<EPI>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
+    static SmemOptIn opt_in;
+    opt_in.ensure(gemm_f16_tc_kernel<EPI>, SMEM_BYTES);
     CUtensorMap tx = make_map(a.x, a.M, a.K, a.ldx, BM);
     CUtensorMap tw = make_map(a.w, a.N, a.K, a.ldw, BN);
     TcParams p;
@@ -776,14 +770,8 @@ void launch(const GemmArgs &a, cudaStream_t s, int num_sms) {
 
 template <int EPI>
 void launch_pair(const GemmArgs &a, cudaStream_t s, int num_sms) {
-    static bool attr_set[64] = {};
-    int dev = 0;
-    HK_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        HK_CUDA(cudaFuncSetAttribute(gemm_f16_tc2_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     P_SMEM_BYTES));
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
+    static SmemOptIn opt_in;
+    opt_in.ensure(gemm_f16_tc2_kernel<EPI>, P_SMEM_BYTES);
     CUtensorMap tx = make_map(a.x, a.M, a.K, a.ldx, BM);
     CUtensorMap tw = make_map(a.w, a.N, a.K, a.ldw, BM);  // each CTA loads 128 rows of W
     TcParams p;

@@ -483,14 +483,18 @@ struct Model {
     }
 
     // Optional per-class device timing of the forward's launches (CUDA events
-    // on the handle's stream): 0 GEMM, 1 delta recurrence, 2 attention,
-    // 3 delta input stage, 4 everything else.
-    static constexpr int kProfClasses = 5;
+    // on the handle's stream), with each launch's algorithmic FLOPs and HBM
+    // bytes (one read of every input, one write of every output): 0 GEMM,
+    // 1 delta layer / recurrence, 2 attention, 3 delta input stage, 4 other
+    // (conv history, SwiGLU, gated norm), 5 RMSNorm, 6 attention input stage,
+    // 7 readout, 8 embedding.
+    static constexpr int kProfClasses = 9;
     bool prof = false;
+    double attn_pairs = 0.0;  // sum over the batch's rows of T (T + 1) / 2 (causal query-key pairs)
     struct ProfRec {
         cudaEvent_t a, b;
         int cls;
-        double work;
+        double flops, bytes;
     };
     std::vector<ProfRec> prof_recs;
     std::vector<cudaEvent_t> prof_pool;
@@ -510,11 +514,11 @@ struct Model {
         HK_CUDA(cudaEventRecord(e, stream));
         return e;
     }
-    void prof_end(cudaEvent_t a, int cls, double work) {
+    void prof_end(cudaEvent_t a, int cls, double flops, double bytes = 0.0) {
         if (!prof || !a) return;
         cudaEvent_t b = prof_event();
         HK_CUDA(cudaEventRecord(b, stream));
-        prof_recs.push_back({a, b, cls, work});
+        prof_recs.push_back({a, b, cls, flops, bytes});
     }
 
     bool packed() const { return dtype == HK_DTYPE_Q8_0 || dtype == HK_DTYPE_Q4_0; }
@@ -887,7 +891,13 @@ struct Model {
         } else {
             gemm_f16_tc(a, stream, num_sms);
         }
-        prof_end(ev, 0, 2.0 * M * W.rows * W.cols);
+        // Algorithmic bytes: the weights, the input rows and the output rows once
+        // (a residual output is read and written; SwiGLU writes half the columns).
+        const double wb = W.q ? (W.kp / 32.0) * (32.0 + 4.0) : static_cast<double>(W.cols) * esz();
+        const double ob = epi == kEpiResidual ? 8.0 : epi == kEpiStoreF32 ? 4.0 : epi == kEpiSwiGLU ? esz() / 2.0
+                                                                                                        : esz();
+        prof_end(ev, 0, 2.0 * M * W.rows * W.cols,
+                 W.rows * wb + static_cast<double>(M) * W.cols * esz() + static_cast<double>(M) * W.rows * ob);
     }
 
     // Algorithmic FLOPs of the chunked delta rule (chunk 32) for n tokens of one layer.
@@ -914,7 +924,9 @@ struct Model {
         const size_t e = esz();
         cudaEvent_t ev = prof_begin();
         launch_embed(A, ids, n_tok, embed, c.hidden, x, stream);
-        prof_end(ev, 4, 0);
+        prof_end(ev, 8, 0.0, static_cast<double>(n_tok) * c.hidden * (e + 4.0));
+        // One RMSNorm: the fp32 residual rows in, the normalised rows out (activation type).
+        const double norm_bytes = static_cast<double>(n_tok) * c.hidden * (4.0 + e) + 4.0 * c.hidden;
         auto at_layer = [&](const uint64_t *arr, int li) -> const uint64_t * {
             return arr ? arr + static_cast<size_t>(li) * n_rows : nullptr;
         };
@@ -925,7 +937,7 @@ struct Model {
             const uint64_t *out_b = cr ? at_layer(cr->out_b, li) : nullptr;
             ev = prof_begin();
             launch_rmsnorm(A, x, c.hidden, L.in_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream);
-            prof_end(ev, 4, 0);
+            prof_end(ev, 5, 0.0, norm_bytes);
             // Half-precision models: the warp-specialised delta layer kernel.
             const bool pipe = !L.full && !f32_model() && c.dk == 128 && c.dv == 128 && c.taps == 4 &&
                               c.nk > 0 && c.nv % c.nk == 0 && (ldp % 4) == 0 && (c.conv_dim() % 4) == 0;
@@ -955,7 +967,11 @@ struct Model {
                 in.hist_in = in_b;
                 ev = prof_begin();
                 launch_delta_pipe(r, in, L.gnorm_w, c.eps, static_cast<__half *>(mix), ldmix, stream);
-                prof_end(ev, 1, delta_chunk_flops(n_tok, c));
+                // Reads each token's q | k | v | z | b | a projection row (fp32), writes its
+                // gated-norm output (fp16).
+                prof_end(ev, 1, delta_chunk_flops(n_tok, c),
+                         static_cast<double>(n_tok) * ((c.conv_dim() + c.value_dim() + 2.0 * c.nv) * 4.0 +
+                                                       c.value_dim() * 2.0));
             } else if (!L.full) {
                 DeltaPrepArgs d;
                 d.proj = proj;
@@ -982,7 +998,9 @@ struct Model {
                     launch_conv_history(proj, ldp, c.conv_dim(), c.taps, cu_seqlens, n_rows, in_b, out_b, stream);
                 ev = prof_begin();
                 launch_delta_prep(d, stream);
-                prof_end(ev, 3, 0);
+                prof_end(ev, 3, 0.0,
+                         static_cast<double>(n_tok) * ((c.conv_dim() + 2.0 * c.nv) * 4.0 +
+                                                       (c.conv_dim() + 2.0 * c.nv) * 4.0));
                 DeltaRecArgs r;
                 r.q = dq;
                 r.k = dkk;
@@ -1002,11 +1020,12 @@ struct Model {
                 r.state_out = out_a;
                 ev = prof_begin();
                 launch_delta_recurrent(r, stream);
-                prof_end(ev, 1, 4.0 * n_tok * c.nv * c.dk * c.dv);
+                prof_end(ev, 1, 4.0 * n_tok * c.nv * c.dk * c.dv,
+                         static_cast<double>(n_tok) * (c.conv_dim() + 2.0 * c.nv + c.value_dim()) * 4.0);
                 ev = prof_begin();
                 launch_gated_norm(A, dout, proj + c.conv_dim(), ldp, L.gnorm_w, c.eps, n_tok, c.nv, c.dv, mix, ldmix,
                                   stream);
-                prof_end(ev, 4, 0);
+                prof_end(ev, 4, 0.0, static_cast<double>(n_tok) * c.value_dim() * (8.0 + e));
             } else {
                 AttnPrepArgs p;
                 p.proj = proj;
@@ -1029,7 +1048,10 @@ struct Model {
                 p.pre_len = cr ? cr->pre_len : nullptr;
                 ev = prof_begin();
                 launch_attn_prep(A, p, stream);
-                prof_end(ev, 4, 0);
+                // Reads q, k, v of the projection row (fp32; the gate stays for the
+                // attention kernel), writes q, k, v in the activation type.
+                prof_end(ev, 6, 0.0,
+                         static_cast<double>(n_tok) * (c.nh + 2.0 * c.nkv) * c.hd * (4.0 + e));
                 AttnArgs at;
                 at.q = aq;
                 at.k = ak;
@@ -1053,19 +1075,21 @@ struct Model {
                 if (out_a) launch_kv_store(A, at, out_a, stream);
                 ev = prof_begin();
                 launch_attention(A, at, stream);
-                prof_end(ev, 2, 0);
+                // QK^T and PV over the causal query-key pairs of every head.
+                prof_end(ev, 2, 4.0 * c.hd * c.nh * attn_pairs,
+                         static_cast<double>(n_tok) * ((c.nh + 2.0 * c.nkv) * c.hd * e + c.nh * c.hd * (4.0 + e)));
             }
             gemm(L.mix_out, mix, ldmix, n_tok, x, c.hidden, kEpiResidual);
             ev = prof_begin();
             launch_rmsnorm(A, x, c.hidden, L.post_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream);
-            prof_end(ev, 4, 0);
+            prof_end(ev, 5, 0.0, norm_bytes);
             if (fused_swiglu) {
                 gemm(L.gu, xn, ld_xn, n_tok, ffn, ldf, kEpiSwiGLU);
             } else {
                 gemm(L.gu, xn, ld_xn, n_tok, proj, ldp, kEpiStoreF32);
                 ev = prof_begin();
                 launch_swiglu(A, proj, ldp, n_tok, c.ffn, ffn, ldf, stream);
-                prof_end(ev, 4, 0);
+                prof_end(ev, 4, 0.0, static_cast<double>(n_tok) * c.ffn * (8.0 + e));
             }
             gemm(L.down, ffn, ldf, n_tok, x, c.hidden, kEpiResidual);
         }
@@ -1089,7 +1113,11 @@ struct Model {
         ro.logits = out_logits;
         ev = prof_begin();
         launch_readout(ro, stream);
-        prof_end(ev, 4, 0);
+        // The decision and option rows of the residual stream, both pointer
+        // projections (fp32) and the logits.
+        prof_end(ev, 7, 2.0 * (n_rows + n_opt) * c.hidden * dp,
+                 (static_cast<double>(n_rows) + n_opt) * c.hidden * 4.0 + 2.0 * dp * (c.hidden + 1.0) * 4.0 +
+                     n_opt * 4.0);
     }
 };
 
@@ -1329,6 +1357,11 @@ static int score_device_impl(hk::Model &m, int n_rows, const int32_t *cu_h, cons
         HK_CUDA(cudaMemcpyAsync(m.meta + L.row_order, t, (n_pages ? w_tail : static_cast<size_t>(n_rows)) * 4,
                                 cudaMemcpyHostToDevice, m.stream));
         HK_CUDA(cudaEventRecord(st.done, m.stream));
+    }
+    m.attn_pairs = 0.0;
+    for (int r = 0; r < n_rows; ++r) {
+        const double t = cu_h[r + 1] - cu_h[r];
+        m.attn_pairs += t * (t + 1.0) / 2.0;
     }
     const uint64_t before = hk::tl_launches;
     hk::build_meta_kernel<<<std::min(hk::ceil_div(L.total, 256), 1024), 256, 0, m.stream>>>(m.meta, n_rows, n, p, L);
@@ -1677,15 +1710,16 @@ int hk_profile_enable(hk_model *h, int enable) {
     return HK_OK;
 }
 
-int hk_profile_read(hk_model *h, double *ms, double *work, int64_t *count, int n_classes) {
-    if (!h || !h->m || !ms || !work || !count) return HK_ERR_ARGUMENT;
+int hk_profile_read(hk_model *h, double *ms, double *flops, double *bytes, int64_t *count, int n_classes) {
+    if (!h || !h->m || !ms || !flops || !bytes || !count) return HK_ERR_ARGUMENT;
     hk::Model &m = *h->m;
     return guarded(h, [&]() -> int {
         HK_CUDA(cudaSetDevice(m.device));
         HK_CUDA(cudaDeviceSynchronize());  // events may sit on a caller's stream
         for (int i = 0; i < n_classes; ++i) {
             ms[i] = 0.0;
-            work[i] = 0.0;
+            flops[i] = 0.0;
+            bytes[i] = 0.0;
             count[i] = 0;
         }
         for (auto &r : m.prof_recs) {
@@ -1693,7 +1727,8 @@ int hk_profile_read(hk_model *h, double *ms, double *work, int64_t *count, int n
             HK_CUDA(cudaEventElapsedTime(&t, r.a, r.b));
             if (r.cls < n_classes) {
                 ms[r.cls] += t;
-                work[r.cls] += r.work;
+                flops[r.cls] += r.flops;
+                bytes[r.cls] += r.bytes;
                 count[r.cls] += 1;
             }
             m.prof_pool.push_back(r.a);

@@ -651,8 +651,13 @@ __global__ void pointer_logits_kernel(const float *__restrict__ proj, int dp, in
     const int o = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (o >= n_opt) return;
+    const int d = opt_dec[o];
+    if (d < 0 || d >= n_dec) {  // no decision row to pair with: a NaN logit, no read
+        if (lane == 0) logits[o] = __int_as_float(0x7fc00000);
+        return;
+    }
     const float *k = proj + static_cast<size_t>(n_dec + o) * dp;
-    const float *q = proj + static_cast<size_t>(opt_dec[o]) * dp;
+    const float *q = proj + static_cast<size_t>(d) * dp;
     float s = 0.f;
     for (int i = lane; i < dp; i += 32) s += k[i] * q[i];
     s = warp_sum(s);

@@ -196,6 +196,10 @@ struct ReadoutArgs {
     float *logits;  // [n_opt]
 };
 void launch_readout(const ReadoutArgs &a, cudaStream_t s);
+// Argument checks shared by the readout entry points (std::invalid_argument on failure).
+void check_readout_args(const float *x, int hidden, const float *final_w, const int32_t *idx, const int32_t *opt_dec,
+                        int n_dec, int n_opt, const float *wq, const float *bq, const float *wk, const float *bk,
+                        int dp, const float *logits);
 
 // Calibrated probabilities and typed answers of every question of a batch
 // (answers.cu). Layout of AnswerRec equals the C ABI's hk_answer.

@@ -36,6 +36,16 @@ int current_sms() {
 namespace hk {
 // Record the calling thread's kernel-level entry-point error (hk_op_last_error).
 void set_op_error(const std::string &msg) { tl_op_error = msg; }
+
+void check_readout_args(const float *x, int hidden, const float *final_w, const int32_t *idx, const int32_t *opt_dec,
+                        int n_dec, int n_opt, const float *wq, const float *bq, const float *wk, const float *bk,
+                        int dp, const float *logits) {
+    if (n_dec < 0 || n_opt < 0 || hidden <= 0 || dp <= 0)
+        throw std::invalid_argument("readout: row counts must be >= 0, hidden and pointer width > 0");
+    if (n_opt > 0 && n_dec == 0) throw std::invalid_argument("readout: options need at least one decision row");
+    if (n_opt > 0 && (!x || !final_w || !idx || !opt_dec || !wq || !bq || !wk || !bk || !logits))
+        throw std::invalid_argument("readout: null pointer");
+}
 }  // namespace hk
 
 extern "C" {
@@ -138,6 +148,38 @@ int hk_op_delta_chunked(int kernel, const float *q, const float *k, const float 
     });
 }
 
+int hk_op_delta_layer(const float *proj, int ldp, const int32_t *cu_seqlens, int n_rows, int nk, int nv,
+                      const float *conv_w, const float *base_g, const float *dt_bias, const float *norm_w, float eps,
+                      void *out, int ldo, void *stream) {
+    return op_guard([&] {
+        if (!proj || !cu_seqlens || !conv_w || !base_g || !dt_bias || !norm_w || !out)
+            throw std::invalid_argument("hk_op_delta_layer: null pointer");
+        if (n_rows < 0 || nk <= 0 || nv <= 0 || nv % nk != 0)
+            throw std::invalid_argument("hk_op_delta_layer: value heads must be a positive multiple of key heads");
+        const int conv_dim = 2 * nk * 128 + nv * 128;
+        if (ldp < conv_dim + nv * 128 + 2 * nv || ldo < nv * 128)
+            throw std::invalid_argument("hk_op_delta_layer: row strides too small for the heads");
+        hk::DeltaRecArgs r;
+        r.cu_seqlens = cu_seqlens;
+        r.n_rows = n_rows;
+        r.nk = nk;
+        r.nv = nv;
+        r.dk = 128;
+        r.dv = 128;
+        r.exact = 0;
+        hk::DeltaFusedInput in;
+        in.proj = proj;
+        in.ldp = ldp;
+        in.conv_dim = conv_dim;
+        in.conv_w = conv_w;
+        in.base_g = base_g;
+        in.dt_bias = dt_bias;
+        if (!hk::delta_pipe_supported(r, in))
+            throw std::invalid_argument("hk_op_delta_layer: ldp must be a multiple of 4 floats");
+        hk::launch_delta_pipe(r, in, norm_w, eps, static_cast<__half *>(out), ldo, static_cast<cudaStream_t>(stream));
+    });
+}
+
 int hk_op_attention(int act, const void *q, const void *k, const void *v, const float *proj, int ldp,
                     const int32_t *cu_seqlens, const int32_t *tok_row, int n, int n_rows, int max_len, int nh,
                     int nkv, int hd, void *out, int ldo, void *stream) {
@@ -166,6 +208,8 @@ int hk_op_readout(const float *x, int hidden, const float *final_w, float eps, c
                   const int32_t *opt_dec, int n_dec, int n_opt, const float *wq, const float *bq, const float *wk,
                   const float *bk, int dp, float *hn, float *proj, float *logits, void *stream) {
     return op_guard([&] {
+        hk::check_readout_args(x, hidden, final_w, idx, opt_dec, n_dec, n_opt, wq, bq, wk, bk, dp, logits);
+        if (!hn || !proj) throw std::invalid_argument("hk_op_readout: null scratch pointer");
         hk::ReadoutArgs a;
         a.x = x;
         a.hidden = hidden;
@@ -185,6 +229,26 @@ int hk_op_readout(const float *x, int hidden, const float *final_w, float eps, c
         a.proj = proj;
         a.logits = logits;
         hk::launch_readout(a, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int hk_op_answers(const float *logits, const int32_t *cu_positions, const int32_t *question_types, int n_rows,
+                  float temperature, float *probs, void *answers, void *stream) {
+    return op_guard([&] {
+        if (n_rows < 0) throw std::invalid_argument("hk_op_answers: negative row count");
+        if (n_rows > 0 && (!logits || !cu_positions || !question_types || !probs || !answers))
+            throw std::invalid_argument("hk_op_answers: null pointer");
+        if (!(temperature > 0.f) || !std::isfinite(temperature))
+            throw std::invalid_argument("hk_op_answers: temperature must be positive and finite");
+        hk::AnswerArgs a;
+        a.logits = logits;
+        a.cu_positions = cu_positions;
+        a.qtype = question_types;
+        a.n_rows = n_rows;
+        a.temperature = temperature;
+        a.probs = probs;
+        a.out = static_cast<hk::AnswerRec *>(answers);
+        hk::launch_answers(a, static_cast<cudaStream_t>(stream));
     });
 }
 

@@ -78,6 +78,12 @@ extern "C" int hk_op_readout_noalloc(const float *x, int hidden, const float *fi
                          ", pointer width <= " + std::to_string(kNoAllocMaxDp) + ")");
         return HK_ERR_ARGUMENT;
     }
+    try {
+        hk::check_readout_args(x, hidden, final_w, idx, opt_dec, n_dec, n_opt, wq, bq, wk, bk, dp, logits);
+    } catch (const std::exception &ex) {
+        hk::set_op_error(std::string("hk_op_readout_noalloc: ") + ex.what());
+        return HK_ERR_ARGUMENT;
+    }
     float *scratch = nullptr;
     const cudaError_t e = scratch_address(&scratch);
     if (e != cudaSuccess) {

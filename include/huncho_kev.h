@@ -236,15 +236,18 @@ uint64_t hk_kernel_launches(const hk_model *m);
 
 /*
  * Device-time profile of the forward's launches, by class: 0 projection GEMMs,
- * 1 delta-rule recurrence, 2 attention, 3 delta input stage, 4 the rest.
+ * 1 delta layer (fused kernel) or delta-rule recurrence, 2 attention, 3 delta
+ * input stage, 4 other (conv history, SwiGLU, gated norm), 5 RMSNorm,
+ * 6 attention input stage, 7 pointer readout, 8 embedding (9 classes).
  * While enabled, each launch is bracketed by CUDA events on the handle's
  * stream. hk_profile_read synchronises the stream, writes per-class summed
- * milliseconds, algorithmic work (FLOPs) and launch counts for the first
+ * milliseconds, algorithmic FLOPs, algorithmic HBM bytes (one read of every
+ * input, one write of every output) and launch counts for the first
  * n_classes classes, and clears the record. No reference counterpart (the
  * reference has no GPU profiler integration).
  */
 int hk_profile_enable(hk_model *m, int enable);
-int hk_profile_read(hk_model *m, double *ms, double *work, int64_t *count, int n_classes);
+int hk_profile_read(hk_model *m, double *ms, double *flops, double *bytes, int64_t *count, int n_classes);
 
 /* The last error message on this handle (never NULL). */
 const char *hk_last_error(const hk_model *m);

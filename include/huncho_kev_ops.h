@@ -56,6 +56,21 @@ int hk_op_delta_chunked(int kernel, const float *q, const float *k, const float 
                         const float *beta, const int32_t *cu_seqlens, int n_rows, int nk, int nv, const float *z,
                         int ldz, const float *norm_w, float eps, void *out, int ldo, void *stream);
 
+/* The whole delta layer between its in-projection and its out-projection, as
+ * the half-precision models run it (one warp-specialised kernel): from the
+ * fp32 projection rows proj [n, ldp] = q (nk*128) | k (nk*128) | v (nv*128) |
+ * z (nv*128) | b (nv) | a (nv), the causal depthwise conv over 4 taps + SiLU
+ * (conv_w [conv_dim][4], conv_dim = 2*nk*128 + nv*128), l2norm of q (times
+ * 1/sqrt(128)) and k, beta = sigmoid(b), g = base_g * softplus(a + dt_bias)
+ * (base_g = -exp(A_log)), the chunked gated delta rule with a zero initial
+ * state per row, and the gated RMSNorm rms(o) * norm_w * silu(z), written in
+ * fp16 to out [n, ldo] (the out-projection input). Replaces
+ * LinearAttn::forward between in_proj and out_proj (qwen3_5.rs:846-938) with
+ * recurrent_gated_delta (qwen3_5.rs:950-987). ldp % 4 == 0. */
+int hk_op_delta_layer(const float *proj, int ldp, const int32_t *cu_seqlens, int n_rows, int nk, int nv,
+                      const float *conv_w, const float *base_g, const float *dt_bias, const float *norm_w, float eps,
+                      void *out, int ldo, void *stream);
+
 /* Causal GQA attention with the sigmoid output gate (qwen3_5.rs:669-714).
  * act 0: fp32, 1: fp16. q [n, nh, hd]; k, v [n, nkv, hd] (act type); gate read
  * from the fp32 proj[t, h*2*hd + hd + i] (row stride ldp); out [n, ldo] (act
@@ -71,7 +86,11 @@ int hk_op_attention(int act, const void *q, const void *k, const void *v, const 
  * norm); each row is RMS-normalised with final_w (effective weight), decision
  * rows projected by wq/bq and option rows by wk/bk ([dp, hidden], [dp], fp32),
  * and logits[j] = k_j . q_{opt_dec[j]} / sqrt(dp). Scratch (caller-owned):
- * hn [n_dec + n_opt, hidden] and proj [n_dec + n_opt, dp], fp32. */
+ * hn [n_dec + n_opt, hidden] and proj [n_dec + n_opt, dp], fp32. Index
+ * contract: every idx entry is a row of x (not checked: the kernels do not
+ * know x's row count); an opt_dec entry outside [0, n_dec) gives that option
+ * a NaN logit without reading another row. Null pointers, negative counts,
+ * or options without a decision row: HK_ERR_ARGUMENT. */
 int hk_op_readout(const float *x, int hidden, const float *final_w, float eps, const int32_t *idx,
                   const int32_t *opt_dec, int n_dec, int n_opt, const float *wq, const float *bq,
                   const float *wk, const float *bk, int dp, float *hn, float *proj, float *logits,
@@ -92,6 +111,15 @@ int hk_op_readout_noalloc(const float *x, int hidden, const float *final_w, floa
                           const int32_t *idx, const int32_t *opt_dec, int n_dec, int n_opt,
                           const float *wq, const float *bq, const float *wk, const float *bk,
                           int dp, float *logits, void *stream);
+
+/* Calibration and typed answers of already-scored questions (the device half
+ * of hk_score_answers) over device buffers: logits [cu_positions[n_rows]]
+ * fp32, cu_positions [n_rows + 1], question_types [n_rows] (HK_QUESTION_*);
+ * writes probs [cu_positions[n_rows]] and answers [n_rows] (hk_answer
+ * layout: best, status, confidence, value). Follows calibration.rs:36-64,
+ * 87-147 and engine.rs:1448-1513. */
+int hk_op_answers(const float *logits, const int32_t *cu_positions, const int32_t *question_types, int n_rows,
+                  float temperature, float *probs, void *answers, void *stream);
 
 /* Number of SMs the GEMM grid is sized for on the current device. */
 int hk_op_num_sms(void);

@@ -24,8 +24,10 @@ from pathlib import Path
 import torch
 from safetensors.numpy import save_file
 
-src = Path(sys.argv[1] if len(sys.argv) > 1 else
-           "/root/reference/crates/huncho-backend/tests/fixtures/tiny_kev")
+if len(sys.argv) != 2:
+    sys.exit("usage: python tests/golden/make_tiny_kev.py <reference fixture dir "
+             "(crates/huncho-backend/tests/fixtures/tiny_kev of a grafuls/huncho checkout)>")
+src = Path(sys.argv[1])
 dst = Path(__file__).resolve().parent / "tiny_kev"
 dst.mkdir(parents=True, exist_ok=True)
 for name in ("config.json", "model.safetensors", "adapter_model.safetensors", "adapter_config.json"):

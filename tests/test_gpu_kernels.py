@@ -378,3 +378,141 @@ def test_tc_gemm_cta_pairs_equal_single_cta(lib, epi, M, N, K):
     gemm(lib, 1, epi, x, w, single)
     gemm(lib, 2, epi, x, w, pair)
     assert torch.equal(single, pair)
+
+
+# ---------------------------------------------------------------------------
+# The fused delta layer (delta_pipe_kernel), the half-precision models' path
+# ---------------------------------------------------------------------------
+
+def _delta_layer_inputs(rng, lens, nk, nv, stress=False):
+    """Projection rows q | k | v | z | b | a for hk_op_delta_layer. With
+    `stress`, g = base_g * softplus(a + dt_bias) is uniform in [-0.1, -1e-4]
+    and beta = sigmoid(b) uniform in (0, 1): the long-context configuration's
+    decay and write strengths, set through the kernel's own gate formulas."""
+    n = sum(lens)
+    conv_dim = 2 * nk * 128 + nv * 128
+    ldp = conv_dim + nv * 128 + 2 * nv
+    ldp += (-ldp) % 4
+    proj = np.zeros((n, ldp), np.float32)
+    proj[:, :conv_dim + nv * 128] = rng.standard_normal((n, conv_dim + nv * 128), dtype=np.float32)
+    conv_w = rng.uniform(-0.5, 0.5, (conv_dim, 4)).astype(np.float32)
+    dt_bias = np.full(nv, 0.1, np.float32)
+    if stress:
+        base_g = np.full(nv, -1.0, np.float32)
+        u = rng.uniform(1e-4, 0.1, (n, nv))
+        beta = rng.uniform(1e-6, 1.0 - 1e-6, (n, nv))
+        proj[:, conv_dim + nv * 128 + nv:conv_dim + nv * 128 + 2 * nv] = np.log(np.expm1(u)) - 0.1
+        proj[:, conv_dim + nv * 128:conv_dim + nv * 128 + nv] = np.log(beta / (1.0 - beta))
+    else:
+        base_g = (-np.exp(np.full(nv, 0.2, np.float32))).astype(np.float32)
+        proj[:, conv_dim + nv * 128:] = rng.standard_normal((n, ldp - conv_dim - nv * 128), dtype=np.float32)
+    norm_w = (1.0 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    return proj, ldp, conv_w, base_g, dt_bias, norm_w, cu
+
+
+def _delta_layer_oracle(proj, conv_w, base_g, dt_bias, norm_w, cu, nk, nv, eps=1e-6):
+    """LinearAttn::forward between in_proj and out_proj (qwen3_5.rs:846-938) on
+    the oracle's pieces: causal conv (conv_cpu.rs order) + SiLU per row, l2norm,
+    gates, the per-token recurrence (delta_cpu.rs order), gated RMSNorm."""
+    conv_dim = 2 * nk * 128 + nv * 128
+    n = proj.shape[0]
+    mixed = np.zeros((n, conv_dim), np.float32)
+    for r in range(len(cu) - 1):
+        s, e = cu[r], cu[r + 1]
+        mixed[s:e] = ko.silu(ko.causal_conv(proj[s:e, :conv_dim].T.copy(), conv_w)).T
+    q = mixed[:, :nk * 128].reshape(n, nk, 128)
+    k = mixed[:, nk * 128:2 * nk * 128].reshape(n, nk, 128)
+    v = mixed[:, 2 * nk * 128:].reshape(n, nv, 128).copy()
+    q = (ko.l2norm(q) * np.float32(128 ** -0.5)).astype(np.float32)
+    k = ko.l2norm(k)
+    z = proj[:, conv_dim:conv_dim + nv * 128].reshape(n, nv, 128)
+    b = ko.sigmoid(proj[:, conv_dim + nv * 128:conv_dim + nv * 128 + nv])
+    a = proj[:, conv_dim + nv * 128 + nv:conv_dim + nv * 128 + 2 * nv]
+    g = (base_g[None, :] * ko.softplus(a + dt_bias[None, :])).astype(np.float32)
+    o = _delta_oracle(q, k, v, g, b, cu, nk, nv)
+    return ko.rms_norm_gated(o, z, norm_w, eps).reshape(n, nv * 128)
+
+
+def _run_delta_layer(lib, proj, ldp, conv_w, base_g, dt_bias, norm_w, cu, nk, nv, eps=1e-6):
+    t = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (proj, cu, conv_w, base_g, dt_bias, norm_w)]
+    n = proj.shape[0]
+    out = torch.zeros(n, nv * 128, dtype=torch.half, device="cuda")
+    lib.hk_op_delta_layer.argtypes = ([ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p] + [ctypes.c_int] * 3
+                                      + [ctypes.c_void_p] * 4 + [ctypes.c_float, ctypes.c_void_p, ctypes.c_int,
+                                                                 ctypes.c_void_p])
+    rc = lib.hk_op_delta_layer(_p(t[0]), ldp, _p(t[1]), len(cu) - 1, nk, nv, _p(t[2]), _p(t[3]), _p(t[4]), _p(t[5]),
+                               eps, _p(out), nv * 128, None)
+    assert rc == 0, lib.hk_op_last_error()
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("nk,nv", [(16, 16), (16, 32)])
+def test_delta_layer_kernel_vs_oracle(lib, nk, nv):
+    """The model's delta kernel (conv + gates + chunked rule + gated norm in one
+    launch) on ragged rows: 1-token rows, a row ending exactly on a chunk
+    boundary, rows of many chunks; nv = 2 nk is the 4B model's head repeat."""
+    rng = np.random.default_rng(31 + nv)
+    args = _delta_layer_inputs(rng, [37, 1, 130, 64, 300, 2, 33], nk, nv)
+    proj, ldp, conv_w, base_g, dt_bias, norm_w, cu = args
+    got = _run_delta_layer(lib, *args, nk, nv)
+    ref = _delta_layer_oracle(proj, conv_w, base_g, dt_bias, norm_w, cu, nk, nv)
+    assert np.isfinite(got).all()
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    print(f"delta layer nk={nk} nv={nv}: max |err| / max |ref| = {err:.3g}")
+    assert err <= 3e-3
+
+
+def test_delta_layer_kernel_long_context_stress(lib):
+    """The long-context stress configuration at the model's own delta kernel:
+    two 8192-token rows, g uniform in [-0.1, 0) and beta uniform in (0, 1)."""
+    rng = np.random.default_rng(88)
+    nk = nv = 16
+    args = _delta_layer_inputs(rng, [8192, 8192], nk, nv, stress=True)
+    proj, ldp, conv_w, base_g, dt_bias, norm_w, cu = args
+    got = _run_delta_layer(lib, *args, nk, nv)
+    ref = _delta_layer_oracle(proj, conv_w, base_g, dt_bias, norm_w, cu, nk, nv)
+    assert np.isfinite(got).all()
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    print(f"delta layer 2 x 8192 stress: max |err| / max |ref| = {err:.3g}")
+    assert err <= 5e-3
+
+
+def test_delta_layer_rejects_bad_shapes(lib):
+    lib.hk_op_delta_layer.argtypes = ([ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p] + [ctypes.c_int] * 3
+                                      + [ctypes.c_void_p] * 4 + [ctypes.c_float, ctypes.c_void_p, ctypes.c_int,
+                                                                 ctypes.c_void_p])
+    x = torch.zeros(64, device="cuda")
+    assert lib.hk_op_delta_layer(_p(x), 8224, _p(x), 1, 16, 24, _p(x), _p(x), _p(x), _p(x), 1e-6, _p(x), 2048,
+                                 None) == -5  # nv not a multiple of nk
+    assert lib.hk_op_delta_layer(_p(x), 100, _p(x), 1, 16, 16, _p(x), _p(x), _p(x), _p(x), 1e-6, _p(x), 2048,
+                                 None) == -5  # row stride too small
+    assert lib.hk_op_delta_layer(None, 8224, _p(x), 1, 16, 16, _p(x), _p(x), _p(x), _p(x), 1e-6, _p(x), 2048,
+                                 None) == -5
+
+
+def test_readout_bad_decision_index_gives_nan_without_reading(lib):
+    """An option whose decision index lies outside [0, n_dec) gets a NaN logit
+    (the kernel checks the index and reads nothing for it); the other options
+    are unchanged."""
+    g = torch.Generator(device="cuda").manual_seed(22)
+    n_tok, hidden, dp, n_dec, n_opt = 50, 256, 64, 4, 12
+    x, w, wq, bq, wk, bk, idx, opt_dec = _readout_inputs(g, n_tok, hidden, dp, n_dec, n_opt)
+    hn = torch.empty(n_dec + n_opt, hidden, device="cuda")
+    proj = torch.empty(n_dec + n_opt, dp, device="cuda")
+    lib.hk_op_readout.argtypes = ([ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_float] + [ctypes.c_void_p] * 2
+                                  + [ctypes.c_int] * 2 + [ctypes.c_void_p] * 4 + [ctypes.c_int] + [ctypes.c_void_p] * 4)
+    good = torch.empty(n_opt, device="cuda")
+    assert lib.hk_op_readout(_p(x), hidden, _p(w), 1e-6, _p(idx), _p(opt_dec), n_dec, n_opt, _p(wq), _p(bq), _p(wk),
+                             _p(bk), dp, _p(hn), _p(proj), _p(good), None) == 0
+    bad_dec = opt_dec.clone()
+    bad_dec[3] = n_dec
+    bad_dec[7] = -1
+    got = torch.empty(n_opt, device="cuda")
+    assert lib.hk_op_readout(_p(x), hidden, _p(w), 1e-6, _p(idx), _p(bad_dec), n_dec, n_opt, _p(wq), _p(bq), _p(wk),
+                             _p(bk), dp, _p(hn), _p(proj), _p(got), None) == 0
+    torch.cuda.synchronize()
+    assert torch.isnan(got[3]) and torch.isnan(got[7])
+    keep = [i for i in range(n_opt) if i not in (3, 7)]
+    assert torch.equal(got[keep], good[keep])
