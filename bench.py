@@ -6,8 +6,8 @@ Kev scorer in bf16 (random-init weights from a fixed seed), 32 requests with
 lengths uniform in [64, 512]; each asks a 4-option choice, a noul and a 5-level
 score, so one step scores 96 independent rows (~27.6k prompt tokens) split into
 two native batches of 48 rows. Each GPU holds `--replicas` (default 2) model
-handles (hk_replica: the same package loaded again, so each handle has its own
-copy of the weights, workspace and CUDA stream); a step's native batches are dealt to them round-robin and run
+handles (hk_replica on the same GPU: one shared copy of the weights, each
+handle with its own workspace and CUDA stream); a step's native batches are dealt to them round-robin and run
 concurrently, so one batch's kernel tails and launch gaps overlap the other's
 work. Under torchrun one request pool is generated from one seed (32 requests
 per GPU for configs 1-4: weak scaling; config 5's fixed 4096 requests: strong
@@ -374,7 +374,7 @@ def main():
                     help="run the workload on the reference's packed profile: the synthetic model converted "
                          "(fp32 weights, projections in GGML Q8_0 / Q4_0 blocks, fp32 activations)")
     ap.add_argument("--replicas", type=int, default=2,
-                    help="model handles per GPU (each its own copy of the weights and its own stream); the step's native "
+                    help="model handles per GPU (shared weights; each its own workspace and stream); the step's native "
                          "batches run on them concurrently (1 = one handle, batches in sequence)")
     ap.add_argument("--prefix-cache", action="store_true",
                     help="score each request's questions as branches of its cached shared prefix (the reference "

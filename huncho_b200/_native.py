@@ -28,7 +28,8 @@ EXPORTED = (
     "hk_create", "hk_replica", "hk_capabilities_get", "hk_score", "hk_score_answers", "hk_score_device",
     "hk_score_cached",
     "hk_prefill", "hk_fork", "hk_release_cache", "hk_cache_info",
-    "hk_synchronize", "hk_kernel_launches", "hk_set_kv_page_tokens", "hk_profile_enable", "hk_profile_read",
+    "hk_synchronize", "hk_kernel_launches", "hk_weight_bytes", "hk_set_kv_page_tokens", "hk_profile_enable",
+    "hk_profile_read",
     "hk_last_error",
     "hk_create_error", "hk_destroy",
 )
@@ -91,6 +92,8 @@ def load(path: Path | None = None) -> ctypes.CDLL:
     lib.hk_synchronize.restype = i32
     lib.hk_kernel_launches.argtypes = [vp]
     lib.hk_kernel_launches.restype = ctypes.c_uint64
+    lib.hk_weight_bytes.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64)]
+    lib.hk_weight_bytes.restype = ctypes.c_uint64
     lib.hk_set_kv_page_tokens.argtypes = [vp, i32, ctypes.c_uint64]
     lib.hk_set_kv_page_tokens.restype = i32
     lib.hk_profile_enable.argtypes = [vp, i32]

@@ -110,6 +110,12 @@ class KevBackend:
     def kernel_launches(self) -> int:
         return int(self._lib.hk_kernel_launches(self._h))
 
+    def weight_store(self):
+        """(device bytes of the weights, store id); replicas on one GPU share the id."""
+        sid = ctypes.c_uint64()
+        n = self._lib.hk_weight_bytes(self._h, ctypes.byref(sid))
+        return int(n), int(sid.value)
+
     # ---------------------------------------------------------------- trait
     def id(self) -> str:
         return "b200-kev"
@@ -125,8 +131,9 @@ class KevBackend:
         )
 
     def replica(self, device: Optional[int] = None) -> "KevBackend":
-        """The same model (on `device`, default the same GPU) with fresh state;
-        the package is loaded again, so the replica holds its own weight copy."""
+        """The same model (on `device`, default the same GPU) with fresh state.
+        On the same GPU the replica shares this handle's weights (one device
+        copy); on another GPU the package is loaded there."""
         h = ctypes.c_void_p()
         dev = self.device if device is None else device
         rc = self._lib.hk_replica(self._h, dev, ctypes.byref(h))

@@ -337,6 +337,21 @@ int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
 }  // namespace
 
+// The device memory of a loaded package's immutable tensors (projections,
+// embedding table, norms, conv and gate parameters, pointer head). Handles on
+// the same GPU share one store (the reference's replicas share their weights
+// through Arc clones, qwen3_5.rs:2515-2535); the last handle frees it.
+struct WeightStore {
+    int device = 0;
+    std::vector<void *> allocs;
+    size_t bytes = 0;
+    ~WeightStore() {
+        if (allocs.empty()) return;
+        cudaSetDevice(device);
+        for (void *p : allocs) cudaFree(p);
+    }
+};
+
 struct Model {
     std::string dir;
     int device = 0;
@@ -349,7 +364,8 @@ struct Model {
     float temperature = 1.0f;
     int dp = 256;
     cudaStream_t stream = nullptr;
-    std::vector<void *> allocs;
+    std::shared_ptr<WeightStore> wstore = std::make_shared<WeightStore>();
+    std::vector<void *> allocs;  // this handle's own small buffers (error word, cache table)
     void *embed = nullptr;
     float *final_norm = nullptr;
     float *inv_freq = nullptr;
@@ -550,6 +566,7 @@ struct Model {
         }
         for (void *p : ws) cudaFree(p);
         for (void *p : allocs) cudaFree(p);
+        wstore.reset();
         if (pinned) cudaFreeHost(pinned);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -557,12 +574,15 @@ struct Model {
     template <typename T>
     T *dev_alloc(size_t count, std::vector<void *> &owner) {
         void *p = nullptr;
-        HK_CUDA(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T)));
+        const size_t bytes = std::max<size_t>(count, 1) * sizeof(T);
+        HK_CUDA(cudaMalloc(&p, bytes));
         owner.push_back(p);
+        if (&owner == &wstore->allocs) wstore->bytes += bytes;
         return static_cast<T *>(p);
     }
+    std::vector<void *> &walloc() { return wstore->allocs; }
     float *upload_f32(const std::vector<float> &v) {
-        float *p = dev_alloc<float>(v.size(), allocs);
+        float *p = dev_alloc<float>(v.size(), walloc());
         HK_CUDA(cudaMemcpy(p, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
         return p;
     }
@@ -590,7 +610,7 @@ struct Model {
             std::vector<float> h(static_cast<size_t>(R) * m.ld, 0.0f);
             for (int r = 0; r < R; ++r)
                 std::memcpy(&h[static_cast<size_t>(r) * m.ld], &full[static_cast<size_t>(src_row(r)) * K], K * 4);
-            float *d = dev_alloc<float>(h.size(), allocs);
+            float *d = dev_alloc<float>(h.size(), walloc());
             HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
             m.w = d;
         } else {
@@ -618,7 +638,7 @@ struct Model {
                     for (int i = 0; i < K; ++i) dst[i] = f32_to_f16_bits(model_round(row[i]));
                 }
             }
-            uint16_t *d = dev_alloc<uint16_t>(h.size(), allocs);
+            uint16_t *d = dev_alloc<uint16_t>(h.size(), walloc());
             HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
             m.w = d;
             if (dtype == HK_DTYPE_INT8W) m.scale = upload_f32(sc);
@@ -669,7 +689,7 @@ struct Model {
         m.cols = K;
         m.ld = kp;
         m.kp = kp;
-        m.q = dev_alloc<int8_t>(q.size(), allocs);
+        m.q = dev_alloc<int8_t>(q.size(), walloc());
         HK_CUDA(cudaMemcpy(m.q, q.data(), q.size(), cudaMemcpyHostToDevice));
         m.qd = upload_f32(d);
         max_kp = std::max(max_kp, kp);
@@ -691,6 +711,7 @@ struct Model {
 
     void load(const std::string &model_dir) {
         dir = model_dir;
+        wstore->device = device;
         std::unique_ptr<WeightSource> srcp(packed() ? new WeightSource(model_dir, WeightSource::Packed{})
                                                     : new WeightSource(model_dir));
         const WeightSource &src = *srcp;
@@ -750,13 +771,13 @@ struct Model {
             std::vector<float> e = src.get("model.language_model.embed_tokens.weight",
                                            {static_cast<int64_t>(c.vocab), c.hidden});
             if (f32_model()) {
-                float *d = dev_alloc<float>(e.size(), allocs);
+                float *d = dev_alloc<float>(e.size(), walloc());
                 HK_CUDA(cudaMemcpy(d, e.data(), e.size() * 4, cudaMemcpyHostToDevice));
                 embed = d;
             } else {
                 std::vector<uint16_t> h(e.size());
                 for (size_t i = 0; i < e.size(); ++i) h[i] = f32_to_f16_bits(model_round(e[i]));
-                uint16_t *d = dev_alloc<uint16_t>(h.size(), allocs);
+                uint16_t *d = dev_alloc<uint16_t>(h.size(), walloc());
                 HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
                 embed = d;
             }
@@ -817,10 +838,46 @@ struct Model {
         ldp = round_up(std::max(std::max(pd, pa), fused_swiglu ? 0 : 2 * c.ffn), 8);
         ldmix = round_up(std::max(c.value_dim(), c.nh * c.hd), 8);
         ldf = round_up(c.ffn, 8);
+        for (const Layer &L : layers) layer_slot.push_back(L.full ? n_attn++ : n_delta++);
+        alloc_handle_state();
+    }
+
+    // The per-handle device state next to the weights: the error word and the
+    // cached-batch address table.
+    void alloc_handle_state() {
         err = dev_alloc<uint32_t>(1, allocs);
         HK_CUDA(cudaMemset(err, 0, 4));
-        for (const Layer &L : layers) layer_slot.push_back(L.full ? n_attn++ : n_delta++);
         cache_meta = dev_alloc<uint64_t>(4 * layers.size() * HK_MAX_CACHED_ROWS + HK_MAX_CACHED_ROWS, allocs);
+    }
+
+    // A replica on the source's GPU: the same immutable weights (shared, not
+    // copied), its own stream, workspace, error word, caches and settings.
+    void share_weights(const Model &src) {
+        dir = src.dir;
+        cfg = src.cfg;
+        fused_swiglu = src.fused_swiglu;
+        lora_rank = src.lora_rank;
+        temperature = src.temperature;
+        dp = src.dp;
+        wstore = src.wstore;
+        embed = src.embed;
+        final_norm = src.final_norm;
+        inv_freq = src.inv_freq;
+        wq = src.wq;
+        bq = src.bq;
+        wk = src.wk;
+        bk = src.bk;
+        layers = src.layers;
+        max_kp = src.max_kp;
+        packed_widths = src.packed_widths;
+        ld_xn = src.ld_xn;
+        ldp = src.ldp;
+        ldmix = src.ldmix;
+        ldf = src.ldf;
+        layer_slot = src.layer_slot;
+        n_delta = src.n_delta;
+        n_attn = src.n_attn;
+        alloc_handle_state();
     }
 
     void ensure_workspace(int tokens, int rows, int readouts) {
@@ -1241,7 +1298,8 @@ int guarded(hk_model *h, F &&f) {
     }
 }
 
-int create_impl(const std::string &dir, int device, int dtype, int max_context, hk_model **out) {
+int create_impl(const std::string &dir, int device, int dtype, int max_context, hk_model **out,
+                const hk::Model *share = nullptr) {
     *out = nullptr;
     if (dtype != HK_DTYPE_FP32 && dtype != HK_DTYPE_BF16 && dtype != HK_DTYPE_INT8W && dtype != HK_DTYPE_FP16 &&
         dtype != HK_DTYPE_Q8_0 && dtype != HK_DTYPE_Q4_0) {
@@ -1266,7 +1324,10 @@ int create_impl(const std::string &dir, int device, int dtype, int max_context, 
         HK_CUDA(cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking));
         m.dtype = dtype;
         m.max_context = max_context;
-        m.load(dir);
+        if (share)
+            m.share_weights(*share);
+        else
+            m.load(dir);
         HK_CUDA(cudaDeviceSynchronize());
     } catch (const hk::ApiError &e) {
         tl_create_error = e.what();
@@ -1297,7 +1358,14 @@ int hk_create(const char *model_dir, int device, int dtype, int max_context, hk_
 
 int hk_replica(const hk_model *src, int device, hk_model **out) {
     if (!src || !out || !src->m) return HK_ERR_ARGUMENT;
-    return create_impl(src->m->dir, device, src->m->dtype, src->m->max_context, out);
+    const hk::Model &s = *src->m;
+    return create_impl(s.dir, device, s.dtype, s.max_context, out, device == s.device ? &s : nullptr);
+}
+
+uint64_t hk_weight_bytes(const hk_model *h, uint64_t *store_id) {
+    if (!h || !h->m || !h->m->wstore) return 0;
+    if (store_id) *store_id = reinterpret_cast<uint64_t>(h->m->wstore.get());
+    return h->m->wstore->bytes;
 }
 
 int hk_capabilities_get(const hk_model *h, hk_capabilities *out) {

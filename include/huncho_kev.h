@@ -94,9 +94,11 @@ typedef struct hk_capabilities {
 int hk_create(const char *model_dir, int device, int dtype, int max_context, hk_model **out);
 
 /* The same model on `device` (another GPU or the source's own), with fresh
- * mutable state: the package is loaded again, so the new handle holds its own
- * copy of the (identical) weights. Replaces Backend::replica
- * (backend.rs:217-222; qwen3_5.rs:2515-2535). */
+ * mutable state (stream, workspace, caches, KV page setting). On the source's
+ * own GPU the new handle shares the source's weights (one device copy, freed
+ * with the last handle that uses it); on another GPU the package is loaded
+ * again. Handles may run concurrently from different host threads. Replaces
+ * Backend::replica (backend.rs:217-222; qwen3_5.rs:2515-2535). */
 int hk_replica(const hk_model *src, int device, hk_model **out);
 
 /* Replaces Backend::capabilities (qwen3_5.rs:2541-2653). */
@@ -230,6 +232,13 @@ int hk_set_kv_page_tokens(hk_model *m, int page_tokens, uint64_t shuffle_seed);
 
 /* Block until the handle's queued work is done; report a device-side error flag. */
 int hk_synchronize(hk_model *m);
+
+/* Device bytes of the handle's immutable weights, and (if store_id is not
+ * NULL) an identifier of the weight store: handles on the same GPU made by
+ * hk_replica share one store, so they report the same identifier. No
+ * reference counterpart (the reference's replicas share Arc'd weights,
+ * qwen3_5.rs:2515-2535). */
+uint64_t hk_weight_bytes(const hk_model *m, uint64_t *store_id);
 
 /* Number of kernels this handle launched since creation (for launch accounting). */
 uint64_t hk_kernel_launches(const hk_model *m);

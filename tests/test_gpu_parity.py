@@ -245,3 +245,32 @@ def test_kv_page_tokens_validation(tiny_fp32):
     for bad in (8, 48, 512, -16):
         with pytest.raises(BackendError):
             tiny_fp32.with_kv_page_tokens(bad)
+
+
+def test_replica_on_the_same_gpu_shares_weights(native_lib, synth_root):
+    """Backend::replica keeps one copy of the immutable weights per GPU (the
+    reference shares them through Arc clones, qwen3_5.rs:2515-2535): the
+    replica reports the source's weight store, allocates far less than the
+    weights, replays the source bit for bit, and keeps working after the
+    source handle is destroyed."""
+    import torch
+    d = _synth(synth_root, "kev-0.8b-l4", "bf16")
+    b = _backend(d, "bf16", max_context=4096)
+    wl = synth.make_workload(2, b.vocab_size, seed=4, n_requests=3)
+    args = pack_rows(wl.rows, wl.positions)
+    ref = b.score_packed(*args)
+    nbytes, sid = b.weight_store()
+    assert nbytes > 50_000_000
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    r = b.replica()
+    free1, _ = torch.cuda.mem_get_info()
+    assert r.weight_store() == (nbytes, sid)
+    assert free0 - free1 < nbytes // 4, (free0 - free1, nbytes)
+    b.close()
+    assert np.array_equal(r.score_packed(*args), ref)
+    r2 = r.replica()
+    assert r2.weight_store()[1] == sid
+    r.close()
+    assert np.array_equal(r2.score_packed(*args), ref)
+    r2.close()
