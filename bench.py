@@ -424,12 +424,12 @@ def main():
     # scaling), config 5's fixed pool of 4096 requests (strong scaling).
     strong = args.config == 5
     per_gpu = args.requests or {1: 1, 2: 32, 3: 64, 4: 8, 5: 4096}[args.config]
-    pool = synth.make_workload(args.config, synth.SPECS[name]["vocab_size"], seed=args.seed,
-                               n_requests=per_gpu if strong else per_gpu * world)
-    req_tokens = [0] * pool.n_requests
-    for r, row in zip(pool.request_of, pool.rows):
+    req_pool = synth.make_workload(args.config, synth.SPECS[name]["vocab_size"], seed=args.seed,
+                                   n_requests=per_gpu if strong else per_gpu * world)
+    req_tokens = [0] * req_pool.n_requests
+    for r, row in zip(req_pool.request_of, req_pool.rows):
         req_tokens[r] += len(row)
-    wl = subset_workload(pool, shard_by_tokens(req_tokens, world)[rank])
+    wl = subset_workload(req_pool, shard_by_tokens(req_tokens, world)[rank])
     max_len = max(len(r) for r in wl.rows)
     backend = KevBackend(d, device=local, dtype=dtype, max_context=max(8192, max_len))
     if args.config == 4:
@@ -635,9 +635,9 @@ def main():
         lat.append(time.perf_counter() - ts)
 
     # Whole-job totals: the pool every rank scored a share of.
-    reqs = pool.n_requests
-    toks_all = pool.n_tokens
-    rows_all = len(pool.rows)
+    reqs = req_pool.n_requests
+    toks_all = req_pool.n_tokens
+    rows_all = len(req_pool.rows)
     value = reqs * args.steps / dev_total_s
     pk = peaks()
     gemm_ms, gemm_flops, _gemm_bytes, gemm_n = prof["gemm"]

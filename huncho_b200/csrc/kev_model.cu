@@ -319,6 +319,10 @@ struct Mat {
     void *w = nullptr;
     float *scale = nullptr;  // int8-weight models: per row
     int rows = 0, cols = 0, ld = 0;
+    // int8-weight models: the int8 values [rows, ld] (w stays null); each
+    // projection expands them to fp16 in the handle's scratch right before its
+    // GEMM, and the per-row scale is applied in the GEMM epilogue.
+    int8_t *q8 = nullptr;
     // Packed profiles: int8 block values [rows, kp] and fp32 block scales [rows, kp / 32].
     int8_t *q = nullptr;
     float *qd = nullptr;
@@ -390,6 +394,7 @@ struct Model {
     AnswerRec *answers = nullptr;     // [cap_rows]
     int32_t *qtype_dev = nullptr;     // [cap_rows]
     uint32_t *err = nullptr;
+    __half *wdq = nullptr;  // int8-weight models: the projection in flight, expanded to fp16
     // device batch description (see build_meta_kernel)
     int32_t *meta = nullptr;
     size_t meta_cap = 0;
@@ -613,35 +618,38 @@ struct Model {
             float *d = dev_alloc<float>(h.size(), walloc());
             HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
             m.w = d;
+        } else if (dtype == HK_DTYPE_INT8W) {
+            // Symmetric per-output-channel int8: scale = max|w| / 127,
+            // q = rint(w / scale) clamped to [-127, 127]; zero rows get scale 1.
+            std::vector<int8_t> h(static_cast<size_t>(R) * m.ld, 0);
+            std::vector<float> sc(R);
+            for (int r = 0; r < R; ++r) {
+                const float *row = &full[static_cast<size_t>(src_row(r)) * K];
+                int8_t *dst = &h[static_cast<size_t>(r) * m.ld];
+                float amax = 0.0f;
+                for (int i = 0; i < K; ++i) amax = std::max(amax, std::fabs(row[i]));
+                float s = amax / 127.0f;
+                if (s == 0.0f) s = 1.0f;
+                sc[r] = s;
+                for (int i = 0; i < K; ++i) {
+                    float q = std::nearbyint(row[i] / s);
+                    dst[i] = static_cast<int8_t>(std::min(127.0f, std::max(-127.0f, q)));
+                }
+            }
+            m.q8 = dev_alloc<int8_t>(h.size(), walloc());
+            HK_CUDA(cudaMemcpy(m.q8, h.data(), h.size(), cudaMemcpyHostToDevice));
+            m.scale = upload_f32(sc);
         } else {
             std::vector<uint16_t> h(static_cast<size_t>(R) * m.ld, 0);
-            std::vector<float> sc;
-            if (dtype == HK_DTYPE_INT8W) sc.resize(R);
             for (int r = 0; r < R; ++r) {
                 const float *row = &full[static_cast<size_t>(src_row(r)) * K];
                 uint16_t *dst = &h[static_cast<size_t>(r) * m.ld];
-                if (dtype == HK_DTYPE_INT8W) {
-                    // Symmetric per-output-channel int8: scale = max|w| / 127,
-                    // q = rint(w / scale) clamped to [-127, 127]; zero rows get scale 1.
-                    float amax = 0.0f;
-                    for (int i = 0; i < K; ++i) amax = std::max(amax, std::fabs(row[i]));
-                    float s = amax / 127.0f;
-                    if (s == 0.0f) s = 1.0f;
-                    sc[r] = s;
-                    for (int i = 0; i < K; ++i) {
-                        float q = std::nearbyint(row[i] / s);
-                        q = std::min(127.0f, std::max(-127.0f, q));
-                        dst[i] = f32_to_f16_bits(q);  // exact for |q| <= 127
-                    }
-                } else {
-                    // bf16 checkpoint values convert to fp16 exactly unless |w| < 2^-17.
-                    for (int i = 0; i < K; ++i) dst[i] = f32_to_f16_bits(model_round(row[i]));
-                }
+                // bf16 checkpoint values convert to fp16 exactly unless |w| < 2^-17.
+                for (int i = 0; i < K; ++i) dst[i] = f32_to_f16_bits(model_round(row[i]));
             }
             uint16_t *d = dev_alloc<uint16_t>(h.size(), walloc());
             HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
             m.w = d;
-            if (dtype == HK_DTYPE_INT8W) m.scale = upload_f32(sc);
         }
         return m;
     }
@@ -845,6 +853,13 @@ struct Model {
     // The per-handle device state next to the weights: the error word and the
     // cached-batch address table.
     void alloc_handle_state() {
+        if (dtype == HK_DTYPE_INT8W) {
+            size_t most = 0;
+            for (const Layer &L : layers)
+                for (const Mat *m : {&L.mix_in, &L.mix_out, &L.gu, &L.down})
+                    most = std::max(most, static_cast<size_t>(m->rows) * m->ld);
+            wdq = dev_alloc<__half>(most, allocs);
+        }
         err = dev_alloc<uint32_t>(1, allocs);
         HK_CUDA(cudaMemset(err, 0, 4));
         cache_meta = dev_alloc<uint64_t>(4 * layers.size() * HK_MAX_CACHED_ROWS + HK_MAX_CACHED_ROWS, allocs);
@@ -933,6 +948,13 @@ struct Model {
         a.w = W.w;
         a.ldw = W.ld;
         a.scale = W.scale;
+        if (W.q8) {
+            cudaEvent_t dq = prof_begin();
+            const size_t n = static_cast<size_t>(W.rows) * W.ld;
+            launch_expand_i8(W.q8, n, wdq, stream);
+            prof_end(dq, 4, 0.0, 3.0 * n);
+            a.w = wdq;
+        }
         a.out = out;
         a.ldo = ldo;
         a.epilogue = epi;
@@ -950,7 +972,7 @@ struct Model {
         }
         // Algorithmic bytes: the weights, the input rows and the output rows once
         // (a residual output is read and written; SwiGLU writes half the columns).
-        const double wb = W.q ? (W.kp / 32.0) * (32.0 + 4.0) : static_cast<double>(W.cols) * esz();
+        const double wb = W.q ? (W.kp / 32.0) * (32.0 + 4.0) : static_cast<double>(W.cols) * (W.q8 ? 2 : esz());
         const double ob = epi == kEpiResidual ? 8.0 : epi == kEpiStoreF32 ? 4.0 : epi == kEpiSwiGLU ? esz() / 2.0
                                                                                                         : esz();
         prof_end(ev, 0, 2.0 * M * W.rows * W.cols,

@@ -613,6 +613,28 @@ __global__ void swiglu_kernel(const float *__restrict__ gu, int ldg, int n, int 
     }
 }
 
+// ------------------------------------------------------------------ int8 expand
+// 16 int8 values per thread and iteration: one 16-byte load, two 16-byte stores.
+__global__ void expand_i8_kernel(const int8_t *__restrict__ q, size_t n16, __half *__restrict__ out) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int4 v = __ldcs(reinterpret_cast<const int4 *>(q) + i);
+        const int w[4] = {v.x, v.y, v.z, v.w};
+        __align__(16) __half h[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) h[j] = __int2half_rn(static_cast<int8_t>(w[j >> 2] >> (8 * (j & 3))));
+        uint4 *o = reinterpret_cast<uint4 *>(out) + 2 * i;
+        o[0] = *reinterpret_cast<const uint4 *>(&h[0]);
+        o[1] = *reinterpret_cast<const uint4 *>(&h[8]);
+    }
+}
+
+__global__ void expand_i8_tail_kernel(const int8_t *__restrict__ q, size_t from, size_t n, __half *__restrict__ out) {
+    for (size_t i = from + blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        out[i] = __int2half_rn(q[i]);
+}
+
 // ------------------------------------------------------------------ readout
 __global__ void readout_norm_kernel(const float *__restrict__ x, int hidden, const float *__restrict__ w,
                                     float eps, const int32_t *__restrict__ idx, int rows,
@@ -882,6 +904,23 @@ void launch_attention(int act, const AttnArgs &a, cudaStream_t s) {
     else
         attn_simt_kernel<__half><<<grid, 256, 0, s>>>(a);
     HK_LAUNCH_CHECK();
+}
+
+void launch_expand_i8(const int8_t *q, size_t n, __half *out, cudaStream_t s) {
+    if (n == 0) return;
+    const bool aligned = (reinterpret_cast<uintptr_t>(q) % 16) == 0 && (reinterpret_cast<uintptr_t>(out) % 16) == 0;
+    const size_t n16 = aligned ? n / 16 : 0;
+    if (n16) {
+        const size_t blocks = (n16 + 255) / 256;
+        expand_i8_kernel<<<static_cast<int>(blocks < 148 * 8 ? blocks : 148 * 8), 256, 0, s>>>(q, n16, out);
+        HK_LAUNCH_CHECK();
+    }
+    if (n16 * 16 < n) {  // the last n % 16 values, or all of them when unaligned
+        const size_t rest = n - n16 * 16, blocks = (rest + 255) / 256;
+        expand_i8_tail_kernel<<<static_cast<int>(blocks < 148 * 8 ? blocks : 148 * 8), 256, 0, s>>>(q, n16 * 16, n,
+                                                                                                  out);
+        HK_LAUNCH_CHECK();
+    }
 }
 
 void launch_swiglu(int act, const float *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s) {

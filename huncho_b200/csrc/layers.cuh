@@ -175,6 +175,10 @@ void launch_kv_store(int act, const AttnArgs &a, const uint64_t *kv_out, cudaStr
 bool attention_tc_supported(int hd);
 void launch_attention_tc(const AttnArgs &a, cudaStream_t s);
 
+// out[i] = (fp16) q[i] for i < n: int8 weights expanded to fp16 (exact for
+// |q| <= 127) right before the projection that uses them.
+void launch_expand_i8(const int8_t *q, size_t n, __half *out, cudaStream_t s);
+
 // out[t, j] = silu(gu[t, j]) * gu[t, F + j] (qwen3_5.rs:1020-1031); gu fp32.
 void launch_swiglu(int act, const float *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s);
 

@@ -69,15 +69,17 @@ def _case(name):
 
 
 def _compare(name, fx, got_rows, temperature):
-    worst, flips = 0.0, []
+    worst, flips, per_row = 0.0, [], []
     for i, (row, got) in enumerate(zip(fx["rows"], got_rows)):
         pr = calibration.calibrate(np.asarray(row["raw_logits"], np.float32), temperature)
         pg = calibration.calibrate(np.asarray(got, np.float32), temperature)
-        worst = max(worst, float(np.abs(pr - pg).max()))
+        per_row.append(float(np.abs(pr - pg).max()))
+        worst = max(worst, per_row[-1])
         if calibration.argmax(pg.tolist()) != calibration.argmax(pr.tolist()):
             flips.append(i)
     _report({"config": name, "rows": len(fx["rows"]), "worst_abs_prob_err": worst, "gate": TOL[name],
-             "argmax_mismatches": len(flips)})
+             "argmax_mismatches": len(flips), "per_row": [round(e, 7) for e in per_row],
+             "raw_logits": [[float(v) for v in g] for g in got_rows]})
     print(f"{name}: {len(fx['rows'])} rows, worst |dp| {worst:.3g} (gate {TOL[name]}), argmax flips {flips}")
     assert not flips, f"argmax differs from the oracle on rows {flips}"
     assert worst < TOL[name], worst

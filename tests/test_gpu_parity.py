@@ -274,3 +274,21 @@ def test_replica_on_the_same_gpu_shares_weights(native_lib, synth_root):
     r.close()
     assert np.array_equal(r2.score_packed(*args), ref)
     r2.close()
+
+
+def test_int8_weights_take_half_the_projection_bytes(native_lib, synth_root):
+    """The int8 per-channel model keeps its projections as int8 in device
+    memory (plus fp32 per-row scales): on the 0.8B-layout model, whose
+    projections dominate its weights, the store is little more than half of
+    the bf16 model's, and both score the same rows within the half-precision
+    gate of each other."""
+    d = _synth(synth_root, "kev-0.8b-l4", "bf16")
+    h16 = _backend(d, "bf16", max_context=4096)
+    h8 = _backend(d, "int8w", max_context=4096)
+    b16, b8 = h16.weight_store()[0], h8.weight_store()[0]
+    assert b8 < 0.56 * b16, (b8, b16)
+    wl = synth.make_workload(2, h16.vocab_size, seed=5, n_requests=2)
+    args = pack_rows(wl.rows, wl.positions)
+    p16 = calibration.calibrate(h16.score_packed(*args), h16.temperature)
+    p8 = calibration.calibrate(h8.score_packed(*args), h8.temperature)
+    assert np.isfinite(p8).all() and np.abs(p16 - p8).max() < 2e-2
