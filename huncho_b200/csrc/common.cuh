@@ -3,6 +3,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -84,6 +85,12 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x));
 // x -> -inf the denominator overflows and the result is 0, as silu's limit.
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// The low part of a split-precision tensor-core input: the e5m2 rounding of
+// v - float(h), where h = fp16(v) is the high part (GemmArgs::x_lo).
+__device__ __forceinline__ uint8_t lo_e5m2(float v, __half h) {
+    return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v - __half2float(h), __NV_SATFINITE, __NV_E5M2));
+}
 
 inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }
 

@@ -112,6 +112,8 @@ struct PipeArgs {
     float eps;
     __half *mix;
     int ldmix;
+    uint8_t *mix_lo;  // e5m2 low part of the output (split-precision out_proj input), or null
+    int ldmix_lo;
     const uint64_t *state_in, *state_out;  // per row [nv][128][128] fp32, or 0
     const uint64_t *hist_in;               // per row [3][conv_dim] fp32, or 0
 };
@@ -284,7 +286,11 @@ __global__ void __launch_bounds__(THREADS, 1) delta_pipe_kernel(PipeArgs a) {
                     const float2 zz = zr[hf][nt];
                     const float y0 = (__fdividef(o[nt][2 * hf], denom) * nwr[nt][0]) * silu_fast(zz.x);
                     const float y1 = (__fdividef(o[nt][2 * hf + 1], denom) * nwr[nt][1]) * silu_fast(zz.y);
-                    *reinterpret_cast<__half2 *>(a.mix + tok * a.ldmix + h * D + c) = __floats2half2_rn(y0, y1);
+                    const __half2 yh = __floats2half2_rn(y0, y1);
+                    *reinterpret_cast<__half2 *>(a.mix + tok * a.ldmix + h * D + c) = yh;
+                    if (a.mix_lo)
+                        *reinterpret_cast<uint16_t *>(a.mix_lo + tok * a.ldmix_lo + h * D + c) =
+                            static_cast<uint16_t>(lo_e5m2(y0, __low2half(yh)) | (lo_e5m2(y1, __high2half(yh)) << 8));
                 }
             }
             // ---- S = gam_C S + Kd^T D (D hi + lo).
@@ -624,7 +630,7 @@ bool delta_pipe_supported(const DeltaRecArgs &r, const DeltaFusedInput &in) {
 }
 
 void launch_delta_pipe(const DeltaRecArgs &r, const DeltaFusedInput &in, const float *norm_w, float eps, __half *mix,
-                       int ldmix, cudaStream_t s) {
+                       int ldmix, cudaStream_t s, uint8_t *mix_lo, int ldmix_lo) {
     if (r.n_rows <= 0) return;
     PipeArgs a;
     a.proj = in.proj;
@@ -643,6 +649,8 @@ void launch_delta_pipe(const DeltaRecArgs &r, const DeltaFusedInput &in, const f
     a.eps = eps;
     a.mix = mix;
     a.ldmix = ldmix;
+    a.mix_lo = mix_lo;
+    a.ldmix_lo = ldmix_lo;
     a.state_in = r.state_in;
     a.state_out = r.state_out;
     a.hist_in = in.hist_in;

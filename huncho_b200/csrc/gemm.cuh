@@ -30,6 +30,19 @@ struct GemmArgs {
     int ldo = 0;
     int epilogue = kEpiStore;
     uint32_t *err = nullptr;
+    // Split-precision input (tensor-core path): x holds fp16(x_true) and x_lo
+    // the e5m2 rounding of x_true - fp16(x_true) [M, ldx_lo bytes]; w8 is an
+    // e4m3 copy of W [N, ldw8 bytes]. The accumulator then also receives
+    // x_lo * w8^T (kind::f8f6f4 MMAs), which restores ~3 more bits of the
+    // input: Y = W x_hi + W8 x_lo.
+    const uint8_t *x_lo = nullptr;
+    int ldx_lo = 0;
+    const uint8_t *w8 = nullptr;
+    int ldw8 = 0;
+    // SwiGLU epilogue: the e5m2 residual of the fp16 output (the next
+    // projection's x_lo), [M, ldo_lo bytes]; null = not written.
+    uint8_t *out_lo = nullptr;
+    int ldo_lo = 0;
 };
 
 // fp16 X and W on tcgen05 tensor cores (TMA-fed, TMEM accumulators), fp32 accumulation.

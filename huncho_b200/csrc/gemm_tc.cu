@@ -45,6 +45,9 @@ constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + EPI_BYTES 
 struct TcParams {
     int M, N, K;
     int m_tiles, n_tiles, k_blocks;
+    int k_blocks_lo;  // split-precision input: 128-wide K blocks of x_lo / w8 after the fp16 ones (0 = none)
+    uint8_t *out_lo;  // SwiGLU: e5m2 residual of the fp16 output, or null
+    int ldo_lo;
     int n_fast;  // tile order: N fastest (narrow N: the N tiles of one M tile run together, X read once)
     void *out;
     int ldo;
@@ -66,7 +69,9 @@ template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                         const __grid_constant__ CUtensorMap tm_w,
-                        const __grid_constant__ CUtensorMap tm_o, TcParams p) {
+                        const __grid_constant__ CUtensorMap tm_o,
+                        const __grid_constant__ CUtensorMap tm_xl,
+                        const __grid_constant__ CUtensorMap tm_wl, TcParams p) {
     using namespace sm100;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -121,15 +126,24 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
                 const int m_blk = p.n_fast ? tile / p.n_tiles : tile % p.m_tiles;
                 const int n_blk = p.n_fast ? tile % p.n_tiles : tile / p.m_tiles;
-                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                for (int kb = 0; kb < p.k_blocks + p.k_blocks_lo; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1)) {
                         set_error(p.err, kErrWaitTimeout);
                         *abort_flag = 1;
                         break;
                     }
+                    // fp16 blocks: 64 K columns = 128 bytes per row; then the
+                    // 8-bit low-part blocks: 128 K columns = 128 bytes per row
+                    // (the same stage geometry).
                     mbar_expect_tx(&full[stage], A_STAGE_BYTES + B_STAGE_BYTES);
-                    tma_load_2d(sA + stage * A_STAGE_BYTES, &tm_x, &full[stage], kb * BK, m_blk * BM);
-                    tma_load_2d(sB + stage * B_STAGE_BYTES, &tm_w, &full[stage], kb * BK, n_blk * BN);
+                    if (kb < p.k_blocks) {
+                        tma_load_2d(sA + stage * A_STAGE_BYTES, &tm_x, &full[stage], kb * BK, m_blk * BM);
+                        tma_load_2d(sB + stage * B_STAGE_BYTES, &tm_w, &full[stage], kb * BK, n_blk * BN);
+                    } else {
+                        const int kl = (kb - p.k_blocks) * 128;
+                        tma_load_2d(sA + stage * A_STAGE_BYTES, &tm_xl, &full[stage], kl, m_blk * BM);
+                        tma_load_2d(sB + stage * B_STAGE_BYTES, &tm_wl, &full[stage], kl, n_blk * BN);
+                    }
                     issued_mask |= 1u << stage;
                     issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
@@ -148,6 +162,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             // ------------------------------------------------ MMA issuer
             constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
+            constexpr uint32_t idesc8 = idesc_e5m2_e4m3_f32(BM, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -160,7 +175,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                for (int kb = 0; kb < p.k_blocks + p.k_blocks_lo; ++kb) {
                     if (!mbar_wait(&full[stage], phase)) {
                         set_error(p.err, kErrWaitTimeout);
                         *abort_flag = 1;
@@ -169,10 +184,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tc_fence_after();
                     const uint32_t a0 = smem_addr(sA + stage * A_STAGE_BYTES);
                     const uint32_t b0 = smem_addr(sB + stage * B_STAGE_BYTES);
+                    if (kb < p.k_blocks) {
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k) {
-                        mma_f16(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32),
-                                 idesc, (kb | k) != 0);
+                        for (int k = 0; k < BK / 16; ++k)
+                            mma_f16(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32), idesc,
+                                    (kb | k) != 0);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)  // 4 x K=32 8-bit steps per 128-byte row
+                            mma_f8(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32), idesc8, 1u);
                     }
                     mma_commit(&empty[stage]);
                     if (++stage == STAGES) {
@@ -251,11 +271,25 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 u[i] *= __ldg(p.scale + wcol + BN / 2 + i);
                             }
                         }
+                        uint32_t lo[8];
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
-                            __half2 h2 = __floats2half2_rn(silu_fast(g[2 * i]) * u[2 * i],
-                                                           silu_fast(g[2 * i + 1]) * u[2 * i + 1]);
+                            const float y0 = silu_fast(g[2 * i]) * u[2 * i], y1 = silu_fast(g[2 * i + 1]) * u[2 * i + 1];
+                            __half2 h2 = __floats2half2_rn(y0, y1);
                             packed[16 * hh + i] = *reinterpret_cast<uint32_t *>(&h2);
+                            const uint32_t l2 = static_cast<uint32_t>(lo_e5m2(y0, __low2half(h2))) |
+                                                (static_cast<uint32_t>(lo_e5m2(y1, __high2half(h2))) << 8);
+                            if (i & 1)
+                                lo[i >> 1] |= l2 << 16;
+                            else
+                                lo[i >> 1] = l2;
+                        }
+                        if (p.out_lo && row_ok) {
+                            // The next projection's low part: 32 bytes of e5m2 per row and half round.
+                            uint4 *dl = reinterpret_cast<uint4 *>(p.out_lo + static_cast<size_t>(row) * p.ldo_lo +
+                                                                  n_blk * (BN / 2) + c + 32 * hh);
+                            dl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                            dl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
                         }
                     }
                     const int ocol = n_blk * (BN / 2) + c;
@@ -377,7 +411,9 @@ template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_f16_tc2_kernel(const __grid_constant__ CUtensorMap tm_x,
                          const __grid_constant__ CUtensorMap tm_w,
-                         const __grid_constant__ CUtensorMap tm_o, TcParams p) {
+                         const __grid_constant__ CUtensorMap tm_o,
+                         const __grid_constant__ CUtensorMap tm_xl,
+                         const __grid_constant__ CUtensorMap tm_wl, TcParams p) {
     using namespace sm100;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -434,7 +470,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int tile = pair; tile < num_tiles && !*abort_flag; tile += n_pairs) {
                 const int m_blk = p.n_fast ? tile / p.n_tiles : tile % p.m_tiles;
                 const int n_blk = p.n_fast ? tile % p.n_tiles : tile / p.m_tiles;
-                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                for (int kb = 0; kb < p.k_blocks + p.k_blocks_lo; ++kb) {
                     if (!mbar_wait_cluster(&empty[stage], phase ^ 1)) {
                         set_error(p.err, kErrWaitTimeout);
                         *abort_flag = 1;
@@ -442,9 +478,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     const uint32_t bar0 = mapa_shared(smem_addr(&full[stage]), 0);
                     if (rank == 0) mbar_expect_tx(&full[stage], 2 * (P_A_BYTES + P_B_BYTES));
-                    tma_load_2d_pair(sA + stage * P_A_BYTES, &tm_x, bar0, kb * BK,
+                    const bool hi = kb < p.k_blocks;
+                    const int kx = hi ? kb * BK : (kb - p.k_blocks) * 128;
+                    tma_load_2d_pair(sA + stage * P_A_BYTES, hi ? &tm_x : &tm_xl, bar0, kx,
                                      m_blk * (2 * BM) + static_cast<int>(rank) * BM);
-                    tma_load_2d_pair(sB + stage * P_B_BYTES, &tm_w, bar0, kb * BK,
+                    tma_load_2d_pair(sB + stage * P_B_BYTES, hi ? &tm_w : &tm_wl, bar0, kx,
                                      n_blk * BN + static_cast<int>(rank) * BM);
                     ++issued;
                     if (++stage == P_STAGES) {
@@ -471,6 +509,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0 && rank == 0) {
             // ------------------------------------------------ MMA issuer (first CTA)
             constexpr uint32_t idesc = idesc_f16_f32(2 * BM, BN);
+            constexpr uint32_t idesc8 = idesc_e5m2_e4m3_f32(2 * BM, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -484,7 +523,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                for (int kb = 0; kb < p.k_blocks + p.k_blocks_lo; ++kb) {
                     if (!mbar_wait_cluster(&full[stage], phase)) {
                         set_error(p.err, kErrWaitTimeout);
                         *abort_flag = 1;
@@ -493,10 +532,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tc_fence_after();
                     const uint32_t a0 = smem_addr(sA + stage * P_A_BYTES);
                     const uint32_t b0 = smem_addr(sB + stage * P_B_BYTES);
+                    if (kb < p.k_blocks) {
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k)
-                        mma_f16_pair(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32), idesc,
-                                     (kb | k) != 0);
+                        for (int k = 0; k < BK / 16; ++k)
+                            mma_f16_pair(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32),
+                                         idesc, (kb | k) != 0);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            mma_f8_pair(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32),
+                                        idesc8, 1u);
+                    }
                     mma_commit_pair(smem_addr(&empty[stage]));
                     mma_commit_pair(mapa_shared(smem_addr(&empty[stage]), peer));
                     if (++stage == P_STAGES) {
@@ -575,11 +621,25 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 u[i] *= __ldg(p.scale + wcol + BN / 2 + i);
                             }
                         }
+                        uint32_t lo[8];
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
-                            __half2 h2 = __floats2half2_rn(silu_fast(g[2 * i]) * u[2 * i],
-                                                           silu_fast(g[2 * i + 1]) * u[2 * i + 1]);
+                            const float y0 = silu_fast(g[2 * i]) * u[2 * i], y1 = silu_fast(g[2 * i + 1]) * u[2 * i + 1];
+                            __half2 h2 = __floats2half2_rn(y0, y1);
                             packed[16 * hh + i] = *reinterpret_cast<uint32_t *>(&h2);
+                            const uint32_t l2 = static_cast<uint32_t>(lo_e5m2(y0, __low2half(h2))) |
+                                                (static_cast<uint32_t>(lo_e5m2(y1, __high2half(h2))) << 8);
+                            if (i & 1)
+                                lo[i >> 1] |= l2 << 16;
+                            else
+                                lo[i >> 1] = l2;
+                        }
+                        if (p.out_lo && row_ok) {
+                            // The next projection's low part: 32 bytes of e5m2 per row and half round.
+                            uint4 *dl = reinterpret_cast<uint4 *>(p.out_lo + static_cast<size_t>(row) * p.ldo_lo +
+                                                                  n_blk * (BN / 2) + c + 32 * hh);
+                            dl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                            dl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
                         }
                     }
                     const int ocol = n_blk * (BN / 2) + c;
@@ -720,6 +780,42 @@ CUtensorMap make_map(const void *base, int rows, int inner, int ld, int box_rows
     return m;
 }
 
+// A 2-D 8-bit tensor map (the low-part operands x_lo / w8) over rows x inner
+// bytes (row stride ld bytes), box of box_rows x 128 bytes, zero fill.
+CUtensorMap make_map8(const void *base, int rows, int inner, int ld, int box_rows) {
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || ld % 16)
+        throw CudaError("8-bit GEMM operand must be 16-byte aligned with a row stride % 16 == 0");
+    CUtensorMap m;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+    cuuint32_t box[2] = {128, static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box,
+                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled (8-bit) failed: " + std::to_string(r));
+    return m;
+}
+
+// The split-precision fields of the launch: low-part maps and block count
+// (zeroed maps and no blocks without a low part), the SwiGLU low output.
+void set_split(const GemmArgs &a, int w_box_rows, TcParams &p, CUtensorMap &txl, CUtensorMap &twl) {
+    std::memset(&txl, 0, sizeof(txl));
+    std::memset(&twl, 0, sizeof(twl));
+    p.k_blocks_lo = 0;
+    if (a.x_lo && a.w8) {
+        txl = make_map8(a.x_lo, a.M, a.K, a.ldx_lo, BM);
+        twl = make_map8(a.w8, a.N, a.K, a.ldw8, w_box_rows);
+        p.k_blocks_lo = ceil_div(a.K, 128);
+    } else if (a.x_lo || a.w8) {
+        throw CudaError("a split-precision GEMM needs both x_lo and w8");
+    }
+    p.out_lo = a.epilogue == kEpiSwiGLU ? a.out_lo : nullptr;
+    p.ldo_lo = a.ldo_lo;
+    if (p.out_lo && ((reinterpret_cast<uintptr_t>(p.out_lo) & 15) || p.ldo_lo % 16))
+        throw CudaError("SwiGLU low-part output must be 16-byte aligned with a row stride % 16 == 0");
+}
+
 // Output tensor map for the epilogue's TMA stores: box of 32 rows x 128 bytes
 // (32 fp32 or 64 fp16 columns), 128B swizzle. Returns false when the output
 // does not meet TMA's alignment rules (the epilogue then stores directly).
@@ -744,6 +840,8 @@ void launch(const GemmArgs &a, cudaStream_t s, int num_sms) {
     CUtensorMap tx = make_map(a.x, a.M, a.K, a.ldx, BM);
     CUtensorMap tw = make_map(a.w, a.N, a.K, a.ldw, BN);
     TcParams p;
+    CUtensorMap txl, twl;
+    set_split(a, BN, p, txl, twl);
     p.M = a.M;
     p.N = a.N;
     p.K = a.K;
@@ -764,7 +862,7 @@ void launch(const GemmArgs &a, cudaStream_t s, int num_sms) {
     p.tma_out = make_out_map(to, a.out, a.M, out_cols, a.ldo, f32) ? 1 : 0;
     const int tiles = p.m_tiles * p.n_tiles;
     const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_f16_tc_kernel<EPI><<<grid, THREADS, SMEM_BYTES, s>>>(tx, tw, to, p);
+    gemm_f16_tc_kernel<EPI><<<grid, THREADS, SMEM_BYTES, s>>>(tx, tw, to, txl, twl, p);
     HK_LAUNCH_CHECK();
 }
 
@@ -775,6 +873,8 @@ void launch_pair(const GemmArgs &a, cudaStream_t s, int num_sms) {
     CUtensorMap tx = make_map(a.x, a.M, a.K, a.ldx, BM);
     CUtensorMap tw = make_map(a.w, a.N, a.K, a.ldw, BM);  // each CTA loads 128 rows of W
     TcParams p;
+    CUtensorMap txl, twl;
+    set_split(a, BM, p, txl, twl);
     p.M = a.M;
     p.N = a.N;
     p.K = a.K;
@@ -807,7 +907,7 @@ void launch_pair(const GemmArgs &a, cudaStream_t s, int num_sms) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    HK_CUDA(cudaLaunchKernelEx(&cfg, gemm_f16_tc2_kernel<EPI>, tx, tw, to, p));
+    HK_CUDA(cudaLaunchKernelEx(&cfg, gemm_f16_tc2_kernel<EPI>, tx, tw, to, txl, twl, p));
     HK_LAUNCH_CHECK();
 }
 

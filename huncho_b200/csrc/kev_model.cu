@@ -323,6 +323,12 @@ struct Mat {
     // projection expands them to fp16 in the handle's scratch right before its
     // GEMM, and the per-row scale is applied in the GEMM epilogue.
     int8_t *q8 = nullptr;
+    // Split-precision projections (the delta layers' and the MLPs' in the
+    // half-precision models): an e4m3 copy of the weight values [rows, ld8
+    // bytes] for the low part of the input (GemmArgs::w8); for int8 weights,
+    // of the int8 values (the row scale applies to both parts).
+    uint8_t *w8 = nullptr;
+    int ld8 = 0;
     // Packed profiles: int8 block values [rows, kp] and fp32 block scales [rows, kp / 32].
     int8_t *q = nullptr;
     float *qd = nullptr;
@@ -381,6 +387,10 @@ struct Model {
     std::vector<void *> ws;
     float *x = nullptr;
     void *xn = nullptr, *mix = nullptr, *ffn = nullptr;
+    // e5m2 low parts of xn / mix / ffn for split-precision projections (rows of
+    // ld_xl / ld_mixl / ld_fl bytes), or null.
+    uint8_t *xn_lo = nullptr, *mix_lo = nullptr, *ffn_lo = nullptr;
+    int ld_xl = 0, ld_mixl = 0, ld_fl = 0;
     float *proj = nullptr;  // projection outputs, always fp32
     float *dq = nullptr, *dkk = nullptr, *dvv = nullptr, *dg = nullptr, *db = nullptr, *dout = nullptr;
     void *aq = nullptr, *ak = nullptr, *av = nullptr;
@@ -395,6 +405,7 @@ struct Model {
     int32_t *qtype_dev = nullptr;     // [cap_rows]
     uint32_t *err = nullptr;
     __half *wdq = nullptr;  // int8-weight models: the projection in flight, expanded to fp16
+    uint8_t *wdq8 = nullptr;  // ... and to e4m3 (the split-precision low part's weights)
     // device batch description (see build_meta_kernel)
     int32_t *meta = nullptr;
     size_t meta_cap = 0;
@@ -543,6 +554,13 @@ struct Model {
     }
 
     bool packed() const { return dtype == HK_DTYPE_Q8_0 || dtype == HK_DTYPE_Q4_0; }
+    // Half-precision models run the delta layers' and the MLPs' projections
+    // with split-precision inputs (fp16 high part + e5m2 low part, see
+    // GemmArgs::x_lo): fp16 rounding of those inputs alone moves calibrated
+    // probabilities of the 0.8B / 4B models by up to 2-4e-3 against the fp32
+    // reference; the low part brings it under 3e-4. The attention layers'
+    // projections are insensitive (< 3e-5) and stay fp16.
+    bool split_inputs() const { return dtype == HK_DTYPE_BF16 || dtype == HK_DTYPE_FP16 || dtype == HK_DTYPE_INT8W; }
     // The fp32 model path: fp32 weights, or the packed profiles (fp32 activations).
     bool f32_model() const { return dtype == HK_DTYPE_FP32 || packed(); }
     int act() const { return f32_model() ? kActF32 : kActF16; }
@@ -594,8 +612,21 @@ struct Model {
 
     // Pack row blocks [(tensor, rows)] into one [R, K] matrix in the model's
     // weight format. `order` optionally permutes output rows (SwiGLU interleave).
+    // The e4m3 copy of a projection for split-precision inputs: vals [R][K]
+    // (row-major, the values the fp16 operand holds), rows padded to 16 bytes.
+    void make_w8(Mat &m, const std::vector<float> &vals, int R, int K) {
+        m.ld8 = round_up(K, 16);
+        std::vector<uint8_t> h(static_cast<size_t>(R) * m.ld8, 0);
+        for (int r = 0; r < R; ++r)
+            for (int i = 0; i < K; ++i)
+                h[static_cast<size_t>(r) * m.ld8 + i] = static_cast<uint8_t>(
+                    __nv_cvt_float_to_fp8(vals[static_cast<size_t>(r) * K + i], __NV_SATFINITE, __NV_E4M3));
+        m.w8 = dev_alloc<uint8_t>(h.size(), walloc());
+        HK_CUDA(cudaMemcpy(m.w8, h.data(), h.size(), cudaMemcpyHostToDevice));
+    }
+
     Mat pack(const WeightSource &src, const std::vector<std::pair<std::string, int>> &parts, int K,
-             const std::vector<int> *order = nullptr) {
+             const std::vector<int> *order = nullptr, bool split = false) {
         if (packed()) return pack_blocks(src, parts, K);
         int R = 0;
         for (auto &p : parts) R += p.second;
@@ -619,6 +650,7 @@ struct Model {
             HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
             m.w = d;
         } else if (dtype == HK_DTYPE_INT8W) {
+            m.ld = round_up(K, 16);  // the int8 rows double as the e4m3 rows' layout
             // Symmetric per-output-channel int8: scale = max|w| / 127,
             // q = rint(w / scale) clamped to [-127, 127]; zero rows get scale 1.
             std::vector<int8_t> h(static_cast<size_t>(R) * m.ld, 0);
@@ -639,6 +671,9 @@ struct Model {
             m.q8 = dev_alloc<int8_t>(h.size(), walloc());
             HK_CUDA(cudaMemcpy(m.q8, h.data(), h.size(), cudaMemcpyHostToDevice));
             m.scale = upload_f32(sc);
+            // The e4m3 copy for split-precision inputs is expanded per
+            // projection with the fp16 values, so device memory holds int8 only.
+            if (split) m.ld8 = m.ld;
         } else {
             std::vector<uint16_t> h(static_cast<size_t>(R) * m.ld, 0);
             for (int r = 0; r < R; ++r) {
@@ -650,6 +685,13 @@ struct Model {
             uint16_t *d = dev_alloc<uint16_t>(h.size(), walloc());
             HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
             m.w = d;
+            if (split) {
+                std::vector<float> vals(static_cast<size_t>(R) * K);
+                for (int r = 0; r < R; ++r)
+                    for (int i = 0; i < K; ++i)
+                        vals[static_cast<size_t>(r) * K + i] = f16_bits_to_f32(h[static_cast<size_t>(r) * m.ld + i]);
+                make_w8(m, vals, R, K);
+            }
         }
         return m;
     }
@@ -817,8 +859,8 @@ struct Model {
                 const std::string a = p + ".linear_attn";
                 L.mix_in = pack(src, {{a + ".in_proj_qkv.weight", c.conv_dim()}, {a + ".in_proj_z.weight", c.value_dim()},
                                       {a + ".in_proj_b.weight", c.nv}, {a + ".in_proj_a.weight", c.nv}},
-                                c.hidden);
-                L.mix_out = pack(src, {{a + ".out_proj.weight", c.hidden}}, c.value_dim());
+                                c.hidden, nullptr, split_inputs());
+                L.mix_out = pack(src, {{a + ".out_proj.weight", c.hidden}}, c.value_dim(), nullptr, split_inputs());
                 L.conv_w = upload_f32(small(src, a + ".conv1d.weight", {c.conv_dim(), 1, c.taps}));
                 std::vector<float> alog = small(src, a + ".A_log", {c.nv});
                 for (auto &v : alog) v = -std::exp(v);  // base_g = -exp(A_log), qwen3_5.rs:800
@@ -836,8 +878,8 @@ struct Model {
             }
             const std::string m = p + ".mlp";
             L.gu = pack(src, {{m + ".gate_proj.weight", c.ffn}, {m + ".up_proj.weight", c.ffn}}, c.hidden,
-                        fused_swiglu ? &gu_order : nullptr);
-            L.down = pack(src, {{m + ".down_proj.weight", c.hidden}}, c.ffn);
+                        fused_swiglu ? &gu_order : nullptr, split_inputs());
+            L.down = pack(src, {{m + ".down_proj.weight", c.hidden}}, c.ffn, nullptr, split_inputs());
             layers.push_back(L);
         }
         ld_xn = round_up(c.hidden, 8);
@@ -859,6 +901,7 @@ struct Model {
                 for (const Mat *m : {&L.mix_in, &L.mix_out, &L.gu, &L.down})
                     most = std::max(most, static_cast<size_t>(m->rows) * m->ld);
             wdq = dev_alloc<__half>(most, allocs);
+            wdq8 = dev_alloc<uint8_t>(most, allocs);
         }
         err = dev_alloc<uint32_t>(1, allocs);
         HK_CUDA(cudaMemset(err, 0, 4));
@@ -910,6 +953,14 @@ struct Model {
         proj = dev_alloc<float>(N * ldp, ws);
         mix = dev_alloc<uint8_t>(N * ldmix * e, ws);
         ffn = dev_alloc<uint8_t>(N * ldf * e, ws);
+        if (split_inputs()) {
+            ld_xl = round_up(c.hidden, 16);
+            ld_mixl = round_up(ldmix, 16);
+            ld_fl = round_up(ldf, 16);
+            xn_lo = dev_alloc<uint8_t>(N * ld_xl, ws);
+            mix_lo = dev_alloc<uint8_t>(N * ld_mixl, ws);
+            ffn_lo = dev_alloc<uint8_t>(N * ld_fl, ws);
+        }
         HK_CUDA(cudaMemset(xn, 0, N * ld_xn * e));
         HK_CUDA(cudaMemset(mix, 0, N * ldmix * e));
         HK_CUDA(cudaMemset(ffn, 0, N * ldf * e));
@@ -938,7 +989,10 @@ struct Model {
         meta = dev_alloc<int32_t>(meta_cap, ws);
     }
 
-    void gemm(const Mat &W, const void *xin, int ldx, int M, void *out, int ldo, int epi) {
+    // xlo (with the weight's e4m3 copy) adds the low part of a split-precision
+    // input; out_lo receives a SwiGLU output's low part.
+    void gemm(const Mat &W, const void *xin, int ldx, int M, void *out, int ldo, int epi,
+              const uint8_t *xlo = nullptr, int ldxl = 0, uint8_t *out_lo = nullptr, int ldol = 0) {
         GemmArgs a;
         a.M = M;
         a.N = W.rows;
@@ -948,12 +1002,27 @@ struct Model {
         a.w = W.w;
         a.ldw = W.ld;
         a.scale = W.scale;
+        if (W.w8 && xlo) {
+            a.x_lo = xlo;
+            a.ldx_lo = ldxl;
+            a.w8 = W.w8;
+            a.ldw8 = W.ld8;
+        }
+        a.out_lo = out_lo;
+        a.ldo_lo = ldol;
         if (W.q8) {
             cudaEvent_t dq = prof_begin();
             const size_t n = static_cast<size_t>(W.rows) * W.ld;
-            launch_expand_i8(W.q8, n, wdq, stream);
-            prof_end(dq, 4, 0.0, 3.0 * n);
+            const bool lo = W.ld8 && xlo;
+            launch_expand_i8(W.q8, n, wdq, lo ? wdq8 : nullptr, stream);
+            prof_end(dq, 4, 0.0, (lo ? 4.0 : 3.0) * n);
             a.w = wdq;
+            if (lo) {
+                a.x_lo = xlo;
+                a.ldx_lo = ldxl;
+                a.w8 = wdq8;
+                a.ldw8 = W.ld8;
+            }
         }
         a.out = out;
         a.ldo = ldo;
@@ -972,11 +1041,13 @@ struct Model {
         }
         // Algorithmic bytes: the weights, the input rows and the output rows once
         // (a residual output is read and written; SwiGLU writes half the columns).
-        const double wb = W.q ? (W.kp / 32.0) * (32.0 + 4.0) : static_cast<double>(W.cols) * (W.q8 ? 2 : esz());
+        const double wb = (W.q ? (W.kp / 32.0) * (32.0 + 4.0) : static_cast<double>(W.cols) * (W.q8 ? 2 : esz())) +
+                          (a.w8 ? static_cast<double>(W.cols) : 0.0);
         const double ob = epi == kEpiResidual ? 8.0 : epi == kEpiStoreF32 ? 4.0 : epi == kEpiSwiGLU ? esz() / 2.0
                                                                                                         : esz();
         prof_end(ev, 0, 2.0 * M * W.rows * W.cols,
-                 W.rows * wb + static_cast<double>(M) * W.cols * esz() + static_cast<double>(M) * W.rows * ob);
+                 W.rows * wb + static_cast<double>(M) * W.cols * (esz() + (a.x_lo ? 1 : 0)) +
+                     static_cast<double>(M) * W.rows * ob);
     }
 
     // Algorithmic FLOPs of the chunked delta rule (chunk 32) for n tokens of one layer.
@@ -1015,12 +1086,13 @@ struct Model {
             const uint64_t *out_a = cr ? at_layer(cr->out_a, li) : nullptr;
             const uint64_t *out_b = cr ? at_layer(cr->out_b, li) : nullptr;
             ev = prof_begin();
-            launch_rmsnorm(A, x, c.hidden, L.in_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream);
+            launch_rmsnorm(A, x, c.hidden, L.in_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream,
+                           L.full ? nullptr : xn_lo, ld_xl);
             prof_end(ev, 5, 0.0, norm_bytes);
             // Half-precision models: the warp-specialised delta layer kernel.
             const bool pipe = !L.full && !f32_model() && c.dk == 128 && c.dv == 128 && c.taps == 4 &&
                               c.nk > 0 && c.nv % c.nk == 0 && (ldp % 4) == 0 && (c.conv_dim() % 4) == 0;
-            gemm(L.mix_in, xn, ld_xn, n_tok, proj, ldp, kEpiStoreF32);
+            gemm(L.mix_in, xn, ld_xn, n_tok, proj, ldp, kEpiStoreF32, L.full ? nullptr : xn_lo, ld_xl);
             if (pipe) {
                 if (out_b)
                     launch_conv_history(proj, ldp, c.conv_dim(), c.taps, cu_seqlens, n_rows, in_b, out_b, stream);
@@ -1045,7 +1117,7 @@ struct Model {
                 in.dt_bias = L.dt_bias;
                 in.hist_in = in_b;
                 ev = prof_begin();
-                launch_delta_pipe(r, in, L.gnorm_w, c.eps, static_cast<__half *>(mix), ldmix, stream);
+                launch_delta_pipe(r, in, L.gnorm_w, c.eps, static_cast<__half *>(mix), ldmix, stream, mix_lo, ld_mixl);
                 // Reads each token's q | k | v | z | b | a projection row (fp32), writes its
                 // gated-norm output (fp16).
                 prof_end(ev, 1, delta_chunk_flops(n_tok, c),
@@ -1103,7 +1175,7 @@ struct Model {
                          static_cast<double>(n_tok) * (c.conv_dim() + 2.0 * c.nv + c.value_dim()) * 4.0);
                 ev = prof_begin();
                 launch_gated_norm(A, dout, proj + c.conv_dim(), ldp, L.gnorm_w, c.eps, n_tok, c.nv, c.dv, mix, ldmix,
-                                  stream);
+                                  stream, mix_lo, ld_mixl);
                 prof_end(ev, 4, 0.0, static_cast<double>(n_tok) * c.value_dim() * (8.0 + e));
             } else {
                 AttnPrepArgs p;
@@ -1158,19 +1230,19 @@ struct Model {
                 prof_end(ev, 2, 4.0 * c.hd * c.nh * attn_pairs,
                          static_cast<double>(n_tok) * ((c.nh + 2.0 * c.nkv) * c.hd * e + c.nh * c.hd * (4.0 + e)));
             }
-            gemm(L.mix_out, mix, ldmix, n_tok, x, c.hidden, kEpiResidual);
+            gemm(L.mix_out, mix, ldmix, n_tok, x, c.hidden, kEpiResidual, L.full ? nullptr : mix_lo, ld_mixl);
             ev = prof_begin();
-            launch_rmsnorm(A, x, c.hidden, L.post_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream);
+            launch_rmsnorm(A, x, c.hidden, L.post_norm, c.eps, n_tok, c.hidden, xn, ld_xn, stream, xn_lo, ld_xl);
             prof_end(ev, 5, 0.0, norm_bytes);
             if (fused_swiglu) {
-                gemm(L.gu, xn, ld_xn, n_tok, ffn, ldf, kEpiSwiGLU);
+                gemm(L.gu, xn, ld_xn, n_tok, ffn, ldf, kEpiSwiGLU, xn_lo, ld_xl, ffn_lo, ld_fl);
             } else {
-                gemm(L.gu, xn, ld_xn, n_tok, proj, ldp, kEpiStoreF32);
+                gemm(L.gu, xn, ld_xn, n_tok, proj, ldp, kEpiStoreF32, xn_lo, ld_xl);
                 ev = prof_begin();
-                launch_swiglu(A, proj, ldp, n_tok, c.ffn, ffn, ldf, stream);
+                launch_swiglu(A, proj, ldp, n_tok, c.ffn, ffn, ldf, stream, ffn_lo, ld_fl);
                 prof_end(ev, 4, 0.0, static_cast<double>(n_tok) * c.ffn * (8.0 + e));
             }
-            gemm(L.down, ffn, ldf, n_tok, x, c.hidden, kEpiResidual);
+            gemm(L.down, ffn, ldf, n_tok, x, c.hidden, kEpiResidual, ffn_lo, ld_fl);
         }
         ReadoutArgs ro;
         ro.x = x;

@@ -28,7 +28,8 @@ __global__ void embed_kernel(const uint32_t *__restrict__ ids, int n, const TW *
 // One warp per row; division by sqrt(mean(x^2) + eps) as the reference writes it.
 template <typename T>
 __global__ void rmsnorm_kernel(const float *__restrict__ x, int ldx, const float *__restrict__ w,
-                               float eps, int rows, int hidden, T *__restrict__ out, int ldo) {
+                               float eps, int rows, int hidden, T *__restrict__ out, int ldo,
+                               uint8_t *__restrict__ out_lo, int ldo_lo) {
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -45,14 +46,21 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, int ldx, const float
     }
     ss = warp_sum(ss);
     const float denom = sqrtf(ss / static_cast<float>(hidden) + eps);
-    for (int i = lane; i < hidden; i += 32) o[i] = Act<T>::from_f((xr[i] / denom) * w[i]);
+    for (int i = lane; i < hidden; i += 32) {
+        const float y = (xr[i] / denom) * w[i];
+        o[i] = Act<T>::from_f(y);
+        if constexpr (sizeof(T) == 2) {
+            if (out_lo) out_lo[static_cast<size_t>(row) * ldo_lo + i] = lo_e5m2(y, o[i]);
+        }
+    }
 }
 
 // Register-resident form for hidden = 128 * NCH: each lane holds NCH float4 of
 // its row, so the row is read once; fp16 output in 8-byte stores.
 template <typename T, int NCH>
 __global__ void rmsnorm_reg_kernel(const float *__restrict__ x, int ldx, const float *__restrict__ w,
-                                   float eps, int rows, T *__restrict__ out, int ldo) {
+                                   float eps, int rows, T *__restrict__ out, int ldo, uint8_t *__restrict__ out_lo,
+                                   int ldo_lo) {
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -76,6 +84,10 @@ __global__ void rmsnorm_reg_kernel(const float *__restrict__ x, int ldx, const f
             const __half2 a = __floats2half2_rn(y0, y1), b = __floats2half2_rn(y2, y3);
             *reinterpret_cast<uint2 *>(o + i) =
                 make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+            if (out_lo)
+                *reinterpret_cast<uint32_t *>(out_lo + static_cast<size_t>(row) * ldo_lo + i) =
+                    lo_e5m2(y0, __low2half(a)) | (lo_e5m2(y1, __high2half(a)) << 8) |
+                    (lo_e5m2(y2, __low2half(b)) << 16) | (static_cast<uint32_t>(lo_e5m2(y3, __high2half(b))) << 24);
         } else {
             *reinterpret_cast<float4 *>(o + i) = make_float4(y0, y1, y2, y3);
         }
@@ -381,7 +393,7 @@ __global__ void __launch_bounds__(128 * SPLIT) delta_recurrent_split_kernel(Delt
 template <typename T>
 __global__ void gated_norm_kernel(const float *__restrict__ o, const float *__restrict__ z, int ldz,
                                   const float *__restrict__ w, float eps, int n, int nv, int dv,
-                                  T *__restrict__ out, int ldo) {
+                                  T *__restrict__ out, int ldo, uint8_t *__restrict__ out_lo, int ldo_lo) {
     const int item = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (item >= n * nv) return;
@@ -393,7 +405,13 @@ __global__ void gated_norm_kernel(const float *__restrict__ o, const float *__re
     const float denom = sqrtf(ss / static_cast<float>(dv) + eps);
     const float *zr = z + static_cast<size_t>(t) * ldz + h * dv;
     T *dst = out + static_cast<size_t>(t) * ldo + h * dv;
-    for (int i = lane; i < dv; i += 32) dst[i] = Act<T>::from_f(((src[i] / denom) * w[i]) * silu_f(zr[i]));
+    for (int i = lane; i < dv; i += 32) {
+        const float y = ((src[i] / denom) * w[i]) * silu_f(zr[i]);
+        dst[i] = Act<T>::from_f(y);
+        if constexpr (sizeof(T) == 2) {
+            if (out_lo) out_lo[static_cast<size_t>(t) * ldo_lo + h * dv + i] = lo_e5m2(y, dst[i]);
+        }
+    }
 }
 
 // ------------------------------------------------------------------ attention prep
@@ -604,18 +622,23 @@ __global__ void attn_simt_kernel(AttnArgs a) {
 // ------------------------------------------------------------------ swiglu
 template <typename T>
 __global__ void swiglu_kernel(const float *__restrict__ gu, int ldg, int n, int f, T *__restrict__ out,
-                              int ldo) {
+                              int ldo, uint8_t *__restrict__ out_lo, int ldo_lo) {
     const size_t total = static_cast<size_t>(n) * f;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const size_t t = i / f, j = i % f;
-        out[t * ldo + j] = Act<T>::from_f(silu_f(gu[t * ldg + j]) * gu[t * ldg + f + j]);
+        const float y = silu_f(gu[t * ldg + j]) * gu[t * ldg + f + j];
+        out[t * ldo + j] = Act<T>::from_f(y);
+        if constexpr (sizeof(T) == 2) {
+            if (out_lo) out_lo[t * ldo_lo + j] = lo_e5m2(y, out[t * ldo + j]);
+        }
     }
 }
 
 // ------------------------------------------------------------------ int8 expand
 // 16 int8 values per thread and iteration: one 16-byte load, two 16-byte stores.
-__global__ void expand_i8_kernel(const int8_t *__restrict__ q, size_t n16, __half *__restrict__ out) {
+__global__ void expand_i8_kernel(const int8_t *__restrict__ q, size_t n16, __half *__restrict__ out,
+                                 uint8_t *__restrict__ out8) {
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const int4 v = __ldcs(reinterpret_cast<const int4 *>(q) + i);
@@ -626,13 +649,23 @@ __global__ void expand_i8_kernel(const int8_t *__restrict__ q, size_t n16, __hal
         uint4 *o = reinterpret_cast<uint4 *>(out) + 2 * i;
         o[0] = *reinterpret_cast<const uint4 *>(&h[0]);
         o[1] = *reinterpret_cast<const uint4 *>(&h[8]);
+        if (out8) {
+            __align__(16) uint8_t e[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                e[j] = static_cast<uint8_t>(__nv_cvt_halfraw_to_fp8(h[j], __NV_SATFINITE, __NV_E4M3));
+            reinterpret_cast<uint4 *>(out8)[i] = *reinterpret_cast<const uint4 *>(e);
+        }
     }
 }
 
-__global__ void expand_i8_tail_kernel(const int8_t *__restrict__ q, size_t from, size_t n, __half *__restrict__ out) {
+__global__ void expand_i8_tail_kernel(const int8_t *__restrict__ q, size_t from, size_t n, __half *__restrict__ out,
+                                      uint8_t *__restrict__ out8) {
     for (size_t i = from + blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
         out[i] = __int2half_rn(q[i]);
+        if (out8) out8[i] = static_cast<uint8_t>(__nv_cvt_halfraw_to_fp8(out[i], __NV_SATFINITE, __NV_E4M3));
+    }
 }
 
 // ------------------------------------------------------------------ readout
@@ -700,18 +733,19 @@ void launch_embed(int act, const uint32_t *ids, int n, const void *table, int hi
 }
 
 void launch_rmsnorm(int act, const float *x, int ldx, const float *w_eff, float eps, int rows,
-                    int hidden, void *out, int ldo, cudaStream_t s) {
+                    int hidden, void *out, int ldo, cudaStream_t s, uint8_t *out_lo, int ldo_lo) {
     if (rows <= 0) return;
+    if (act == kActF32) out_lo = nullptr;
     const int grid = ceil_div(rows, 8);
     const bool vec = (ldx % 4) == 0 && (ldo % 4) == 0 && (hidden % 128) == 0;
 #define HK_RMS_REG(NCH)                                                                                          \
     if (vec && hidden == 128 * (NCH)) {                                                                          \
         if (act == kActF32)                                                                                      \
             rmsnorm_reg_kernel<float, NCH><<<grid, 256, 0, s>>>(x, ldx, w_eff, eps, rows, static_cast<float *>(out), \
-                                                                ldo);                                            \
+                                                                ldo, nullptr, 0);                                \
         else                                                                                                     \
             rmsnorm_reg_kernel<__half, NCH><<<grid, 256, 0, s>>>(x, ldx, w_eff, eps, rows,                        \
-                                                                 static_cast<__half *>(out), ldo);               \
+                                                                 static_cast<__half *>(out), ldo, out_lo, ldo_lo); \
         HK_LAUNCH_CHECK();                                                                                       \
         return;                                                                                                  \
     }
@@ -722,10 +756,11 @@ void launch_rmsnorm(int act, const float *x, int ldx, const float *w_eff, float 
     HK_RMS_REG(32)
 #undef HK_RMS_REG
     if (act == kActF32)
-        rmsnorm_kernel<float><<<grid, 256, 0, s>>>(x, ldx, w_eff, eps, rows, hidden, static_cast<float *>(out), ldo);
+        rmsnorm_kernel<float><<<grid, 256, 0, s>>>(x, ldx, w_eff, eps, rows, hidden, static_cast<float *>(out), ldo,
+                                                   nullptr, 0);
     else
         rmsnorm_kernel<__half><<<grid, 256, 0, s>>>(x, ldx, w_eff, eps, rows, hidden, static_cast<__half *>(out),
-                                                    ldo);
+                                                    ldo, out_lo, ldo_lo);
     HK_LAUNCH_CHECK();
 }
 
@@ -849,13 +884,15 @@ void launch_delta_recurrent(const DeltaRecArgs &a, cudaStream_t s) {
 }
 
 void launch_gated_norm(int act, const float *o, const float *z, int ldz, const float *w, float eps,
-                       int n, int nv, int dv, void *out, int ldo, cudaStream_t s) {
+                       int n, int nv, int dv, void *out, int ldo, cudaStream_t s, uint8_t *out_lo, int ldo_lo) {
     if (n <= 0) return;
     const int grid = ceil_div(static_cast<long>(n) * nv, 8);
     if (act == kActF32)
-        gated_norm_kernel<float><<<grid, 256, 0, s>>>(o, z, ldz, w, eps, n, nv, dv, static_cast<float *>(out), ldo);
+        gated_norm_kernel<float><<<grid, 256, 0, s>>>(o, z, ldz, w, eps, n, nv, dv, static_cast<float *>(out), ldo,
+                                                      nullptr, 0);
     else
-        gated_norm_kernel<__half><<<grid, 256, 0, s>>>(o, z, ldz, w, eps, n, nv, dv, static_cast<__half *>(out), ldo);
+        gated_norm_kernel<__half><<<grid, 256, 0, s>>>(o, z, ldz, w, eps, n, nv, dv, static_cast<__half *>(out), ldo,
+                                                       out_lo, ldo_lo);
     HK_LAUNCH_CHECK();
 }
 
@@ -906,31 +943,33 @@ void launch_attention(int act, const AttnArgs &a, cudaStream_t s) {
     HK_LAUNCH_CHECK();
 }
 
-void launch_expand_i8(const int8_t *q, size_t n, __half *out, cudaStream_t s) {
+void launch_expand_i8(const int8_t *q, size_t n, __half *out, uint8_t *out8, cudaStream_t s) {
     if (n == 0) return;
-    const bool aligned = (reinterpret_cast<uintptr_t>(q) % 16) == 0 && (reinterpret_cast<uintptr_t>(out) % 16) == 0;
+    const bool aligned = (reinterpret_cast<uintptr_t>(q) % 16) == 0 && (reinterpret_cast<uintptr_t>(out) % 16) == 0 &&
+                         (reinterpret_cast<uintptr_t>(out8) % 16) == 0;
     const size_t n16 = aligned ? n / 16 : 0;
     if (n16) {
         const size_t blocks = (n16 + 255) / 256;
-        expand_i8_kernel<<<static_cast<int>(blocks < 148 * 8 ? blocks : 148 * 8), 256, 0, s>>>(q, n16, out);
+        expand_i8_kernel<<<static_cast<int>(blocks < 148 * 8 ? blocks : 148 * 8), 256, 0, s>>>(q, n16, out, out8);
         HK_LAUNCH_CHECK();
     }
     if (n16 * 16 < n) {  // the last n % 16 values, or all of them when unaligned
         const size_t rest = n - n16 * 16, blocks = (rest + 255) / 256;
         expand_i8_tail_kernel<<<static_cast<int>(blocks < 148 * 8 ? blocks : 148 * 8), 256, 0, s>>>(q, n16 * 16, n,
-                                                                                                  out);
+                                                                                                  out, out8);
         HK_LAUNCH_CHECK();
     }
 }
 
-void launch_swiglu(int act, const float *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s) {
+void launch_swiglu(int act, const float *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s,
+                   uint8_t *out_lo, int ldo_lo) {
     if (n <= 0) return;
     const long total = static_cast<long>(n) * f;
     const int grid = static_cast<int>(total / 256 + 1 < 148 * 16 ? total / 256 + 1 : 148 * 16);
     if (act == kActF32)
-        swiglu_kernel<float><<<grid, 256, 0, s>>>(gu, ldg, n, f, static_cast<float *>(out), ldo);
+        swiglu_kernel<float><<<grid, 256, 0, s>>>(gu, ldg, n, f, static_cast<float *>(out), ldo, nullptr, 0);
     else
-        swiglu_kernel<__half><<<grid, 256, 0, s>>>(gu, ldg, n, f, static_cast<__half *>(out), ldo);
+        swiglu_kernel<__half><<<grid, 256, 0, s>>>(gu, ldg, n, f, static_cast<__half *>(out), ldo, out_lo, ldo_lo);
     HK_LAUNCH_CHECK();
 }
 

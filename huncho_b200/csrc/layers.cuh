@@ -18,8 +18,10 @@ void launch_embed(int act, const uint32_t *ids, int n, const void *table, int hi
                   cudaStream_t s);
 
 // out[r, :] = rms_norm(x[r, :]) * w_eff (qwen3_5.rs:180-190); w_eff = 1 + w, fp32.
+// fp16 outputs optionally also write the e5m2 low part of each value to
+// out_lo [rows, ldo_lo bytes] (the split-precision GEMM input, GemmArgs::x_lo).
 void launch_rmsnorm(int act, const float *x, int ldx, const float *w_eff, float eps, int rows,
-                    int hidden, void *out, int ldo, cudaStream_t s);
+                    int hidden, void *out, int ldo, cudaStream_t s, uint8_t *out_lo = nullptr, int ldo_lo = 0);
 
 // Gated DeltaNet input stage for every token (qwen3_5.rs:817-925): causal
 // depthwise conv (K taps, restricted to the token's own row) + SiLU on the
@@ -101,13 +103,15 @@ struct DeltaFusedInput {
 // j+1's state-independent operands while 8 warps run chunk j's state-dependent
 // products); 128-wide heads, 4 taps.
 bool delta_pipe_supported(const DeltaRecArgs &r, const DeltaFusedInput &in);
+// mix_lo (optional): the e5m2 low part of the output [n, ldmix_lo bytes].
 void launch_delta_pipe(const DeltaRecArgs &r, const DeltaFusedInput &in, const float *norm_w, float eps, __half *mix,
-                       int ldmix, cudaStream_t s);
+                       int ldmix, cudaStream_t s, uint8_t *mix_lo = nullptr, int ldmix_lo = 0);
 
 // out[t, h*dv + j] = rms(o)[j] * w[j] * silu(z[t, h, j]) (qwen3_5.rs:193-201,
 // 934-938); o and z fp32, out in the activation type (the out_proj input).
 void launch_gated_norm(int act, const float *o, const float *z, int ldz, const float *w, float eps,
-                       int n, int nv, int dv, void *out, int ldo, cudaStream_t s);
+                       int n, int nv, int dv, void *out, int ldo, cudaStream_t s, uint8_t *out_lo = nullptr,
+                       int ldo_lo = 0);
 
 // Full-attention input stage (qwen3_5.rs:596-615): split q | gate per head,
 // q_norm / k_norm (zero-centred weights, fp32), partial RoPE on the first
@@ -176,11 +180,13 @@ bool attention_tc_supported(int hd);
 void launch_attention_tc(const AttnArgs &a, cudaStream_t s);
 
 // out[i] = (fp16) q[i] for i < n: int8 weights expanded to fp16 (exact for
-// |q| <= 127) right before the projection that uses them.
-void launch_expand_i8(const int8_t *q, size_t n, __half *out, cudaStream_t s);
+// |q| <= 127) right before the projection that uses them; out8 (optional)
+// receives the e4m3 rounding of the same values (split-precision low part).
+void launch_expand_i8(const int8_t *q, size_t n, __half *out, uint8_t *out8, cudaStream_t s);
 
 // out[t, j] = silu(gu[t, j]) * gu[t, F + j] (qwen3_5.rs:1020-1031); gu fp32.
-void launch_swiglu(int act, const float *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s);
+void launch_swiglu(int act, const float *gu, int ldg, int n, int f, void *out, int ldo, cudaStream_t s,
+                   uint8_t *out_lo = nullptr, int ldo_lo = 0);
 
 // Pointer readout (qwen3_5.rs:3196-3255, kev.rs:169-173). idx lists the token
 // rows to read: first the n_dec decision rows, then the n_opt option rows.

@@ -77,6 +77,37 @@ int hk_op_gemm(int dtype, int epilogue, int M, int N, int K, const void *x, int 
     });
 }
 
+int hk_op_gemm_split(int epilogue, int M, int N, int K, const void *x, int ldx, const uint8_t *x_lo, int ldx_lo,
+                     const void *w, int ldw, const uint8_t *w8, int ldw8, const float *scale, void *out, int ldo,
+                     uint8_t *out_lo, int ldo_lo, int pairs, void *stream) {
+    return op_guard([&] {
+        if (!x || !x_lo || !w || !w8 || !out) throw std::invalid_argument("hk_op_gemm_split: null pointer");
+        hk::GemmArgs a;
+        a.M = M;
+        a.N = N;
+        a.K = K;
+        a.x = x;
+        a.ldx = ldx;
+        a.x_lo = x_lo;
+        a.ldx_lo = ldx_lo;
+        a.w = w;
+        a.ldw = ldw;
+        a.w8 = w8;
+        a.ldw8 = ldw8;
+        a.scale = scale;
+        a.out = out;
+        a.ldo = ldo;
+        a.out_lo = out_lo;
+        a.ldo_lo = ldo_lo;
+        a.epilogue = epilogue;
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (pairs)
+            hk::gemm_f16_tc_pair(a, s, current_sms());
+        else
+            hk::gemm_f16_tc(a, s, current_sms());
+    });
+}
+
 int hk_op_gemm_packed(int M, int N, int K, int kp, const float *x, int ldx, const int8_t *w_q, const float *w_d,
                       int8_t *x_q, float *x_d, float *out, int ldo, int residual, void *stream) {
     return op_guard([&] {

@@ -229,6 +229,34 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32_mj(int M, int N, bool a_mn,
     return idesc_f16_f32_neg(M, N, neg_a) | (a_mn ? (1u << 15) : 0u) | (b_mn ? (1u << 16) : 0u);
 }
 
+// Instruction descriptor for kind::f8f6f4: A e5m2 (format 1 in bits 7-9), B
+// e4m3 (format 0 in bits 10-12), fp32 accumulation, both K-major; K is 32 per
+// instruction (32 bytes of a K-major 128-byte row, as kind::f16's 16).
+__host__ __device__ constexpr uint32_t idesc_e5m2_e4m3_f32(int M, int N) {
+    return (1u << 4) | (1u << 7) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T with 8-bit float operands (kind::f8f6f4).
+// Accumulates into the same fp32 TMEM accumulator as kind::f16 instructions.
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {

@@ -27,6 +27,21 @@ extern "C" {
 int hk_op_gemm(int dtype, int epilogue, int M, int N, int K, const void *x, int ldx, const void *w,
                int ldw, const float *scale, void *out, int ldo, void *stream);
 
+/* The split-precision form of hk_op_gemm's fp16 tensor-core GEMM (dtype 1),
+ * the one the half-precision models run for the delta layers' and the MLPs'
+ * projections: x fp16 [M, ldx] is the high part of the input and x_lo
+ * [M, ldx_lo bytes] its e5m2 low part (x_true - fp16(x_true)); w fp16 [N, ldw]
+ * and w8 [N, ldw8 bytes] an e4m3 copy of it. out (epilogue) = x w^T + x_lo w8^T
+ * with fp32 accumulation (kind::f16 then kind::f8f6f4 tcgen05 MMAs into one
+ * accumulator). SwiGLU (epilogue 2) also writes the e5m2 low part of its fp16
+ * output to out_lo [M, ldo_lo bytes] when out_lo is not NULL. Byte strides
+ * are multiples of 16. pairs = 1 forces CTA pairs (cta_group::2); 0 lets the
+ * shape choose, as the model does. No reference counterpart (the reference's
+ * CUDA path runs plain fp16 projections). */
+int hk_op_gemm_split(int epilogue, int M, int N, int K, const void *x, int ldx, const uint8_t *x_lo, int ldx_lo,
+                     const void *w, int ldw, const uint8_t *w8, int ldw8, const float *scale, void *out, int ldo,
+                     uint8_t *out_lo, int ldo_lo, int pairs, void *stream);
+
 /* A packed projection (the reference's Projection::Packed, qwen3_5.rs:320-369):
  * x fp32 [M, K] (leading dim ldx) quantized to Q8_0 blocks of 32 (columns >= K
  * zero; x_q int8 [M, kp] and x_d fp32 [M, kp/32] are caller-provided scratch),

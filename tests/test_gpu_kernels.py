@@ -516,3 +516,100 @@ def test_readout_bad_decision_index_gives_nan_without_reading(lib):
     assert torch.isnan(got[3]) and torch.isnan(got[7])
     keep = [i for i in range(n_opt) if i not in (3, 7)]
     assert torch.equal(got[keep], good[keep])
+
+
+# ---------------------------------------------------------------------------
+# Split-precision projections (fp16 high part + e5m2 low part, fp8 MMAs)
+# ---------------------------------------------------------------------------
+
+def _e5m2(t):
+    return t.to(torch.float8_e5m2)
+
+
+def _e4m3(t):
+    return t.to(torch.float8_e4m3fn)
+
+
+def _pad16(t8, cols):
+    """An 8-bit [rows, cols] tensor with rows padded to a multiple of 16 bytes."""
+    ld = (cols + 15) // 16 * 16
+    out = torch.zeros(t8.shape[0], ld, dtype=torch.uint8, device="cuda")
+    out[:, :cols] = t8.view(torch.uint8)
+    return out, ld
+
+
+def gemm_split(lib, epi, x_true, w, out, pairs=0, scale=None, out_lo=None):
+    M, K = x_true.shape
+    N = w.shape[0]
+    xh = x_true.half()
+    xl, ldxl = _pad16(_e5m2(x_true - xh.float()), K)
+    w8, ldw8 = _pad16(_e4m3(w.float()), K)
+    lib.hk_op_gemm_split.argtypes = ([ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_int] * 4
+                                     + [ctypes.c_void_p] + [ctypes.c_void_p, ctypes.c_int] * 2
+                                     + [ctypes.c_int, ctypes.c_void_p])
+    olo, ldol = (None, 0) if out_lo is None else out_lo
+    rc = lib.hk_op_gemm_split(epi, M, N, K, _p(xh), xh.stride(0), _p(xl), ldxl, _p(w), w.stride(0), _p(w8), ldw8,
+                              _p(scale), _p(out), out.stride(0), _p(olo), ldol, pairs, None)
+    assert rc == 0, lib.hk_op_last_error()
+    torch.cuda.synchronize()
+    ref = xh.float() @ w.float().T + _e5m2(x_true - xh.float()).float() @ _e4m3(w.float()).float().T
+    return xh, ref
+
+
+SPLIT_SHAPES = [(7, 32, 16), (130, 300, 1024), (257, 512, 200), (1000, 1024, 2048), (555, 1024, 3584),
+                (700, 8224, 1024)]
+
+
+@pytest.mark.parametrize("pairs", [0, 1])
+@pytest.mark.parametrize("M,N,K", SPLIT_SHAPES)
+def test_split_gemm_f32_store_and_accuracy(lib, M, N, K, pairs):
+    """x w^T + x_lo w8^T accumulated in one fp32 accumulator (kind::f16 then
+    kind::f8f6f4 MMAs), single CTAs and CTA pairs, ragged M / N / K: equal to
+    the fp32 sum of both products, and much closer to the fp32 product of the
+    unrounded input than the fp16 input alone."""
+    if pairs and M < 13:
+        pytest.skip("CTA pairs run M >= 13 here, as in the pair-kernel test above")
+    g = torch.Generator(device="cuda").manual_seed(M + N + K + pairs)
+    x = torch.randn(M, K, device="cuda", generator=g) * 2.0
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    out = torch.zeros(M, N, device="cuda")
+    xh, ref = gemm_split(lib, 3, x, w, out, pairs=pairs)
+    # The tensor cores sum each MMA's products in their own order and width;
+    # over K = 3584 that moves outputs of magnitude ~2 by up to ~3e-5.
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
+    exact = x @ w.float().T
+    err_split = (out - exact).abs().max().item()
+    err_f16 = (xh.float() @ w.float().T - exact).abs().max().item()
+    assert err_split < err_f16 / 4, (err_split, err_f16)
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 1024, 2048), (257, 1024, 3584)])
+def test_split_gemm_residual(lib, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(3 * M + N)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
+    res = torch.randn(M, N, device="cuda", generator=g)
+    out = res.clone()
+    _, ref = gemm_split(lib, 1, x, w, out)
+    torch.testing.assert_close(out, res + ref, rtol=1e-4, atol=1e-4)
+
+
+def test_split_gemm_swiglu_writes_low_part(lib):
+    """The SwiGLU epilogue on a split-precision input writes the fp16 output
+    and the e5m2 rounding of (output - fp16(output)): together they carry the
+    SwiGLU value to ~14 bits."""
+    g = torch.Generator(device="cuda").manual_seed(19)
+    M, F, K = 333, 512, 1024
+    x = torch.randn(M, K, device="cuda", generator=g)
+    gate = (torch.randn(F, K, device="cuda", generator=g) * 0.05).half()
+    up = (torch.randn(F, K, device="cuda", generator=g) * 0.05).half()
+    w = torch.cat([torch.cat([gate[b:b + 128], up[b:b + 128]]) for b in range(0, F, 128)])
+    out = torch.zeros(M, F, device="cuda", dtype=torch.float16)
+    lo = torch.zeros(M, F, device="cuda", dtype=torch.uint8)
+    _, acc = gemm_split(lib, 2, x, w, out, out_lo=(lo, F))
+    ga = torch.cat([acc[:, b:b + 128] for b in range(0, 2 * F, 256)], 1)
+    ua = torch.cat([acc[:, b + 128:b + 256] for b in range(0, 2 * F, 256)], 1)
+    y = ga / (1 + torch.exp(-ga)) * ua
+    torch.testing.assert_close(out.float(), y, rtol=2e-3, atol=2e-3)
+    two = out.float() + lo.view(torch.float8_e5m2).float()
+    assert (two - y).abs().max() < (out.float() - y).abs().max() / 3
