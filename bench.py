@@ -642,12 +642,9 @@ def main():
     pk = peaks()
     gemm_ms, gemm_flops, _gemm_bytes, gemm_n = prof["gemm"]
     achieved = (gemm_flops / 1e12) / (gemm_ms / 1e3) if gemm_ms > 0 else None
-    traffic = None  # DRAM bytes per GEMM launch from the committed full-size ncu capture
-    tf = ROOT / "profiles" / "gemm_f16_tc_kernel_cfg2_dram.md"
-    if tf.exists() and args.config == 2:
-        for line in tf.read_text().splitlines():
-            if line.startswith("traffic_bytes_per_launch:"):
-                traffic = int(line.split(":")[1])
+    # DRAM traffic of the GEMM class is not measured live (ncu counters come
+    # from small-case captures of single launches, profiles/gemm_split_*.md).
+    traffic = None
     total_prof_ms = sum(v[0] for v in prof.values())
     line = {
         "metric": "scored requests/s", "value": value, "unit": "requests/s", "n_gpus": world,
@@ -688,7 +685,12 @@ def main():
                      "bound": "tensor", "achieved": achieved,
                      "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                      "frac": (achieved / pk["bf16_tflops_sustained"]) if achieved else None,
-                     "traffic": traffic, "peak_source": pk["source"] + " (sustained: kernels timed inside a step)",
+                     "traffic": traffic,
+                     "traffic_note": "per-launch DRAM bytes of single GEMM launches on a small case are in "
+                                     "profiles/gemm_split_projections_cfg2_small.md",
+                     "work": "algorithmic 2 M N K per projection; split-precision launches also run the 8-bit "
+                             "low-part MMAs (half the fp16 MMA time), which are not counted",
+                     "peak_source": pk["source"] + " (sustained: kernels timed inside a step)",
                      "launches": int(gemm_n),
                      "timed_over": ("a serial pass of the same steps after the timed region (one handle, one "
                                     "stream; the timed region runs replicas on concurrent streams)"

@@ -486,10 +486,15 @@ __global__ void __launch_bounds__(THREADS, 1) delta_pipe_kernel(PipeArgs a) {
         {
             const bool kk = pw < 4;
             const int mt = (pw >> 1) & 1, n0 = (pw & 1) * 16;
-            float acc[2][4];
+            // hi x hi and the two cross terms in separate accumulators (four
+            // independent MMA chains instead of two), summed at the end.
+            float acc[2][4], acx[2][4];
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-#pragma unroll 2
+            for (int nt = 0; nt < 2; ++nt) {
+                acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+                acx[nt][0] = acx[nt][1] = acx[nt][2] = acx[nt][3] = 0.f;
+            }
+#pragma unroll
             for (int k0 = 0; k0 < D; k0 += 16) {
                 uint32_t ah[4], al[4], bh[4], bl[4];
                 frag_a<LDH>(ah, kk ? sm.Kh : H.Qh, mt * 16, k0, lane);
@@ -498,11 +503,15 @@ __global__ void __launch_bounds__(THREADS, 1) delta_pipe_kernel(PipeArgs a) {
                 frag_b_nk<LDH>(bl, sm.Kl, k0, n0, lane);
                 mma(acc[0], ah, bh[0], bh[1]);
                 mma(acc[1], ah, bh[2], bh[3]);
-                mma(acc[0], ah, bl[0], bl[1]);
-                mma(acc[1], ah, bl[2], bl[3]);
-                mma(acc[0], al, bh[0], bh[1]);
-                mma(acc[1], al, bh[2], bh[3]);
+                mma(acx[0], ah, bl[0], bl[1]);
+                mma(acx[1], ah, bl[2], bl[3]);
+                mma(acx[0], al, bh[0], bh[1]);
+                mma(acx[1], al, bh[2], bh[3]);
             }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[nt][e] += acx[nt][e];
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
 #pragma unroll

@@ -461,7 +461,8 @@ def test_delta_layer_kernel_vs_oracle(lib, nk, nv):
     assert np.isfinite(got).all()
     err = np.abs(got - ref).max() / np.abs(ref).max()
     print(f"delta layer nk={nk} nv={nv}: max |err| / max |ref| = {err:.3g}")
-    assert err <= 3e-3
+    # The output is fp16 (half an ulp = 4.9e-4 relative); measured 2.5e-4.
+    assert err <= 1e-3
 
 
 def test_delta_layer_kernel_long_context_stress(lib):
@@ -476,7 +477,7 @@ def test_delta_layer_kernel_long_context_stress(lib):
     assert np.isfinite(got).all()
     err = np.abs(got - ref).max() / np.abs(ref).max()
     print(f"delta layer 2 x 8192 stress: max |err| / max |ref| = {err:.3g}")
-    assert err <= 5e-3
+    assert err <= 1e-3  # measured 3.0e-4
 
 
 def test_delta_layer_rejects_bad_shapes(lib):
