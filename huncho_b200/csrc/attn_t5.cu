@@ -23,6 +23,8 @@
 // tensor memory and returns.
 #include <math.h>
 
+#include <cstring>
+
 #include "common.cuh"
 #include "layers.cuh"
 #include "sm100.cuh"
@@ -81,15 +83,22 @@ __device__ __forceinline__ void st8h(uint8_t *p, const float *v) {
     *reinterpret_cast<uint4 *>(p) = u;
 }
 
-template <int HD>
-__global__ void __launch_bounds__(THREADS, 1) attn_t5_kernel(AttnArgs a) {
+// TMA = true: Q, K and V tiles come by TMA (one thread issues them; K / V per
+// page or 64-key box through the block table), completing on mbarriers; rows
+// without a cached prefix only. TMA = false: every thread stages its 16-byte
+// chunks with cp.async (any row).
+template <int HD, bool TMA>
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_t5_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, AttnArgs a) {
     using L = Tiles<HD>;
     constexpr int CH = HD / 8;  // 16-byte chunks per row
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L::END);
     uint64_t *bar_s = bars, *bar_pv = bars + 2, *bar_drain = bars + 3;
-    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 4);
+    uint64_t *bar_q = bars + 4, *bar_k = bars + 5, *bar_v = bars + 7;  // TMA completions (K, V: per buffer)
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 9);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
     const int row = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * BM;
@@ -109,7 +118,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_t5_kernel(AttnArgs a) {
     const uint32_t s_base = smem_addr(sm);
 
     if (tid == 0) {
-        for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < 9; ++i) mbar_init(&bars[i], 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -156,6 +165,31 @@ __global__ void __launch_bounds__(THREADS, 1) attn_t5_kernel(AttnArgs a) {
             cpa16(dst + sw128_off(BKV, r, c_own * 8), src, ok);
         }
     };
+    // TMA form (thread 0): a K or V tile of 64 keys as boxes of R = min(page,
+    // 64) rows x 64 columns (one 128-byte swizzle row) per 64-column block of
+    // the head; pages past the row's last one read that last page instead (its
+    // values are finite; those keys are masked and their V rows zeroed).
+    const int R = pt ? (pt < BKV ? pt : BKV) : BKV;
+    const int last_page = pt ? (len - 1) >> pshift : 0;
+    uint32_t kv_pend = 0;  // bit b: K buffer b, bit 2 + b: V buffer b has a load in flight
+    auto tma_kv = [&](bool is_v, int kv0, int b) {
+        uint8_t *dst = sm + (is_v ? L::V0 : L::K0) + b * L::KV_BYTES;
+        uint64_t *bar = is_v ? &bar_v[b] : &bar_k[b];
+        mbar_expect_tx(bar, L::KV_BYTES);
+        const CUtensorMap *m = is_v ? &tm_v : &tm_k;
+        for (int r0 = 0; r0 < BKV; r0 += R) {
+            const int j = kv0 + r0;
+            int slot = start + j;
+            if (pt) {
+                const int pidx = (j >> pshift) < last_page ? (j >> pshift) : last_page;
+                slot = (ptab[pidx] << pshift) + (j & (pt - 1));
+            }
+#pragma unroll
+            for (int kt = 0; kt < HD / 64; ++kt)
+                tma_load_2d(dst + kt * BKV * 128 + r0 * 128, m, bar, kh * HD + kt * 64, slot);
+        }
+        kv_pend |= 1u << (is_v ? 2 + b : b);
+    };
     // S = Q K^T into S buffer sb from K buffer kb (thread 0).
     auto issue_s = [&](int kb, int sb, uint32_t tmem) {
         const uint64_t d0 = desc_sw128(s_base, 16, 1024);
@@ -178,33 +212,55 @@ __global__ void __launch_bounds__(THREADS, 1) attn_t5_kernel(AttnArgs a) {
         for (int ks = 0; ks < BKV / 16; ++ks)
             mma_f16(tmem + TM_O, pa + ((ks * 32) >> 4), vb + ((ks * 2048) >> 4), id, (acc || ks > 0) ? 1u : 0u);
     };
-    auto wait = [&](uint64_t *bar, uint32_t parity) {
+    auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {
         if (!mbar_wait(bar, parity)) {
             set_error(a.err, kErrWaitTimeout);
             *abort_flag = 1;
+            return false;
         }
+        return true;
     };
 
     const int kv_end = P + min(len, q0 + BM);  // causal: keys up to the last query of the tile
     const int n_tiles = (kv_end + BKV - 1) / BKV;
     // cp.async groups per thread: {Q, K0, V0}, {K1}, then per tile i {K(i+2)}, {V(i+1)}.
-    load_q();
-    load_kv(false, 0, 0);
-    load_kv(true, 0, 0);
-    cpa_commit();
-    if (n_tiles > 1) load_kv(false, BKV, 1);
-    cpa_commit();
-    cpa_wait<1>();
-    fence_async_smem();
+    uint32_t kph = 0, vph = 0;  // TMA: bit b = parity of the next wait on K / V buffer b
+    if constexpr (TMA) {
+        __syncthreads();  // barriers initialised
+        if (tid == 0) {
+            mbar_expect_tx(bar_q, L::Q_BYTES);
+#pragma unroll
+            for (int kt = 0; kt < HD / 64; ++kt)
+                tma_load_2d(sm + L::Q + kt * BM * 128, &tm_q, bar_q, h * HD + kt * 64, start + q0);
+            tma_kv(false, 0, 0);
+            tma_kv(true, 0, 0);
+            if (n_tiles > 1) tma_kv(false, BKV, 1);
+        }
+    } else {
+        load_q();
+        load_kv(false, 0, 0);
+        load_kv(true, 0, 0);
+        cpa_commit();
+        if (n_tiles > 1) load_kv(false, BKV, 1);
+        cpa_commit();
+        cpa_wait<1>();
+        fence_async_smem();
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     if (tid == 0) {
+        if constexpr (TMA) {
+            wait(bar_q, 0);
+            if (wait(&bar_k[0], 0)) kv_pend &= ~1u;
+            tc_fence_after();
+        }
         issue_s(0, 0, tmem);
         mma_commit(&bar_s[0]);
     }
+    if constexpr (TMA) kph ^= 1u;
 
     const int qi = q0 + tid;  // this thread's query (own index) and its absolute key limit
     const bool q_ok = qi < len;
@@ -217,25 +273,40 @@ __global__ void __launch_bounds__(THREADS, 1) attn_t5_kernel(AttnArgs a) {
         const int b = it & 1, kv0 = it * BKV;
         // 1. S of the next tile, once its keys have landed.
         if (it + 1 < n_tiles) {
-            if (it == 0)
-                cpa_wait<0>();
-            else
-                cpa_wait<1>();
-            fence_async_smem();
-            tc_fence_before();
-            __syncthreads();
-            if (tid == 0) {
-                tc_fence_after();
-                issue_s((it + 1) & 1, (it + 1) & 1, tmem);
-                mma_commit(&bar_s[(it + 1) & 1]);
+            const int nb = (it + 1) & 1;
+            if constexpr (TMA) {
+                if (tid == 0) {
+                    if (wait(&bar_k[nb], (kph >> nb) & 1u)) kv_pend &= ~(1u << nb);
+                    tc_fence_after();
+                    issue_s(nb, nb, tmem);
+                    mma_commit(&bar_s[nb]);
+                }
+                kph ^= 1u << nb;
+            } else {
+                if (it == 0)
+                    cpa_wait<0>();
+                else
+                    cpa_wait<1>();
+                fence_async_smem();
+                tc_fence_before();
+                __syncthreads();
+                if (tid == 0) {
+                    tc_fence_after();
+                    issue_s(nb, nb, tmem);
+                    mma_commit(&bar_s[nb]);
+                }
             }
         }
         // 2. This tile's scores; its K buffer is then free for tile it+2.
         wait(&bar_s[b], (ph_s >> b) & 1u);
         ph_s ^= 1u << b;
         tc_fence_after();
-        if (it + 2 < n_tiles) load_kv(false, kv0 + 2 * BKV, b);
-        cpa_commit();
+        if constexpr (TMA) {
+            if (it + 2 < n_tiles && tid == 0) tma_kv(false, kv0 + 2 * BKV, b);
+        } else {
+            if (it + 2 < n_tiles) load_kv(false, kv0 + 2 * BKV, b);
+            cpa_commit();
+        }
         float sv[BKV];
         {
             float t32[32];
@@ -277,8 +348,12 @@ __global__ void __launch_bounds__(THREADS, 1) attn_t5_kernel(AttnArgs a) {
             ph_pv ^= 1u;
             tc_fence_after();
         }
-        if (it + 1 < n_tiles) load_kv(true, kv0 + BKV, (it + 1) & 1);
-        cpa_commit();
+        if constexpr (TMA) {
+            if (it + 1 < n_tiles && tid == 0) tma_kv(true, kv0 + BKV, (it + 1) & 1);
+        } else {
+            if (it + 1 < n_tiles) load_kv(true, kv0 + BKV, (it + 1) & 1);
+            cpa_commit();
+        }
         if (__any_sync(0xffffffffu, resc)) {
             const float f = resc ? corr : 1.f;
 #pragma unroll 1
@@ -295,21 +370,63 @@ __global__ void __launch_bounds__(THREADS, 1) attn_t5_kernel(AttnArgs a) {
 #pragma unroll
         for (int c8 = 0; c8 < BKV / 8; ++c8) st8h(pb + sw128_off(BM, tid, c8 * 8), sv + c8 * 8);
         // 6. O += P V once this tile's V has landed.
-        if (it > 0) cpa_wait<2>();
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            issue_pv(b, it > 0, tmem);
-            mma_commit(bar_pv);
+        if constexpr (TMA) {
+            // A paged tile that reaches past the row's end holds keys of the
+            // row's last page beyond its tokens (never written in this batch):
+            // their probabilities are 0, and their V rows are zeroed so that no
+            // stale non-finite value reaches the product.
+            const int valid = P + len - kv0;
+            const bool tail = pt && valid < BKV;
+            bool v_done = false;
+            if (tail) {
+                v_done = wait(&bar_v[b], (vph >> b) & 1u);
+                constexpr int CPR = HD / 8;  // 16-byte chunks per key row
+                uint8_t *vb = sm + L::V0 + b * L::KV_BYTES;
+                for (int i = tid; i < (BKV - valid) * CPR; i += THREADS) {
+                    const int r = valid + i / CPR, c = i % CPR;
+                    *reinterpret_cast<uint4 *>(vb + (c >> 3) * BKV * 128 + r * 128 + (c & 7) * 16) =
+                        make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                if (!tail) v_done = wait(&bar_v[b], (vph >> b) & 1u);
+                if (v_done) kv_pend &= ~(1u << (2 + b));
+                tc_fence_after();
+                issue_pv(b, it > 0, tmem);
+                mma_commit(bar_pv);
+            }
+            vph ^= 1u << b;
+        } else {
+            if (it > 0) cpa_wait<2>();
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                issue_pv(b, it > 0, tmem);
+                mma_commit(bar_pv);
+            }
         }
     }
     if (!*abort_flag) {
         wait(bar_pv, ph_pv);
         tc_fence_after();
     }
-    cpa_wait<0>();
+    if constexpr (TMA) {
+        // After an aborted wait: let this CTA's own loads land before it exits.
+        if (tid == 0) {
+            for (int b2 = 0; b2 < 2; ++b2) {
+                if (kv_pend & (1u << b2)) (void)mbar_wait(&bar_k[b2], (kph >> b2) & 1u);
+                if (kv_pend & (1u << (2 + b2))) (void)mbar_wait(&bar_v[b2], (vph >> b2) & 1u);
+            }
+            (void)mbar_wait(bar_q, 0);
+        }
+    } else {
+        cpa_wait<0>();
+    }
     __syncthreads();
 
     if (!*abort_flag) {
@@ -360,10 +477,29 @@ __global__ void __launch_bounds__(THREADS, 1) attn_t5_kernel(AttnArgs a) {
 
 template <int HD>
 void launch_t5(const AttnArgs &a, cudaStream_t s) {
-    static SmemOptIn opt_in;
-    opt_in.ensure(attn_t5_kernel<HD>, Tiles<HD>::SMEM);
     dim3 grid(ceil_div(a.max_len, BM), a.nh, a.n_rows);
-    attn_t5_kernel<HD><<<grid, THREADS, Tiles<HD>::SMEM, s>>>(a);
+    const auto aligned = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    // TMA staging for rows without cached prefixes (their keys live in the
+    // k / v buffers only) when the slot count is known.
+    if (!a.pre_len && a.kv_slots > 0 && aligned(a.q) && aligned(a.k) && aligned(a.v)) {
+        static SmemOptIn opt_in;
+        opt_in.ensure(attn_t5_kernel<HD, true>, Tiles<HD>::SMEM);
+        const int pt = a.pages.page_tokens;
+        const uint32_t rows = pt ? (pt < BKV ? pt : BKV) : BKV;
+        const CUtensorMap tq = tensor_map_f16(a.q, a.n, static_cast<uint64_t>(a.nh) * HD,
+                                              static_cast<uint64_t>(a.nh) * HD * 2, 64, BM);
+        const CUtensorMap tk = tensor_map_f16(a.k, a.kv_slots, static_cast<uint64_t>(a.nkv) * HD,
+                                              static_cast<uint64_t>(a.nkv) * HD * 2, 64, rows);
+        const CUtensorMap tv = tensor_map_f16(a.v, a.kv_slots, static_cast<uint64_t>(a.nkv) * HD,
+                                              static_cast<uint64_t>(a.nkv) * HD * 2, 64, rows);
+        attn_t5_kernel<HD, true><<<grid, THREADS, Tiles<HD>::SMEM, s>>>(tq, tk, tv, a);
+    } else {
+        static SmemOptIn opt_in;
+        opt_in.ensure(attn_t5_kernel<HD, false>, Tiles<HD>::SMEM);
+        CUtensorMap z;
+        std::memset(&z, 0, sizeof(z));
+        attn_t5_kernel<HD, false><<<grid, THREADS, Tiles<HD>::SMEM, s>>>(z, z, z, a);
+    }
     HK_LAUNCH_CHECK();
 }
 

@@ -762,6 +762,26 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+}  // namespace
+
+CUtensorMap tensor_map_f16(const void *base, uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
+                           uint32_t box_cols, uint32_t box_rows) {
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || row_stride_bytes % 16)
+        throw CudaError("tensor map base must be 16-byte aligned with a row stride % 16 == 0");
+    CUtensorMap m;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_bytes)};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(r));
+    return m;
+}
+
+namespace {
+
 // A 2-D fp16 tensor map over rows x inner (row stride ld elements) with a
 // box of box_rows x 64 elements (128 bytes, one swizzle row) and zero fill.
 CUtensorMap make_map(const void *base, int rows, int inner, int ld, int box_rows) {

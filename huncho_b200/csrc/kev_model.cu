@@ -1223,6 +1223,7 @@ struct Model {
                 at.pre_len = cr ? cr->pre_len : nullptr;
                 at.kv_in = in_a;
                 at.err = err;
+                at.kv_slots = pages.page_tokens ? kv_slot_cap : n_tok;
                 if (out_a) launch_kv_store(A, at, out_a, stream);
                 ev = prof_begin();
                 launch_attention(A, at, stream);

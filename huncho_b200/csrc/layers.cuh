@@ -165,6 +165,10 @@ struct AttnArgs {
     const int32_t *pre_len = nullptr;
     const uint64_t *kv_in = nullptr;
     uint32_t *err = nullptr;  // device error word (bounded waits of the tcgen05 kernel)
+    // K / V slots the k and v buffers hold (flat: n; paged: the page pool);
+    // 0 = unknown (the tcgen05 kernel then stages K / V with cp.async instead
+    // of TMA).
+    int kv_slots = 0;
 };
 void launch_attention(int act, const AttnArgs &a, cudaStream_t s);
 // The tcgen05 kernel behind launch_attention for fp16 activations and

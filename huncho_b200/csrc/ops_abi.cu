@@ -231,6 +231,7 @@ int hk_op_attention(int act, const void *q, const void *k, const void *v, const 
         a.hd = hd;
         a.out = out;
         a.ldo = ldo;
+        a.kv_slots = n;  // flat K / V: one slot per token
         hk::launch_attention(act, a, static_cast<cudaStream_t>(stream));
     });
 }

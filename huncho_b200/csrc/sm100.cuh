@@ -389,4 +389,11 @@ __host__ __device__ __forceinline__ uint32_t sw128_off(int R, int r, int k) {
 }
 
 }  // namespace sm100
+
+// Host side: a 2-D fp16 tensor map over rows x cols (row stride in bytes, a
+// multiple of 16; 16-byte aligned base) with a box of box_cols x box_rows
+// elements, 128-byte swizzle (box_cols * 2 == 128) and zero fill outside the
+// tensor. Throws CudaError when the driver rejects it.
+CUtensorMap tensor_map_f16(const void *base, uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
+                           uint32_t box_cols, uint32_t box_rows);
 }  // namespace hk
