@@ -43,6 +43,17 @@ struct GemmArgs {
     // projection's x_lo), [M, ldo_lo bytes]; null = not written.
     uint8_t *out_lo = nullptr;
     int ldo_lo = 0;
+    // 3xTF32 (fp32 model on the tensor cores): x and w are fp32; x_lo32 =
+    // x - tf32(x) and w_lo32 = w - tf32(w), where tf32() keeps the sign, the
+    // exponent and the top 10 mantissa bits (what kind::tf32 reads). Y = x w^T
+    // + x w_lo^T + x_lo w^T, each term on kind::tf32, fp32 accumulation: the
+    // dropped x_lo w_lo^T and the operands' own truncation leave ~2^-20
+    // relative error. Epilogues 1 (residual) and 3 (fp32 store) only.
+    bool tf32 = false;
+    const float *x_lo32 = nullptr;
+    int ldx_lo32 = 0;  // elements
+    const float *w_lo32 = nullptr;
+    int ldw_lo32 = 0;  // elements
 };
 
 // fp16 X and W on tcgen05 tensor cores (TMA-fed, TMEM accumulators), fp32 accumulation.
@@ -52,6 +63,18 @@ void gemm_f16_tc(const GemmArgs &a, cudaStream_t s, int num_sms);
 void gemm_f16_tc_pair(const GemmArgs &a, cudaStream_t s, int num_sms);
 // fp32 X and W on CUDA cores (the fp32 model path).
 void gemm_f32_simt(const GemmArgs &a, cudaStream_t s);
+// lo[r, c] = x[r, c] - tf32(x[r, c]) for the 3xTF32 GEMM's input (rows of ld /
+// ldl floats).
+void launch_tf32_lo(const float *x, int ldx, int rows, int cols, float *lo, int ldl, cudaStream_t s);
+// Host: the same split for a weight matrix.
+inline float tf32_trunc_host(float v) {
+    uint32_t u;
+    __builtin_memcpy(&u, &v, 4);
+    u &= 0xFFFFE000u;
+    float r;
+    __builtin_memcpy(&r, &u, 4);
+    return r;
+}
 
 // Packed projections (GGML Q8_0 / Q4_0 weights as int8 block values [N, kp]
 // and fp32 block scales [N, kp/32]): the fp32 input rows quantized to Q8_0

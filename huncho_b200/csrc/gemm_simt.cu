@@ -67,7 +67,44 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(int M, int N, int K, cons
     }
 }
 
+// lo = x - tf32(x): the low part of a 3xTF32 input (tf32 keeps the top 10
+// mantissa bits; the difference is exact in fp32). float4 per thread when the
+// rows allow it.
+__global__ void tf32_lo_kernel(const float *__restrict__ x, int ldx, int rows, int cols, float *__restrict__ lo,
+                               int ldl, int vec) {
+    const size_t per_row = vec ? cols / 4 : cols;
+    const size_t total = static_cast<size_t>(rows) * per_row;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t r = i / per_row, c = i % per_row;
+        if (vec) {
+            const float4 v = *reinterpret_cast<const float4 *>(x + r * ldx + 4 * c);
+            float4 o;
+            o.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+            o.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+            o.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+            o.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+            *reinterpret_cast<float4 *>(lo + r * ldl + 4 * c) = o;
+        } else {
+            const float v = x[r * ldx + c];
+            lo[r * ldl + c] = v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+        }
+    }
+}
+
 }  // namespace
+
+void launch_tf32_lo(const float *x, int ldx, int rows, int cols, float *lo, int ldl, cudaStream_t s) {
+    if (rows <= 0 || cols <= 0) return;
+    const int vec = (cols % 4 == 0 && ldx % 4 == 0 && ldl % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(lo) & 15) == 0)
+                        ? 1
+                        : 0;
+    const long items = static_cast<long>(rows) * (vec ? cols / 4 : cols);
+    const int grid = static_cast<int>(items / 256 + 1 < 148 * 8 ? items / 256 + 1 : 148 * 8);
+    tf32_lo_kernel<<<grid, 256, 0, s>>>(x, ldx, rows, cols, lo, ldl, vec);
+    HK_LAUNCH_CHECK();
+}
 
 void gemm_f32_simt(const GemmArgs &a, cudaStream_t s) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return;

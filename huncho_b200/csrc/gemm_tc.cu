@@ -34,6 +34,7 @@ namespace hk {
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+enum : int { kPassF16 = 0, kPassF8 = 1, kPassTF32 = 2 };
 constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
 constexpr int TMEM_COLS = 2 * BN;           // double-buffered accumulator
@@ -45,7 +46,12 @@ constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + EPI_BYTES 
 struct TcParams {
     int M, N, K;
     int m_tiles, n_tiles, k_blocks;
-    int k_blocks_lo;  // split-precision input: 128-wide K blocks of x_lo / w8 after the fp16 ones (0 = none)
+    // The K loop of a tile as up to three passes over 128-byte stage rows, each
+    // with its operand maps (0: tm_x / tm_w, 1: tm_xl / tm_wl), its K elements
+    // per block (64 fp16, 128 8-bit, 32 tf32) and its MMA kind (kPass*).
+    int n_pass;
+    int pass_kb[3], pass_kw[3], pass_a[3], pass_b[3], pass_kind[3];
+    int total_kb;
     uint8_t *out_lo;  // SwiGLU: e5m2 residual of the fp16 output, or null
     int ldo_lo;
     int n_fast;  // tile order: N fastest (narrow N: the N tiles of one M tile run together, X read once)
@@ -126,23 +132,22 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
                 const int m_blk = p.n_fast ? tile / p.n_tiles : tile % p.m_tiles;
                 const int n_blk = p.n_fast ? tile % p.n_tiles : tile / p.m_tiles;
-                for (int kb = 0; kb < p.k_blocks + p.k_blocks_lo; ++kb) {
+                for (int kb = 0, ps = 0, lk = 0; kb < p.total_kb; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1)) {
                         set_error(p.err, kErrWaitTimeout);
                         *abort_flag = 1;
                         break;
                     }
-                    // fp16 blocks: 64 K columns = 128 bytes per row; then the
-                    // 8-bit low-part blocks: 128 K columns = 128 bytes per row
-                    // (the same stage geometry).
+                    // Every pass's block is 128 bytes per row (the same stage geometry).
                     mbar_expect_tx(&full[stage], A_STAGE_BYTES + B_STAGE_BYTES);
-                    if (kb < p.k_blocks) {
-                        tma_load_2d(sA + stage * A_STAGE_BYTES, &tm_x, &full[stage], kb * BK, m_blk * BM);
-                        tma_load_2d(sB + stage * B_STAGE_BYTES, &tm_w, &full[stage], kb * BK, n_blk * BN);
-                    } else {
-                        const int kl = (kb - p.k_blocks) * 128;
-                        tma_load_2d(sA + stage * A_STAGE_BYTES, &tm_xl, &full[stage], kl, m_blk * BM);
-                        tma_load_2d(sB + stage * B_STAGE_BYTES, &tm_wl, &full[stage], kl, n_blk * BN);
+                    const int kx = lk * p.pass_kw[ps];
+                    tma_load_2d(sA + stage * A_STAGE_BYTES, p.pass_a[ps] ? &tm_xl : &tm_x, &full[stage], kx,
+                                m_blk * BM);
+                    tma_load_2d(sB + stage * B_STAGE_BYTES, p.pass_b[ps] ? &tm_wl : &tm_w, &full[stage], kx,
+                                n_blk * BN);
+                    if (++lk == p.pass_kb[ps]) {
+                        lk = 0;
+                        ++ps;
                     }
                     issued_mask |= 1u << stage;
                     issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -163,6 +168,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             // ------------------------------------------------ MMA issuer
             constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
             constexpr uint32_t idesc8 = idesc_e5m2_e4m3_f32(BM, BN);
+            constexpr uint32_t idesc32 = idesc_tf32_f32(BM, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -175,7 +181,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < p.k_blocks + p.k_blocks_lo; ++kb) {
+                for (int kb = 0, ps = 0, lk = 0; kb < p.total_kb; ++kb) {
                     if (!mbar_wait(&full[stage], phase)) {
                         set_error(p.err, kErrWaitTimeout);
                         *abort_flag = 1;
@@ -184,15 +190,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tc_fence_after();
                     const uint32_t a0 = smem_addr(sA + stage * A_STAGE_BYTES);
                     const uint32_t b0 = smem_addr(sB + stage * B_STAGE_BYTES);
-                    if (kb < p.k_blocks) {
+                    // Four MMAs per 128-byte row: K = 16 fp16, 32 8-bit or 8 tf32 each.
+                    const int kind = p.pass_kind[ps];
 #pragma unroll
-                        for (int k = 0; k < BK / 16; ++k)
-                            mma_f16(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32), idesc,
-                                    (kb | k) != 0);
-                    } else {
-#pragma unroll
-                        for (int k = 0; k < 4; ++k)  // 4 x K=32 8-bit steps per 128-byte row
-                            mma_f8(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32), idesc8, 1u);
+                    for (int k = 0; k < 4; ++k) {
+                        const uint64_t ad = desc_kmajor_sw128(a0 + k * 32), bd = desc_kmajor_sw128(b0 + k * 32);
+                        const uint32_t acc = (kb | k) != 0;
+                        if (kind == kPassF16)
+                            mma_f16(d_tmem, ad, bd, idesc, acc);
+                        else if (kind == kPassF8)
+                            mma_f8(d_tmem, ad, bd, idesc8, acc);
+                        else
+                            mma_tf32(d_tmem, ad, bd, idesc32, acc);
+                    }
+                    if (++lk == p.pass_kb[ps]) {
+                        lk = 0;
+                        ++ps;
                     }
                     mma_commit(&empty[stage]);
                     if (++stage == STAGES) {
@@ -470,7 +483,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int tile = pair; tile < num_tiles && !*abort_flag; tile += n_pairs) {
                 const int m_blk = p.n_fast ? tile / p.n_tiles : tile % p.m_tiles;
                 const int n_blk = p.n_fast ? tile % p.n_tiles : tile / p.m_tiles;
-                for (int kb = 0; kb < p.k_blocks + p.k_blocks_lo; ++kb) {
+                for (int kb = 0, ps = 0, lk = 0; kb < p.total_kb; ++kb) {
                     if (!mbar_wait_cluster(&empty[stage], phase ^ 1)) {
                         set_error(p.err, kErrWaitTimeout);
                         *abort_flag = 1;
@@ -478,12 +491,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     const uint32_t bar0 = mapa_shared(smem_addr(&full[stage]), 0);
                     if (rank == 0) mbar_expect_tx(&full[stage], 2 * (P_A_BYTES + P_B_BYTES));
-                    const bool hi = kb < p.k_blocks;
-                    const int kx = hi ? kb * BK : (kb - p.k_blocks) * 128;
-                    tma_load_2d_pair(sA + stage * P_A_BYTES, hi ? &tm_x : &tm_xl, bar0, kx,
+                    const int kx = lk * p.pass_kw[ps];
+                    tma_load_2d_pair(sA + stage * P_A_BYTES, p.pass_a[ps] ? &tm_xl : &tm_x, bar0, kx,
                                      m_blk * (2 * BM) + static_cast<int>(rank) * BM);
-                    tma_load_2d_pair(sB + stage * P_B_BYTES, hi ? &tm_w : &tm_wl, bar0, kx,
+                    tma_load_2d_pair(sB + stage * P_B_BYTES, p.pass_b[ps] ? &tm_wl : &tm_w, bar0, kx,
                                      n_blk * BN + static_cast<int>(rank) * BM);
+                    if (++lk == p.pass_kb[ps]) {
+                        lk = 0;
+                        ++ps;
+                    }
                     ++issued;
                     if (++stage == P_STAGES) {
                         stage = 0;
@@ -510,6 +526,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             // ------------------------------------------------ MMA issuer (first CTA)
             constexpr uint32_t idesc = idesc_f16_f32(2 * BM, BN);
             constexpr uint32_t idesc8 = idesc_e5m2_e4m3_f32(2 * BM, BN);
+            constexpr uint32_t idesc32 = idesc_tf32_f32(2 * BM, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -523,7 +540,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < p.k_blocks + p.k_blocks_lo; ++kb) {
+                for (int kb = 0, ps = 0, lk = 0; kb < p.total_kb; ++kb) {
                     if (!mbar_wait_cluster(&full[stage], phase)) {
                         set_error(p.err, kErrWaitTimeout);
                         *abort_flag = 1;
@@ -532,16 +549,21 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tc_fence_after();
                     const uint32_t a0 = smem_addr(sA + stage * P_A_BYTES);
                     const uint32_t b0 = smem_addr(sB + stage * P_B_BYTES);
-                    if (kb < p.k_blocks) {
+                    const int kind = p.pass_kind[ps];
 #pragma unroll
-                        for (int k = 0; k < BK / 16; ++k)
-                            mma_f16_pair(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32),
-                                         idesc, (kb | k) != 0);
-                    } else {
-#pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            mma_f8_pair(d_tmem, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32),
-                                        idesc8, 1u);
+                    for (int k = 0; k < 4; ++k) {
+                        const uint64_t ad = desc_kmajor_sw128(a0 + k * 32), bd = desc_kmajor_sw128(b0 + k * 32);
+                        const uint32_t acc = (kb | k) != 0;
+                        if (kind == kPassF16)
+                            mma_f16_pair(d_tmem, ad, bd, idesc, acc);
+                        else if (kind == kPassF8)
+                            mma_f8_pair(d_tmem, ad, bd, idesc8, acc);
+                        else
+                            mma_tf32_pair(d_tmem, ad, bd, idesc32, acc);
+                    }
+                    if (++lk == p.pass_kb[ps]) {
+                        lk = 0;
+                        ++ps;
                     }
                     mma_commit_pair(smem_addr(&empty[stage]));
                     mma_commit_pair(mapa_shared(smem_addr(&empty[stage]), peer));
@@ -764,8 +786,9 @@ EncodeTiledFn encode_fn() {
 
 }  // namespace
 
-CUtensorMap tensor_map_f16(const void *base, uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
-                           uint32_t box_cols, uint32_t box_rows) {
+namespace {
+CUtensorMap tensor_map_2d(CUtensorMapDataType t, const void *base, uint64_t rows, uint64_t cols,
+                          uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows) {
     if ((reinterpret_cast<uintptr_t>(base) & 15) || row_stride_bytes % 16)
         throw CudaError("tensor map base must be 16-byte aligned with a row stride % 16 == 0");
     CUtensorMap m;
@@ -773,11 +796,22 @@ CUtensorMap tensor_map_f16(const void *base, uint64_t rows, uint64_t cols, uint6
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_bytes)};
     cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box,
-                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+    CUresult r = encode_fn()(&m, t, 2, const_cast<void *>(base), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(r));
     return m;
+}
+}  // namespace
+
+CUtensorMap tensor_map_f16(const void *base, uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
+                           uint32_t box_cols, uint32_t box_rows) {
+    return tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, rows, cols, row_stride_bytes, box_cols, box_rows);
+}
+
+CUtensorMap tensor_map_f32(const void *base, uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
+                           uint32_t box_cols, uint32_t box_rows) {
+    return tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, rows, cols, row_stride_bytes, box_cols, box_rows);
 }
 
 namespace {
@@ -817,19 +851,54 @@ CUtensorMap make_map8(const void *base, int rows, int inner, int ld, int box_row
     return m;
 }
 
-// The split-precision fields of the launch: low-part maps and block count
-// (zeroed maps and no blocks without a low part), the SwiGLU low output.
-void set_split(const GemmArgs &a, int w_box_rows, TcParams &p, CUtensorMap &txl, CUtensorMap &twl) {
+// A 2-D fp32 tensor map (the 3xTF32 operands): box of box_rows x 32
+// elements (one 128-byte swizzle row), zero fill.
+CUtensorMap make_map32(const void *base, int rows, int inner, int ld, int box_rows) {
+    return tensor_map_f32(base, rows, inner, static_cast<uint64_t>(ld) * 4, 32, box_rows);
+}
+
+// The operand maps and the K-pass table of a launch: fp16 (64-wide blocks),
+// optionally followed by the 8-bit low part (128-wide blocks), or the three
+// tf32 passes (32-wide blocks); plus the SwiGLU low output.
+void set_passes(const GemmArgs &a, int w_box_rows, TcParams &p, CUtensorMap &tx, CUtensorMap &tw, CUtensorMap &txl,
+                CUtensorMap &twl) {
     std::memset(&txl, 0, sizeof(txl));
     std::memset(&twl, 0, sizeof(twl));
-    p.k_blocks_lo = 0;
-    if (a.x_lo && a.w8) {
-        txl = make_map8(a.x_lo, a.M, a.K, a.ldx_lo, BM);
-        twl = make_map8(a.w8, a.N, a.K, a.ldw8, w_box_rows);
-        p.k_blocks_lo = ceil_div(a.K, 128);
-    } else if (a.x_lo || a.w8) {
-        throw CudaError("a split-precision GEMM needs both x_lo and w8");
+    auto pass = [&](int kb, int kw, int as, int bs, int kind) {
+        p.pass_kb[p.n_pass] = kb;
+        p.pass_kw[p.n_pass] = kw;
+        p.pass_a[p.n_pass] = as;
+        p.pass_b[p.n_pass] = bs;
+        p.pass_kind[p.n_pass] = kind;
+        ++p.n_pass;
+    };
+    p.n_pass = 0;
+    if (a.tf32) {
+        if (!a.x_lo32 || !a.w_lo32) throw CudaError("a 3xTF32 GEMM needs x_lo32 and w_lo32");
+        if (a.epilogue != kEpiResidual && a.epilogue != kEpiStoreF32)
+            throw CudaError("the 3xTF32 GEMM stores fp32 outputs only");
+        tx = make_map32(a.x, a.M, a.K, a.ldx, BM);
+        tw = make_map32(a.w, a.N, a.K, a.ldw, w_box_rows);
+        txl = make_map32(a.x_lo32, a.M, a.K, a.ldx_lo32, BM);
+        twl = make_map32(a.w_lo32, a.N, a.K, a.ldw_lo32, w_box_rows);
+        const int kb = ceil_div(a.K, 32);
+        pass(kb, 32, 0, 0, kPassTF32);  // x   w
+        pass(kb, 32, 0, 1, kPassTF32);  // x   w_lo
+        pass(kb, 32, 1, 0, kPassTF32);  // x_lo w
+    } else {
+        tx = make_map(a.x, a.M, a.K, a.ldx, BM);
+        tw = make_map(a.w, a.N, a.K, a.ldw, w_box_rows);
+        pass(ceil_div(a.K, BK), BK, 0, 0, kPassF16);
+        if (a.x_lo && a.w8) {
+            txl = make_map8(a.x_lo, a.M, a.K, a.ldx_lo, BM);
+            twl = make_map8(a.w8, a.N, a.K, a.ldw8, w_box_rows);
+            pass(ceil_div(a.K, 128), 128, 1, 1, kPassF8);
+        } else if (a.x_lo || a.w8) {
+            throw CudaError("a split-precision GEMM needs both x_lo and w8");
+        }
     }
+    p.total_kb = 0;
+    for (int i = 0; i < p.n_pass; ++i) p.total_kb += p.pass_kb[i];
     p.out_lo = a.epilogue == kEpiSwiGLU ? a.out_lo : nullptr;
     p.ldo_lo = a.ldo_lo;
     if (p.out_lo && ((reinterpret_cast<uintptr_t>(p.out_lo) & 15) || p.ldo_lo % 16))
@@ -857,18 +926,16 @@ template <int EPI>
 void launch(const GemmArgs &a, cudaStream_t s, int num_sms) {
     static SmemOptIn opt_in;
     opt_in.ensure(gemm_f16_tc_kernel<EPI>, SMEM_BYTES);
-    CUtensorMap tx = make_map(a.x, a.M, a.K, a.ldx, BM);
-    CUtensorMap tw = make_map(a.w, a.N, a.K, a.ldw, BN);
     TcParams p;
-    CUtensorMap txl, twl;
-    set_split(a, BN, p, txl, twl);
+    CUtensorMap tx, tw, txl, twl;
+    set_passes(a, BN, p, tx, tw, txl, twl);
     p.M = a.M;
     p.N = a.N;
     p.K = a.K;
     p.m_tiles = ceil_div(a.M, BM);
     p.n_tiles = ceil_div(a.N, BN);
     p.n_fast = p.n_tiles <= 8 ? 1 : 0;
-    p.k_blocks = ceil_div(a.K, BK);
+
     p.out = a.out;
     p.ldo = a.ldo;
     p.scale = a.scale;
@@ -890,18 +957,16 @@ template <int EPI>
 void launch_pair(const GemmArgs &a, cudaStream_t s, int num_sms) {
     static SmemOptIn opt_in;
     opt_in.ensure(gemm_f16_tc2_kernel<EPI>, P_SMEM_BYTES);
-    CUtensorMap tx = make_map(a.x, a.M, a.K, a.ldx, BM);
-    CUtensorMap tw = make_map(a.w, a.N, a.K, a.ldw, BM);  // each CTA loads 128 rows of W
     TcParams p;
-    CUtensorMap txl, twl;
-    set_split(a, BM, p, txl, twl);
+    CUtensorMap tx, tw, txl, twl;
+    set_passes(a, BM, p, tx, tw, txl, twl);  // each CTA of a pair loads 128 rows of W
     p.M = a.M;
     p.N = a.N;
     p.K = a.K;
     p.m_tiles = ceil_div(a.M, 2 * BM);
     p.n_tiles = ceil_div(a.N, BN);
     p.n_fast = p.n_tiles <= 8 ? 1 : 0;
-    p.k_blocks = ceil_div(a.K, BK);
+
     p.out = a.out;
     p.ldo = a.ldo;
     p.scale = a.scale;

@@ -329,6 +329,8 @@ struct Mat {
     // of the int8 values (the row scale applies to both parts).
     uint8_t *w8 = nullptr;
     int ld8 = 0;
+    // fp32 model: w - tf32(w) [rows, ld] for the 3xTF32 tensor-core GEMM.
+    float *w_lo = nullptr;
     // Packed profiles: int8 block values [rows, kp] and fp32 block scales [rows, kp / 32].
     int8_t *q = nullptr;
     float *qd = nullptr;
@@ -391,6 +393,8 @@ struct Model {
     // ld_xl / ld_mixl / ld_fl bytes), or null.
     uint8_t *xn_lo = nullptr, *mix_lo = nullptr, *ffn_lo = nullptr;
     int ld_xl = 0, ld_mixl = 0, ld_fl = 0;
+    float *x_lo32 = nullptr;  // fp32 model: x - tf32(x) of the projection input in flight
+    int ld_lo32 = 0;
     float *proj = nullptr;  // projection outputs, always fp32
     float *dq = nullptr, *dkk = nullptr, *dvv = nullptr, *dg = nullptr, *db = nullptr, *dout = nullptr;
     void *aq = nullptr, *ak = nullptr, *av = nullptr;
@@ -649,6 +653,10 @@ struct Model {
             float *d = dev_alloc<float>(h.size(), walloc());
             HK_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
             m.w = d;
+            // The low part of each weight for the 3xTF32 GEMM.
+            for (auto &v : h) v -= tf32_trunc_host(v);
+            m.w_lo = dev_alloc<float>(h.size(), walloc());
+            HK_CUDA(cudaMemcpy(m.w_lo, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
         } else if (dtype == HK_DTYPE_INT8W) {
             m.ld = round_up(K, 16);  // the int8 rows double as the e4m3 rows' layout
             // Symmetric per-output-channel int8: scale = max|w| / 127,
@@ -953,6 +961,10 @@ struct Model {
         proj = dev_alloc<float>(N * ldp, ws);
         mix = dev_alloc<uint8_t>(N * ldmix * e, ws);
         ffn = dev_alloc<uint8_t>(N * ldf * e, ws);
+        if (dtype == HK_DTYPE_FP32) {
+            ld_lo32 = round_up(std::max(std::max(ld_xn, ldmix), std::max(ldf, ldp)), 4);
+            x_lo32 = dev_alloc<float>(N * ld_lo32, ws);
+        }
         if (split_inputs()) {
             ld_xl = round_up(c.hidden, 16);
             ld_mixl = round_up(ldmix, 16);
@@ -1034,6 +1046,15 @@ struct Model {
                 throw ApiError(HK_ERR_UNSUPPORTED, "packed projections store fp32 outputs only");
             launch_quantize_rows(static_cast<const float *>(xin), ldx, M, W.cols, W.kp, xq, xd, stream);
             gemm_q8(xq, xd, W.q, W.qd, M, W.rows, W.kp, static_cast<float *>(out), ldo, epi == kEpiResidual, stream);
+        } else if (W.w_lo) {
+            // fp32 model: 3xTF32 on the tensor cores.
+            launch_tf32_lo(static_cast<const float *>(xin), ldx, M, W.cols, x_lo32, ld_lo32, stream);
+            a.tf32 = true;
+            a.x_lo32 = x_lo32;
+            a.ldx_lo32 = ld_lo32;
+            a.w_lo32 = W.w_lo;
+            a.ldw_lo32 = W.ld;
+            gemm_f16_tc(a, stream, num_sms);
         } else if (f32_model()) {
             gemm_f32_simt(a, stream);
         } else {

@@ -1,6 +1,8 @@
 // Kernel-level C entry points (include/huncho_kev_ops.h) for per-kernel
 // parity tests and timing.
+#include <algorithm>
 #include <cmath>
+#include <exception>
 #include <string>
 
 #include "../../include/huncho_kev.h"
@@ -72,8 +74,32 @@ int hk_op_gemm(int dtype, int epilogue, int M, int N, int K, const void *x, int 
             hk::gemm_f16_tc(a, s, current_sms());
         else if (dtype == 2)
             hk::gemm_f16_tc_pair(a, s, current_sms());
-        else
-            throw std::runtime_error("hk_op_gemm: dtype must be 0 (fp32), 1 (fp16) or 2 (fp16, CTA pairs)");
+        else if (dtype == 3) {
+            // 3xTF32: the low parts of x and w in stream-ordered scratch.
+            if (!x || !w || (ldx % 4) || (ldw % 4)) throw std::invalid_argument("hk_op_gemm: bad fp32 operands");
+            const int ldl = (K + 3) / 4 * 4;
+            float *xl = nullptr, *wl = nullptr;
+            HK_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&xl), static_cast<size_t>(std::max(M, 1)) * ldl * 4, s));
+            HK_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&wl), static_cast<size_t>(std::max(N, 1)) * ldl * 4, s));
+            hk::launch_tf32_lo(static_cast<const float *>(x), ldx, M, K, xl, ldl, s);
+            hk::launch_tf32_lo(static_cast<const float *>(w), ldw, N, K, wl, ldl, s);
+            a.tf32 = true;
+            a.x_lo32 = xl;
+            a.ldx_lo32 = ldl;
+            a.w_lo32 = wl;
+            a.ldw_lo32 = ldl;
+            std::exception_ptr err;
+            try {
+                hk::gemm_f16_tc(a, s, current_sms());
+            } catch (...) {
+                err = std::current_exception();
+            }
+            cudaFreeAsync(xl, s);
+            cudaFreeAsync(wl, s);
+            if (err) std::rethrow_exception(err);
+        } else
+            throw std::runtime_error(
+                "hk_op_gemm: dtype must be 0 (fp32), 1 (fp16), 2 (fp16, CTA pairs) or 3 (fp32 as 3xTF32)");
     });
 }
 

@@ -236,6 +236,32 @@ __host__ __device__ constexpr uint32_t idesc_e5m2_e4m3_f32(int M, int N) {
     return (1u << 4) | (1u << 7) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Instruction descriptor for kind::tf32 (A and B format TF32 = 2: fp32 data of
+// which the MMA uses sign, exponent and the top 10 mantissa bits), fp32
+// accumulation, both K-major; K is 8 per instruction (32 bytes of a row).
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T with 8-bit float operands (kind::f8f6f4).
 // Accumulates into the same fp32 TMEM accumulator as kind::f16 instructions.
 __device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -395,5 +421,8 @@ __host__ __device__ __forceinline__ uint32_t sw128_off(int R, int r, int k) {
 // elements, 128-byte swizzle (box_cols * 2 == 128) and zero fill outside the
 // tensor. Throws CudaError when the driver rejects it.
 CUtensorMap tensor_map_f16(const void *base, uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
+                           uint32_t box_cols, uint32_t box_rows);
+// The same for fp32 elements (box_cols * 4 == 128).
+CUtensorMap tensor_map_f32(const void *base, uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
                            uint32_t box_cols, uint32_t box_rows);
 }  // namespace hk

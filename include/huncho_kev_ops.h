@@ -20,7 +20,10 @@ extern "C" {
  * 1: fp16 X/W (tcgen05 tensor cores, fp32 accumulation; single CTAs or CTA
  * pairs chosen by shape, as the model runs it), 2: fp16 X/W always on CTA
  * pairs (clusters of two CTAs sharing one cta_group::2 MMA on 256 x 256
- * tiles; the same results as 1). `epilogue` 0: store
+ * tiles; the same results as 1), 3: fp32 X/W on the tensor cores as three
+ * tf32 products (x w + x w_lo + x_lo w with v_lo = v - tf32(v); ~2^-20
+ * relative error; epilogues 1 and 3; the low parts live in stream-ordered
+ * scratch for the call). `epilogue` 0: store
  * (fp16 for dtype 1), 1: fp32 residual add into out, 2: SwiGLU over 128-row
  * gate/up blocks (fp16), 3: store fp32. `scale` (nullable) multiplies output column n by scale[n].
  * Replaces one Linear::forward of the backbone (qwen3_5.rs:306-515). */

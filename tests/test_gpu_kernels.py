@@ -614,3 +614,29 @@ def test_split_gemm_swiglu_writes_low_part(lib):
     torch.testing.assert_close(out.float(), y, rtol=2e-3, atol=2e-3)
     two = out.float() + lo.view(torch.float8_e5m2).float()
     assert (two - y).abs().max() < (out.float() - y).abs().max() / 3
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 5, 8), (70, 130, 16), (256, 1000, 1024), (256, 8224, 1024), (600, 1024, 3584)])
+def test_tf32x3_gemm_f32(lib, M, N, K):
+    """The fp32 model's projections on the tensor cores (hk_op_gemm dtype 3:
+    three kind::tf32 products) against an fp32 matmul, store and residual
+    epilogues. The operands carry ~2^-20 relative error; the tensor core's
+    accumulator adds up to about half an fp32 ulp of the running sum per K step
+    (measured: 5.4e-4 on outputs of 15 at K = 3584), so the bound is
+    (2e-5 + K 2^-24) of the output scale; a single tf32 product would be ~1e-3
+    relative regardless of K."""
+    g = torch.Generator(device="cuda").manual_seed(M + 3 * K)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.05
+    ref = x @ w.T
+    tol = 2e-5 + K * 2.0 ** -24
+    out = torch.zeros(M, N, device="cuda")
+    gemm(lib, 3, 3, x, w, out)
+    scale = ref.abs().max().item() + 1e-30
+    err = (out - ref).abs().max().item()
+    print(f"3xTF32 {M}x{N}x{K}: max err {err:.3g} of scale {scale:.3g}")
+    assert err <= tol * scale
+    res = torch.randn(M, N, device="cuda", generator=g)
+    out2 = res.clone()
+    gemm(lib, 3, 1, x, w, out2)
+    assert (out2 - (res + ref)).abs().max().item() <= tol * (scale + res.abs().max().item())
