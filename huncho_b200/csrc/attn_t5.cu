@@ -165,28 +165,36 @@ __global__ void __launch_bounds__(THREADS, 1)
             cpa16(dst + sw128_off(BKV, r, c_own * 8), src, ok);
         }
     };
-    // TMA form (thread 0): a K or V tile of 64 keys as boxes of R = min(page,
-    // 64) rows x 64 columns (one 128-byte swizzle row) per 64-column block of
-    // the head; pages past the row's last one read that last page instead (its
-    // values are finite; those keys are masked and their V rows zeroed).
+    // TMA form (warp 0, every lane): a K or V tile of 64 keys as boxes of
+    // R = min(page, 64) rows x 64 columns (one 128-byte swizzle row) per
+    // 64-column block of the head, one box per lane (at most 16), so the page
+    // table lookups run in parallel; pages past the row's last one read that
+    // last page instead (its values are finite; those keys are masked and
+    // their V rows zeroed).
     const int R = pt ? (pt < BKV ? pt : BKV) : BKV;
     const int last_page = pt ? (len - 1) >> pshift : 0;
+    const int lane = tid & 31;
     uint32_t kv_pend = 0;  // bit b: K buffer b, bit 2 + b: V buffer b has a load in flight
+    constexpr int KT = HD / 64;
+    const int nbox = (BKV / R) * KT;
+    // K and V tiles are each loaded in order (tiles 0, 1, 2, ...): this lane's
+    // page-table entry for the next tile of each stream is read one call
+    // ahead, so the lookup's latency is off the issue path.
+    auto page_of = [&](int j) { return ptab[(j >> pshift) < last_page ? (j >> pshift) : last_page]; };
+    int pg_k = 0, pg_v = 0;
+    if (TMA && pt && warp == 0 && lane < nbox) pg_k = pg_v = page_of((lane / KT) * R);
     auto tma_kv = [&](bool is_v, int kv0, int b) {
         uint8_t *dst = sm + (is_v ? L::V0 : L::K0) + b * L::KV_BYTES;
         uint64_t *bar = is_v ? &bar_v[b] : &bar_k[b];
-        mbar_expect_tx(bar, L::KV_BYTES);
+        if (lane == 0) mbar_expect_tx(bar, L::KV_BYTES);
+        __syncwarp();
         const CUtensorMap *m = is_v ? &tm_v : &tm_k;
-        for (int r0 = 0; r0 < BKV; r0 += R) {
-            const int j = kv0 + r0;
-            int slot = start + j;
-            if (pt) {
-                const int pidx = (j >> pshift) < last_page ? (j >> pshift) : last_page;
-                slot = (ptab[pidx] << pshift) + (j & (pt - 1));
-            }
-#pragma unroll
-            for (int kt = 0; kt < HD / 64; ++kt)
-                tma_load_2d(dst + kt * BKV * 128 + r0 * 128, m, bar, kh * HD + kt * 64, slot);
+        if (lane < nbox) {
+            const int r0 = (lane / KT) * R, kt = lane % KT, j = kv0 + r0;
+            int &pg = is_v ? pg_v : pg_k;
+            const int slot = pt ? (pg << pshift) + (j & (pt - 1)) : start + j;
+            tma_load_2d(dst + kt * BKV * 128 + r0 * 128, m, bar, kh * HD + kt * 64, slot);
+            if (pt) pg = page_of(j + BKV);
         }
         kv_pend |= 1u << (is_v ? 2 + b : b);
     };
@@ -232,6 +240,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int kt = 0; kt < HD / 64; ++kt)
                 tma_load_2d(sm + L::Q + kt * BM * 128, &tm_q, bar_q, h * HD + kt * 64, start + q0);
+        }
+        if (warp == 0) {
             tma_kv(false, 0, 0);
             tma_kv(true, 0, 0);
             if (n_tiles > 1) tma_kv(false, BKV, 1);
@@ -302,7 +312,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         ph_s ^= 1u << b;
         tc_fence_after();
         if constexpr (TMA) {
-            if (it + 2 < n_tiles && tid == 0) tma_kv(false, kv0 + 2 * BKV, b);
+            if (it + 2 < n_tiles && warp == 0) tma_kv(false, kv0 + 2 * BKV, b);
         } else {
             if (it + 2 < n_tiles) load_kv(false, kv0 + 2 * BKV, b);
             cpa_commit();
@@ -349,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
         }
         if constexpr (TMA) {
-            if (it + 1 < n_tiles && tid == 0) tma_kv(true, kv0 + BKV, (it + 1) & 1);
+            if (it + 1 < n_tiles && warp == 0) tma_kv(true, kv0 + BKV, (it + 1) & 1);
         } else {
             if (it + 1 < n_tiles) load_kv(true, kv0 + BKV, (it + 1) & 1);
             cpa_commit();
