@@ -159,6 +159,25 @@ KERNEL_NAMES = {
     "embed": "embed_kernel",
 }
 TENSOR_CLASSES = ("gemm", "delta", "attention")
+# The fp32-activation paths (the fp32 model and the packed profiles) run other
+# kernels in some classes.
+FP32_ACT_KERNELS = {
+    "delta": "delta_recurrent_kernel (the reference's per-token order, fp32)",
+    "attention": "attn_simt_kernel (fp32 causal GQA attention on CUDA cores)",
+}
+PACKED_DTYPES = ("q8_0-fp32", "q4_0-fp32")
+
+
+def kernel_label(cls, dtype):
+    """(kernel name, bound) of a profile class under a model dtype."""
+    if cls == "gemm" and dtype in PACKED_DTYPES:
+        return ("quantize_rows_kernel + gemm_q8_tc_kernel (tcgen05 kind::i8 packed projections, block scales "
+                "in the epilogue; int8 ops against the bf16 peak, no measured int8 peak)", "tensor")
+    if cls == "gemm" and dtype == "fp32":
+        return "gemm_f16_tc_kernel (3xTF32 projections: three kind::tf32 products per tile)", "tensor"
+    if (dtype == "fp32" or dtype in PACKED_DTYPES) and cls in FP32_ACT_KERNELS:
+        return FP32_ACT_KERNELS[cls], "fp32 CUDA cores"
+    return KERNEL_NAMES.get(cls, cls), "tensor" if cls in TENSOR_CLASSES else "hbm"
 
 
 def kernel_rooflines(prof, pk, dtype):
@@ -173,9 +192,9 @@ def kernel_rooflines(prof, pk, dtype):
         if not n or ms <= 0:
             continue
         sec = ms / 1e3
-        e = {"kernel": KERNEL_NAMES.get(cls, cls), "class": cls, "launches": int(n), "avg_ms": ms / n,
-             "share": round(ms / total_ms, 4),
-             "bound": "tensor" if cls in TENSOR_CLASSES and dtype not in ("fp32",) else "hbm"}
+        name, bound = kernel_label(cls, dtype)
+        e = {"kernel": name, "class": cls, "launches": int(n), "avg_ms": ms / n,
+             "share": round(ms / total_ms, 4), "bound": bound}
         if fl:
             e["flops_per_launch"] = fl / n
             e["achieved_tflops"] = fl / sec / 1e12
@@ -680,8 +699,7 @@ def main():
                              "answer fields, D2H probabilities and answers; one host thread per replica) + "
                              "answer dicts")},
         "gpu_launches": int(launches),
-        "roofline": {"kernel": ("gemm_q8 (int8 mma.sync packed projections; int8 ops against the bf16 peak, no "
-                                "measured int8 peak)" if args.packed else "gemm_f16_tc (tcgen05 projections)"),
+        "roofline": {"kernel": kernel_label("gemm", dtype)[0],
                      "bound": "tensor", "achieved": achieved,
                      "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                      "frac": (achieved / pk["bf16_tflops_sustained"]) if achieved else None,

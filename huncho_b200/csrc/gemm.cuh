@@ -77,11 +77,15 @@ inline float tf32_trunc_host(float v) {
 }
 
 // Packed projections (GGML Q8_0 / Q4_0 weights as int8 block values [N, kp]
-// and fp32 block scales [N, kp/32]): the fp32 input rows quantized to Q8_0
-// (q int8 [M, kp], d fp32 [M, kp/32]; columns >= K are zero), then
-// out[m, n] (+)= sum over blocks in order of (float(int dot) * d_w) * d_x.
+// and fp32 block scales, block-major [kp/32, N]): the fp32 input rows
+// quantized to Q8_0 (q int8 [M, kp]; d fp32 block-major [kp/32, M]; columns
+// >= K are zero), then out[m, n] (+)= sum over blocks in order of
+// (float(int dot) * d_w) * d_x, the block dots on tcgen05 kind::i8 (xq, wq
+// 16-byte aligned).
 void launch_quantize_rows(const float *x, int ldx, int M, int K, int kp, int8_t *q, float *d, cudaStream_t s);
+// out[b * rows + r] = in[r * nb + b]: block scales [rows, nb] to block-major.
+void launch_transpose_scales(const float *in, int rows, int nb, float *out, cudaStream_t s);
 void gemm_q8(const int8_t *xq, const float *xd, const int8_t *wq, const float *wd, int M, int N, int kp, float *out,
-             int ldo, bool residual, cudaStream_t s);
+             int ldo, bool residual, cudaStream_t s, int num_sms, uint32_t *err = nullptr);
 
 }  // namespace hk

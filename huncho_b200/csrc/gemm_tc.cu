@@ -814,6 +814,11 @@ CUtensorMap tensor_map_f32(const void *base, uint64_t rows, uint64_t cols, uint6
     return tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, rows, cols, row_stride_bytes, box_cols, box_rows);
 }
 
+CUtensorMap tensor_map_u8(const void *base, uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
+                          uint32_t box_cols, uint32_t box_rows) {
+    return tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, base, rows, cols, row_stride_bytes, box_cols, box_rows);
+}
+
 namespace {
 
 // A 2-D fp16 tensor map over rows x inner (row stride ld elements) with a

@@ -331,7 +331,8 @@ struct Mat {
     int ld8 = 0;
     // fp32 model: w - tf32(w) [rows, ld] for the 3xTF32 tensor-core GEMM.
     float *w_lo = nullptr;
-    // Packed profiles: int8 block values [rows, kp] and fp32 block scales [rows, kp / 32].
+    // Packed profiles: int8 block values [rows, kp] and fp32 block scales,
+    // block-major [kp / 32, rows] (a warp's 32 rows read one line per block).
     int8_t *q = nullptr;
     float *qd = nullptr;
     int kp = 0;
@@ -705,7 +706,8 @@ struct Model {
     }
 
     // Packed projections: the artifact's Q8_0 / Q4_0 blocks of each part,
-    // rows concatenated, as int8 values (Q4_0 as q - 8) and fp32 scales.
+    // rows concatenated, as int8 values (Q4_0 as q - 8) and fp32 scales
+    // (block-major).
     Mat pack_blocks(const WeightSource &src, const std::vector<std::pair<std::string, int>> &parts, int K) {
         const uint32_t want = dtype == HK_DTYPE_Q8_0 ? kGgufQ8_0 : kGgufQ4_0;
         const int kp = round_up(K, 32), nb = kp / 32;
@@ -729,7 +731,7 @@ struct Model {
                     const uint8_t *blk = t->data + (static_cast<size_t>(r) * nb + b) * per;
                     uint16_t h;
                     std::memcpy(&h, blk, 2);
-                    d[static_cast<size_t>(r0 + r) * nb + b] = f16_bits_to_f32(h);
+                    d[static_cast<size_t>(b) * R + r0 + r] = f16_bits_to_f32(h);
                     int8_t *dst = &q[static_cast<size_t>(r0 + r) * kp + b * 32];
                     if (want == kGgufQ8_0) {
                         std::memcpy(dst, blk + 2, 32);
@@ -1045,7 +1047,8 @@ struct Model {
             if (epi != kEpiStoreF32 && epi != kEpiResidual)
                 throw ApiError(HK_ERR_UNSUPPORTED, "packed projections store fp32 outputs only");
             launch_quantize_rows(static_cast<const float *>(xin), ldx, M, W.cols, W.kp, xq, xd, stream);
-            gemm_q8(xq, xd, W.q, W.qd, M, W.rows, W.kp, static_cast<float *>(out), ldo, epi == kEpiResidual, stream);
+            gemm_q8(xq, xd, W.q, W.qd, M, W.rows, W.kp, static_cast<float *>(out), ldo, epi == kEpiResidual, stream,
+                    num_sms, err);
         } else if (W.w_lo) {
             // fp32 model: 3xTF32 on the tensor cores.
             launch_tf32_lo(static_cast<const float *>(xin), ldx, M, W.cols, x_lo32, ld_lo32, stream);

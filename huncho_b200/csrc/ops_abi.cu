@@ -140,8 +140,22 @@ int hk_op_gemm_packed(int M, int N, int K, int kp, const float *x, int ldx, cons
         if (M < 0 || N < 0 || K < 0 || kp <= 0 || kp % 32 != 0 || K > kp || ldx < K || ldo < N)
             throw std::runtime_error("hk_op_gemm_packed: bad shape");
         cudaStream_t s = static_cast<cudaStream_t>(stream);
-        hk::launch_quantize_rows(x, ldx, M, K, kp, x_q, x_d, s);
-        hk::gemm_q8(x_q, x_d, w_q, w_d, M, N, kp, out, ldo, residual != 0, s);
+        if (M == 0 || N == 0) return;
+        // The kernel reads block scales block-major: w_d [N, kp/32] transposed
+        // into stream-ordered scratch; x_d is written block-major [kp/32, M].
+        const int nb = kp / 32;
+        float *wdt = nullptr;
+        HK_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&wdt), static_cast<size_t>(N) * nb * 4, s));
+        std::exception_ptr err;
+        try {
+            hk::launch_transpose_scales(w_d, N, nb, wdt, s);
+            hk::launch_quantize_rows(x, ldx, M, K, kp, x_q, x_d, s);
+            hk::gemm_q8(x_q, x_d, w_q, wdt, M, N, kp, out, ldo, residual != 0, s, current_sms());
+        } catch (...) {
+            err = std::current_exception();
+        }
+        cudaFreeAsync(wdt, s);
+        if (err) std::rethrow_exception(err);
     });
 }
 

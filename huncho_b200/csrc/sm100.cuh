@@ -64,6 +64,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     }
 }
 
+// mbar_wait for a single-thread role (a TMA producer or an MMA issuer) that
+// shares its SM sub-partition with compute warps: between polls it sleeps
+// `ns`, so the poll loop does not take issue slots from them. Same 2 s bound.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity, uint32_t ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        __nanosleep(ns);
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) return false;
+    }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -262,6 +275,24 @@ __device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t adesc, u
         : "memory");
 }
 
+// Instruction descriptor for kind::i8: signed 8-bit A and B (format 1 in bits
+// 7-9 and 10-12), s32 accumulation (D format 2 in bits 4-5), both K-major, no
+// saturation; K is 32 per instruction (32 bytes of a K-major 128-byte row).
+__host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+// D[tmem] (+)= A[smem] * B[smem]^T over int8 operands into an int32 accumulator.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T with 8-bit float operands (kind::f8f6f4).
 // Accumulates into the same fp32 TMEM accumulator as kind::f16 instructions.
 __device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -425,4 +456,7 @@ CUtensorMap tensor_map_f16(const void *base, uint64_t rows, uint64_t cols, uint6
 // The same for fp32 elements (box_cols * 4 == 128).
 CUtensorMap tensor_map_f32(const void *base, uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
                            uint32_t box_cols, uint32_t box_rows);
+// The same for 8-bit elements (box_cols == 128).
+CUtensorMap tensor_map_u8(const void *base, uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
+                          uint32_t box_cols, uint32_t box_rows);
 }  // namespace hk

@@ -47,11 +47,14 @@ int hk_op_gemm_split(int epilogue, int M, int N, int K, const void *x, int ldx, 
 
 /* A packed projection (the reference's Projection::Packed, qwen3_5.rs:320-369):
  * x fp32 [M, K] (leading dim ldx) quantized to Q8_0 blocks of 32 (columns >= K
- * zero; x_q int8 [M, kp] and x_d fp32 [M, kp/32] are caller-provided scratch),
- * then out fp32 [M, ldo] (+= when residual) = per output, over the blocks in
- * order, sum of (float(int dot) * w_d) * x_d, with w_q int8 [N, kp] block
- * values (Q4_0 as q - 8) and w_d fp32 [N, kp/32] block scales. kp % 32 == 0,
- * K <= kp. Device pointers. */
+ * zero; x_q int8 [M, kp] and x_d (M * kp/32 floats, written block-major) are
+ * caller-provided scratch, x_q 16-byte aligned), then out fp32 [M, ldo] (+=
+ * when residual) = per output, over the blocks in order, sum of
+ * (float(int dot) * w_d) * x_d, with w_q int8 [N, kp] block values (Q4_0 as
+ * q - 8; 16-byte aligned) and w_d fp32 [N, kp/32] block scales, fp16 values as
+ * GGML stores them (the kernel's exact rounding rests on it). The block dots
+ * run on tcgen05 kind::i8; w_d is transposed into stream-ordered scratch for
+ * the call. kp % 32 == 0, K <= kp. Device pointers. */
 int hk_op_gemm_packed(int M, int N, int K, int kp, const float *x, int ldx, const int8_t *w_q, const float *w_d,
                       int8_t *x_q, float *x_d, float *out, int ldo, int residual, void *stream);
 

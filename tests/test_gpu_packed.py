@@ -1,8 +1,9 @@
 """The reference's packed profiles (q8_0-fp32 / q4_0-fp32) on the GPU.
 
 * The packed projection kernel (Q8_0 activation quantization + per-block int8
-  tensor-core dots with the block scales applied in the reference's order)
-  equals the oracle's block-sequential definition bit for bit.
+  tcgen05 dots with the block scales applied in the reference's order)
+  equals the oracle's block-sequential definition bit for bit, on shapes with
+  ragged edges, one row, more tiles than SMs and 112 blocks per row.
 * Whole packed packages (converted from the tiny golden package and from a
   synthetic model) against the oracle's packed forward: raw logits within the
   fp32 model's gate, probabilities within the reference's own gate for packed
@@ -61,7 +62,11 @@ def _run_op(lib, x, wq, wd, K, residual=None):
 
 
 @pytest.mark.parametrize("scheme", ["q8_0", "q4_0"])
-@pytest.mark.parametrize("M,N,K", [(300, 130, 200), (1, 1, 1), (129, 65, 64), (64, 3584 // 8, 1024)])
+# (2100, 1300, 512): more 128 x 128 tiles than SMs, so CTAs run several tiles
+# (the block accumulators carry over between tiles); (700, 1100, 3584): the MLP
+# down projection's 112 blocks per row.
+@pytest.mark.parametrize("M,N,K", [(300, 130, 200), (1, 1, 1), (129, 65, 64), (64, 3584 // 8, 1024),
+                                   (2100, 1300, 512), (700, 1100, 3584)])
 def test_packed_gemm_bit_exact_vs_oracle(native_lib, scheme, M, N, K):
     from oracle import kev_oracle as ko
     rng = np.random.default_rng(M + N + K)
