@@ -11,9 +11,9 @@ fixture carries fingerprints of both, which the test checks first.
 Configurations (the workload definitions of BASELINE.json):
   cfg1  Kev-0.8B fp32 weights, fp32 model, 1 x 256 tokens, choice-4
   cfg2  Kev-0.8B bf16, all 96 question rows of the benchmark workload (seed 0)
-  cfg3  Kev-0.8B bf16 weights quantized int8 per output channel, 4 x 1024, choice-8
-  cfg4  Kev-0.8B bf16, 2 x 8192 tokens, noul
-  cfg5  Kev-4B bf16, 8 requests, lengths log-uniform in [32, 2048], mixed questions
+  cfg3  Kev-0.8B bf16 weights quantized int8 per output channel, 16 x 1024, choice-8
+  cfg4  Kev-0.8B bf16, 4 x 8192 tokens, noul
+  cfg5  Kev-4B bf16, 24 requests, lengths log-uniform in [32, 2048], mixed questions
 
 Usage: python tests/golden/make_fullsize_oracle.py [cfg1 cfg2 ...]
 """
@@ -39,9 +39,9 @@ OUT = Path(__file__).resolve().parent / "fullsize"
 CASES = {
     "cfg1": ("kev-0.8b", "fp32", "fp32", 1, 0, None),
     "cfg2": ("kev-0.8b", "bf16", "bf16", 2, 0, None),
-    "cfg3": ("kev-0.8b", "bf16", "int8w", 3, 0, 4),
-    "cfg4": ("kev-0.8b", "bf16", "bf16", 4, 0, 2),
-    "cfg5": ("kev-4b", "bf16", "bf16", 5, 0, 8),
+    "cfg3": ("kev-0.8b", "bf16", "int8w", 3, 0, 16),
+    "cfg4": ("kev-0.8b", "bf16", "bf16", 4, 0, 4),
+    "cfg5": ("kev-4b", "bf16", "bf16", 5, 0, 24),
 }
 
 

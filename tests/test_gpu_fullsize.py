@@ -9,8 +9,8 @@ calibrated probabilities with the oracle's:
 
   * cfg1 Kev-0.8B fp32, 1 x 256: within 1e-4 (the reference's fp32 gate);
   * cfg2 Kev-0.8B bf16, all 96 benchmark rows; cfg3 int8 per-channel weights,
-    4 x 1024 tokens, choice-8; cfg4 2 x 8192 tokens on 16-token pages in a
-    shuffled block table; cfg5 Kev-4B bf16, 8 mixed rows: within 2e-3 (the
+    16 x 1024 tokens, choice-8; cfg4 4 x 8192 tokens on 16-token pages in a
+    shuffled block table; cfg5 Kev-4B bf16, 24 mixed rows: within 2e-3 (the
     reference's half-precision gate, tests/kev_reference.rs:64-76);
   * every configuration: the same argmax as the oracle on every row.
 
