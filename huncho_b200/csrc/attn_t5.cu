@@ -3,7 +3,8 @@
 // tensor memory, for head_dim 128 and 256, fp16 operands.
 //
 // One CTA = 128 queries of one (row, query head); 4 warps, thread = query row
-// = TMEM lane. Per tile of 64 keys:
+// = TMEM lane; CTAs are dispatched longest (last query tile) first. Per tile
+// of 64 keys:
 //   S = Q K^T   (M=128, N=64, K=HD) into one of two TMEM S buffers;
 //   the row softmax in registers (tcgen05.ld), P = exp2(...) as fp16 into
 //   shared memory;
@@ -101,7 +102,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 9);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
-    const int row = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * BM;
+    // Query tiles are the slowest grid dimension, last tile first: under the
+    // causal mask a tile's work grows with its position, so the longest CTAs
+    // start first and the short ones fill the tail.
+    const int row = blockIdx.y, h = blockIdx.x, q0 = (gridDim.z - 1 - blockIdx.z) * BM;
     const int start = a.cu_seqlens[row];
     const int len = a.cu_seqlens[row + 1] - start;
     if (q0 >= len) return;
@@ -487,7 +491,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 template <int HD>
 void launch_t5(const AttnArgs &a, cudaStream_t s) {
-    dim3 grid(ceil_div(a.max_len, BM), a.nh, a.n_rows);
+    dim3 grid(a.nh, a.n_rows, ceil_div(a.max_len, BM));
     const auto aligned = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     // TMA staging for rows without cached prefixes (their keys live in the
     // k / v buffers only) when the slot count is known.
