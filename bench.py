@@ -150,7 +150,7 @@ def request_plan(wl):
 KERNEL_NAMES = {
     "gemm": "gemm_f16_tc_kernel + gemm_f16_tc2_kernel (tcgen05 projections)",
     "delta": "delta_pipe_kernel (fused delta layer: conv, gates, chunked rule, gated norm)",
-    "attention": "attn_t5_kernel (tcgen05 causal GQA attention)",
+    "attention": "attn_ws_kernel (warp-specialised tcgen05 causal GQA attention; attn_t5_kernel for prefix rows)",
     "delta_prep": "delta_prep_vec_kernel (fp32 model's delta input stage)",
     "other": "swiglu / gated_norm / conv_history kernels",
     "rmsnorm": "rmsnorm_reg_kernel",
