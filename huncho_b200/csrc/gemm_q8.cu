@@ -26,9 +26,10 @@
 //   warp 1       allocates all 512 TMEM columns (four 128 x 128 int32 block
 //                accumulators) and issues one MMA per block from one thread;
 //   warps 2..17  epilogue: warp w drains the 32 TMEM lanes (rows) of quarter
-//                w % 4 and 32 of the tile's columns, releases the accumulator
-//                right after tcgen05.ld, then scales the block's 32 dots and
-//                adds them to its running fp32 sums.
+//                w % 4 and 32 of the tile's columns in two 16-column loads
+//                (the second in flight while the first half is scaled),
+//                releases the accumulator once both have landed, and adds the
+//                scaled block dots to its running fp32 sums.
 // Each block dot v leaves TMEM as int32; adding the bits of C = 1.5 * 2^23
 // makes the fp32 value C + v (exact), and one paired fma per two outputs,
 // fma(C + v, d_w, -C d_w), gives v * d_w with a single rounding (the exact
