@@ -223,8 +223,9 @@ def test_full_size_batch_invariance(native_lib):
 @pytest.mark.parametrize("name,dtype,store", [("tiny", "fp32", None), ("tiny", "bf16", None),
                                               ("kev-mini", "bf16", "bf16"), ("kev-0.8b-l4", "bf16", "bf16")])
 def test_paged_kv_equals_flat(native_lib, synth_root, name, dtype, store):
-    """16-token KV pages in a shuffled block table give the flat result bit for
-    bit (the reference's pages-vs-flat parity, tests/kv_pages.rs:36-103)."""
+    """16-, 64- and 128-token KV pages in a shuffled block table give the flat
+    result bit for bit (the reference's pages-vs-flat parity,
+    tests/kv_pages.rs:36-103)."""
     d = GOLDEN if name == "tiny" else _synth(synth_root, name, store)
     b = _backend(d, dtype, max_context=4096)
     vocab = b.vocab_size
@@ -235,6 +236,8 @@ def test_paged_kv_equals_flat(native_lib, synth_root, name, dtype, store):
     paged = b.score_packed(*args)
     assert np.array_equal(flat, paged)
     b.with_kv_page_tokens(64, shuffle_seed=0)
+    assert np.array_equal(flat, b.score_packed(*args))
+    b.with_kv_page_tokens(128, shuffle_seed=1)  # pages wider than a 64-key tile
     assert np.array_equal(flat, b.score_packed(*args))
     b.with_kv_page_tokens(0)
     assert np.array_equal(flat, b.score_packed(*args))
