@@ -94,6 +94,17 @@ def test_latency_summary_and_kernel_rooflines():
     assert abs(rl["gemm"]["frac_tensor"] - 1.0) < 1e-9 and rl["gemm"]["bound"] == "tensor"
     assert abs(rl["rmsnorm"]["frac_hbm"] - 1.0) < 1e-9 and rl["rmsnorm"]["bound"] == "hbm"
     assert abs(rl["gemm"]["avg_ms"] - 0.1) < 1e-12
+    # The kernels each class names follow the model dtype: the packed profiles'
+    # projections are the tcgen05 kind::i8 GEMM, and their (fp32-activation)
+    # attention and recurrence are the CUDA-core kernels.
+    name, bound = bench.kernel_label("gemm", "q8_0-fp32")
+    assert "gemm_q8_tc_kernel" in name and bound == "tensor"
+    name, bound = bench.kernel_label("attention", "q4_0-fp32")
+    assert "attn_simt_kernel" in name and bound != "tensor"
+    assert "3xTF32" in bench.kernel_label("gemm", "fp32")[0]
+    assert "attn_ws_kernel" in bench.kernel_label("attention", "bf16")[0]
+    rl = {e["class"]: e for e in bench.kernel_rooflines(prof, pk, "q8_0-fp32")}
+    assert "gemm_q8_tc_kernel" in rl["gemm"]["kernel"]
 
 
 def test_cpu_legs_use_every_core_under_torchrun_threads():
