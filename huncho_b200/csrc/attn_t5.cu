@@ -2,9 +2,14 @@
 // on the 5th-generation tensor cores: tcgen05.mma with the accumulators in
 // tensor memory, for head_dim 128 and 256, fp16 operands.
 //
-// One CTA = 128 queries of one (row, query head); 4 warps, thread = query row
-// = TMEM lane; CTAs are dispatched longest (last query tile) first. Per tile
-// of 64 keys:
+// Two kernels share the algebra below. attn_ws_kernel (rows without a cached
+// prefix: the model's path) is warp-specialised, with TMA loads through the
+// page table; it is described where it is defined. attn_t5_kernel (rows that
+// continue a cached prefix) runs it in one group of 4 warps.
+//
+// One CTA = 128 queries of one (row, query head); in attn_t5_kernel, thread =
+// query row = TMEM lane; CTAs are dispatched longest (last query tile) first.
+// Per tile of 64 keys:
 //   S = Q K^T   (M=128, N=64, K=HD) into one of two TMEM S buffers;
 //   the row softmax in registers (tcgen05.ld), P = exp2(...) as fp16 into
 //   shared memory;
@@ -17,7 +22,8 @@
 //
 // Q, K, V and P live in shared memory as 128B-swizzled K-major tiles (V's
 // tile is the same bytes read MN-major); K and V tiles are double-buffered and
-// stream in with cp.async while earlier tiles are used. Keys are read through
+// stream in (cp.async here, TMA in attn_ws_kernel) while earlier tiles are
+// used. Keys are read through
 // kv_slot() (flat or paged) and, for a row that continues a cached prefix,
 // from the prefix's K/V first. Every mbarrier wait is bounded: on a timeout
 // the kernel records an error bit, lets the MMAs it issued finish, frees its
